@@ -1,0 +1,383 @@
+"""Benchmark of siliconfer's Q4Linear path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload 7b|70b|0.5b] [--batch T]
+
+Workload (default, N=1): BASELINE config 3 -- a 7B-shaped decode step, 32
+layers x 7 projections (hidden 4096, intermediate 11008), symmetric int4,
+group 128, seeded N(0, 0.02) weights quantized on the device with the
+reference's RTN (bit-exact with pack_weights_sym), fp16 activations N(0,1),
+fp32 outputs.  One step = all 224 GEMVs, replayed as one CUDA graph.  The
+weights (3.44 GB) are far larger than L2 (126 MB), so every step streams them
+from HBM; no flush is needed.
+
+metric/value: algorithmic bytes per step / device time per step, in GB/s
+(the reference's formula, scripts/benchmark.py:97-102, extended with the
+output).  decode_step_us is the same step as latency.
+
+With N > 1 (torchrun) every rank runs the same workload on its own GPU
+(replicas, weak scaling) unless --workload 70b selects the tensor-parallel
+70B step (column/row-parallel shards with an all-reduce after o/down).
+
+--impl reference times the reference's own CPU kernels (oracle/_ref, built
+from the reference sources; else the oracle's C port) on the host cores with
+every thread, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+HIDDEN = {"7b": (4096, 11008, 32), "70b": (8192, 28672, 80), "0.5b": (896, 4864, 24)}
+KV_OUT = {"7b": 4096, "70b": 1024, "0.5b": 128}
+PROJ = ("q", "k", "v", "o", "gate", "up", "down")
+
+
+def shapes(workload: str):
+    """(name, N, K) of one layer's projections."""
+    h, f, _ = HIDDEN[workload]
+    kv = KV_OUT[workload]
+    return [("q", h, h), ("k", kv, h), ("v", kv, h), ("o", h, h),
+            ("gate", f, h), ("up", f, h), ("down", h, f)]
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        mhz, maxm, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                maxm = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": maxm,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+def build_layers(workload, device, tp_rank=0, tp_size=1, seed=1234):
+    """Random-init projections of the named architecture, quantized on the GPU."""
+    import torch
+    from siliconfer_b200.q4_linear import Q4Linear
+    from siliconfer_b200.quant import pack_weights_device
+    _, _, n_layers = HIDDEN[workload]
+    layers = []
+    gen = torch.Generator(device=device)
+    for li in range(n_layers):
+        for pi, (name, n, k) in enumerate(shapes(workload)):
+            gen.manual_seed(seed + 1000 * li + pi)
+            row_parallel = name in ("o", "down")
+            if tp_size > 1:
+                if row_parallel:
+                    k = k // tp_size
+                else:
+                    n = n // tp_size
+            W = torch.randn((n, k), generator=gen, device=device) * 0.02
+            p, s = pack_weights_device(W, 128)
+            del W
+            layers.append(Q4Linear(p, s, group_size=128, device=device))
+    torch.cuda.synchronize(device)
+    return layers
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    from siliconfer_b200 import _lib
+    from siliconfer_b200.runner import Q4StepRunner
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=device)
+
+    t_build = time.perf_counter()
+    layers = build_layers(args.workload, device)
+    runner = Q4StepRunner(layers, tokens=args.batch, x_dtype=torch.float16,
+                          y_dtype=torch.float32, pdl=True, device=device)
+    g = torch.Generator(device=device)
+    g.manual_seed(7)
+    runner.x.copy_(torch.randn(runner.x.shape, generator=g, device=device).to(runner.x.dtype))
+    runner.x_host.copy_(runner.x.cpu())
+    runner.capture()
+    build_s = time.perf_counter() - t_build
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    # ---- device-resident timing -------------------------------------------
+    for _ in range(args.warmup):
+        runner.run()
+    runner.stream.synchronize()
+    barrier()
+    torch.cuda.synchronize(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = _lib.launch_count()
+    with ClockSampler(local_rank) as clocks:
+        start.record(runner.stream)
+        for _ in range(args.steps):
+            runner.run()
+        stop.record(runner.stream)
+        stop.synchronize()
+    barrier()
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(stop) / args.steps
+    host_launches = _lib.launch_count() - launches0   # 0: graph replays launch on the device
+
+    # ---- end to end: pinned host in, pinned host out -------------------------
+    for _ in range(max(1, args.warmup)):
+        runner.run_host()
+    runner.stream.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(runner.stream)
+    for _ in range(args.steps):
+        runner.run_host()
+    e1.record(runner.stream)
+    e1.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    if dist is not None:
+        t = torch.tensor([ms, e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+
+    step_bytes = runner.algorithmic_bytes()
+    total_bytes = step_bytes * world
+    value = total_bytes / (ms * 1e-3) / 1e9
+    e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peak()
+    per_gpu = step_bytes / (ms * 1e-3) / 1e9
+    xin = runner.x.numel() * runner.x.element_size()
+    yout = runner.y.numel() * runner.y.element_size()
+
+    result = {
+        "metric": f"int4 GEMV HBM GB/s, {args.workload} decode step (batch {args.batch})",
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 5),
+        "decode_step_us": round(ms * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int4 weights (u8 nibbles) x fp16 activations, fp32 accumulate",
+        "data": "synthetic: seeded N(0,0.02) weights, RTN int4 sym g128 (device pack, bit-exact "
+                "with the reference packer); fp16 N(0,1) activations",
+        "config": {"workload": f"BASELINE config 3: {args.workload}-shaped decode step, "
+                               f"{HIDDEN[args.workload][2]} layers x 7 projections",
+                   "batch": args.batch, "group_size": 128, "layout": "sym",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "weights 3.44 GB per step >> 126 MB L2 (no flush needed)"
+                   if args.workload == "7b" else "weights >> L2 (no flush needed)"},
+        "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(per_gpu / peak, 4),
+                     "peak_kind": peak_kind,
+                     "kernel": "q4_gemv_kernel<1,false> (all launches of the step)",
+                     "bytes_per_launch_avg": step_bytes // runner.kernels_per_step,
+                     "launch_us_avg": round(ms * 1e3 / runner.kernels_per_step, 3),
+                     "traffic": traffic_from_profile(args.workload, args.batch)},
+        "e2e": {"value": round(e2e_value, 1), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 5),
+                "h2d_bytes_per_step": xin, "d2h_bytes_per_step": yout,
+                "api": "siliconfer_b200.runner.Q4StepRunner.run_host (pinned host in/out)"},
+        "gpu_launches": runner.kernels_per_step * args.steps,
+        "host_launch_calls_in_timed_region": host_launches,
+        "clocks": clocks.summary(),
+        "build_s": round(build_s, 1),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(args, layers)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def traffic_from_profile(workload, batch):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return d.get(f"{workload}_b{batch}")
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (reference's compiled kernels, else the oracle's C port)
+# ---------------------------------------------------------------------------
+def _cpu_impl():
+    from oracle import cref
+    if cref.ref_available():
+        return cref.ref_gemm, "reference", "siliconfer q4_gemv_sym_neon (scalar C on x86) " \
+                                           "compiled from the reference sources, rows split over threads"
+    return cref.oracle_gemm, "port", "oracle C restatement, rows split over threads"
+
+
+def _host_triples(workload, layers, n_layers_sample, batch):
+    if layers is not None:
+        trip = [(m.packed_d.cpu().numpy(), m.scales_d.cpu().numpy())
+                for m in layers[:7 * n_layers_sample]]
+    else:
+        from siliconfer_b200.quant import pack_weights_sym
+        rng = np.random.default_rng(1234)
+        trip = []
+        for _ in range(n_layers_sample):
+            for _, n, k in shapes(workload):
+                trip.append(pack_weights_sym(rng.normal(0, 0.02, (n, k)).astype(np.float32), 128))
+    xs = [np.random.default_rng(i).normal(0, 1, (batch, p.shape[1] * 2)).astype(np.float16)
+          .astype(np.float32) for i, (p, _) in enumerate(trip)]
+    return trip, xs
+
+
+def _time_cpu(trip, xs, batch, budget_s):
+    fn, kind, desc = _cpu_impl()
+    threads = os.cpu_count() or 1
+    nbytes = sum(p.nbytes + s.nbytes + batch * (p.shape[1] * 2 * 4 + p.shape[0] * 4)
+                 for p, s in trip)
+    # one untimed pass, then as many passes as fit the budget
+    t0 = time.perf_counter()
+    for (p, s), x in zip(trip, xs):
+        fn(p, s, None, x, 128, threads=threads)
+    one = time.perf_counter() - t0
+    reps = max(1, int(budget_s / max(one, 1e-3)))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        for (p, s), x in zip(trip, xs):
+            fn(p, s, None, x, 128, threads=threads)
+    dt = (time.perf_counter() - t0) / reps
+    return nbytes / dt / 1e9, dt, kind, desc, threads
+
+
+def cpu_baseline(args, layers):
+    n_sample = 2 if args.workload != "0.5b" else HIDDEN["0.5b"][2]
+    trip, xs = _host_triples(args.workload, layers, n_sample, args.batch)
+    gbs, dt, kind, desc, threads = _time_cpu(trip, xs, args.batch, budget_s=10.0)
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": f"{n_sample} of {HIDDEN[args.workload][2]} layers (7 projections each), "
+                      f"batch {args.batch}: {dt * 1e3:.1f} ms per sample; {desc}"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    n_sample = 2 if args.workload != "0.5b" else HIDDEN["0.5b"][2]
+    trip, xs = _host_triples(args.workload, None, n_sample, args.batch)
+    vals = []
+    for _ in range(args.warmup):
+        _time_cpu(trip, xs, args.batch, budget_s=0.0)
+    for _ in range(args.steps):
+        gbs, dt, kind, desc, threads = _time_cpu(trip, xs, args.batch, budget_s=0.0)
+        vals.append((gbs, dt))
+    gbs = statistics.median(v[0] for v in vals)
+    dt = statistics.median(v[1] for v in vals)
+    full_layers = HIDDEN[args.workload][2]
+    print(json.dumps({
+        "impl": "reference",
+        "metric": f"int4 GEMV HBM GB/s, {args.workload} decode step (batch {args.batch})",
+        "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt * 1e3 * full_layers / n_sample, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int4 weights x fp32 activations (fp16-representable), fp32 accumulate",
+        "data": "synthetic: seeded N(0,0.02) weights, RTN int4 sym g128",
+        "config": {"workload": f"BASELINE config 3: {args.workload}-shaped decode step",
+                   "batch": args.batch, "group_size": 128, "layout": "sym"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": f"{n_sample} of {full_layers} layers per step "
+                                   f"(ms_per_step extrapolated to all layers); {desc}"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="7b", choices=sorted(HIDDEN))
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

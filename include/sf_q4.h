@@ -1,0 +1,112 @@
+/*
+ * sf_q4.h -- C ABI of the B200 (sm_100a) Q4Linear kernels.
+ *
+ * This is the drop-in boundary for siliconfer's int4 weight-only linear path.
+ * Every pointer is a DEVICE pointer (cudaMalloc / torch CUDA storage) unless a
+ * comment says otherwise, and every call is asynchronous on `stream`
+ * (a cudaStream_t passed as void*; NULL = legacy default stream).  The caller
+ * owns every buffer, as in the reference's C kernels
+ * (siliconfer/kernels/neon/q4_gemv.h:17-62).  Shape errors are reported as a
+ * status code instead of the reference binding's std::runtime_error
+ * (siliconfer/kernels/neon/bindings.cpp:24-40, 98-140); sf_last_error() gives
+ * the same message text.
+ *
+ * Storage format (unchanged from the reference, q4_gemv.h:5-12 and
+ * siliconfer/kernels/neon/__init__.py:42-81):
+ *   W       uint8 [N, K/2]  byte j of row i = w(i,2j) | w(i,2j+1) << 4
+ *                           sym: two's-complement nibbles (-8..7)
+ *                           asym: unsigned nibbles (0..15)
+ *   scales  float [N, K/group_size]
+ *   zeros   float [N, K/group_size] or NULL (NULL selects the symmetric layout)
+ *   x / X   [T, K] row-major, dtype SF_F32 / SF_F16 / SF_BF16
+ *   y / Y   [T, N] row-major, dtype SF_F32 / SF_F16 / SF_BF16
+ */
+#ifndef SF_Q4_H_
+#define SF_Q4_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  SF_OK = 0,
+  SF_ERR_NULL = 1,        /* a required pointer is NULL                       */
+  SF_ERR_SHAPE = 2,       /* N/K/T/group_size inconsistent                     */
+  SF_ERR_DTYPE = 3,       /* unknown dtype code                                */
+  SF_ERR_ALIGN = 4,       /* pointer alignment the kernel needs is not met     */
+  SF_ERR_CUDA = 5,        /* a CUDA runtime call failed                        */
+  SF_ERR_UNSUPPORTED = 6, /* valid request this build does not implement       */
+  SF_ERR_TIMEOUT = 7,     /* a device-side bounded wait expired                */
+  SF_ERR_COMM = 8         /* tensor-parallel peer exchange failed              */
+} sf_status;
+
+typedef enum { SF_F32 = 0, SF_F16 = 1, SF_BF16 = 2 } sf_dtype;
+
+/* Human-readable text of a status code, and the detailed message of the last
+   failing call on this host thread (mirrors bindings.cpp:27-39 wording). */
+const char* sf_status_string(int status);
+const char* sf_last_error(void);
+int sf_version(void);
+
+/* ---- reference-named entry points (fp32 activations in and out) ----------
+ * Each replaces the reference C function of the same role:
+ *   sf_q4_gemv_sym   <- q4_gemv_sym_neon   (q4_gemv.h:17-24;  bindings.cpp:45-55)
+ *   sf_q4_gemv_scalar<- q4_gemv_sym_scalar (q4_gemv.h:27-33;  bindings.cpp:60-70)
+ *   sf_q4_gemv_asym  <- q4_gemv_asym_neon  (q4_gemv.h:36-43;  bindings.cpp:75-92)
+ *   sf_q4_gemm_sym   <- q4_gemm_sym_neon   (q4_gemv.h:46-53;  bindings.cpp:97-119)
+ *   sf_q4_gemm_asym  <- q4_gemm_asym_neon  (q4_gemv.h:56-62;  bindings.cpp:124-150)
+ * Argument order and meaning follow the reference; `stream` is appended.    */
+int sf_q4_gemv_sym(const uint8_t* W, const float* scales, const float* x, float* y,
+                   int out_f, int in_f, int group_size, void* stream);
+int sf_q4_gemv_scalar(const uint8_t* W, const float* scales, const float* x, float* y,
+                      int out_f, int in_f, int group_size, void* stream);
+int sf_q4_gemv_asym(const uint8_t* W, const float* scales, const float* zeros,
+                    const float* x, float* y, int out_f, int in_f, int group_size,
+                    void* stream);
+int sf_q4_gemm_sym(const uint8_t* W, const float* scales, const float* X, float* Y,
+                   int out_f, int in_f, int T, int group_size, void* stream);
+int sf_q4_gemm_asym(const uint8_t* W, const float* scales, const float* zeros,
+                    const float* X, float* Y, int out_f, int in_f, int T,
+                    int group_size, void* stream);
+
+/* ---- general entry point used by Q4Linear ----------------------------------
+ * Y[T,N] = X[T,K] @ dequant(W)^T (+ bias), fp32 accumulation.
+ * Replaces Q4Linear.__call__'s kernel dispatch (siliconfer/model/q4_linear.py:
+ * 57-66): zeros != NULL selects the asymmetric kernel, bias (fp32 [N], may be
+ * NULL) is added after the product.  T <= 8 runs the decode GEMV kernel;
+ * larger T runs the prefill GEMM.  flags: bit 0 = allow programmatic
+ * dependent launch (the kernel may start streaming weights before the
+ * previous kernel on `stream` has finished; x is read only after it has). */
+int sf_q4_linear(const uint8_t* W, const float* scales, const float* zeros,
+                 const float* bias, const void* X, int x_dtype, void* Y, int y_dtype,
+                 int N, int K, int T, int group_size, int flags, void* stream);
+#define SF_FLAG_PDL 1
+
+/* Device dequant to fp32/fp16/bf16 [N, K].  fp32 output is bit-exact with
+   dequantize_sym / dequantize_asym (siliconfer/quant/primitives.py:54-75,
+   117-140); fp16/bf16 are that value rounded to nearest even. */
+int sf_q4_dequant(const uint8_t* W, const float* scales, const float* zeros, void* out,
+                  int out_dtype, int N, int K, int group_size, void* stream);
+
+/* Device RTN quantize + pack of an fp32 [N, K] weight, bit-exact with
+   pack_weights_sym / pack_weights_asym (siliconfer/kernels/neon/__init__.py:
+   42-81 -> siliconfer/quant/primitives.py:24-51, 82-114).  zeros == NULL
+   selects symmetric packing. */
+int sf_q4_quantize_pack(const float* W, uint8_t* packed, float* scales, float* zeros,
+                        int N, int K, int group_size, void* stream);
+
+/* Sticky device-side error word (set when a bounded wait inside a kernel
+   expires).  Synchronous: reads and clears it.  Returns SF_OK or
+   SF_ERR_TIMEOUT. */
+int sf_q4_check_device_error(void);
+
+/* Number of kernels this library has launched since load (host counter). */
+long long sf_q4_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SF_Q4_H_ */

@@ -1,0 +1,188 @@
+"""CPU oracle for siliconfer's Q4Linear int4 path -- TEST INFRASTRUCTURE ONLY.
+
+This module is a plain numpy restatement of the reference's algorithm for the
+hot path.  It exists to *check* the CUDA implementation; nothing in the product
+(``siliconfer_b200``) imports it.  Only ``tests/``, ``__graft_entry__.smoke()``
+and the ``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may use it.
+
+Parity pin: every function here is checked against golden vectors produced by
+the reference's own Python code (``tests/golden/make_golden.py`` imports
+``siliconfer.kernels.neon`` and ``siliconfer.quant`` from the reference tree
+and stores their outputs in ``tests/golden/*.npz``), see
+``tests/test_oracle_golden.py``.
+
+Reference citations are ``path:line`` inside the siliconfer project.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+INT4_SYM_MIN, INT4_SYM_MAX, INT4_UINT_MAX = -8, 7, 15
+
+
+# ---------------------------------------------------------------------------
+# Format producers (siliconfer/quant/primitives.py, kernels/neon/__init__.py)
+# ---------------------------------------------------------------------------
+
+def quantize_sym(w: np.ndarray, group_size: int = 128):
+    """Group-wise symmetric RTN int4 (siliconfer/quant/primitives.py:24-51).
+
+    scale = absmax / 7 in fp32; a zero scale divides by 1; q = round-half-even
+    (w / scale) clipped to [-8, 7].
+    """
+    rows, cols = w.shape
+    if cols % group_size:
+        raise ValueError(f"cols={cols} not divisible by group_size={group_size}")
+    g = w.reshape(rows, cols // group_size, group_size)
+    absmax = np.max(np.abs(g), axis=-1, keepdims=True)
+    scale = (absmax / np.float32(7)).astype(np.float32)
+    safe = np.where(scale == 0, np.float32(1), scale)
+    q = np.clip(np.round(g / safe), -8, 7).astype(np.int8)
+    return q.reshape(rows, cols), scale[..., 0]
+
+
+def quantize_asym(w: np.ndarray, group_size: int = 128):
+    """Group-wise asymmetric RTN int4 (siliconfer/quant/primitives.py:82-114).
+
+    scale = (max - min) / 15; zero = clip(round(-min / scale), 0, 15) kept as an
+    integer-valued float32; q = clip(round(w / scale) + zero, 0, 15).
+    """
+    rows, cols = w.shape
+    if cols % group_size:
+        raise ValueError(f"cols={cols} not divisible by group_size={group_size}")
+    g = w.reshape(rows, cols // group_size, group_size)
+    lo = g.min(axis=-1, keepdims=True)
+    hi = g.max(axis=-1, keepdims=True)
+    scale = ((hi - lo) / np.float32(15)).astype(np.float32)
+    safe = np.where(scale == 0, np.float32(1), scale)
+    zero = np.clip(np.round(-lo / safe), 0, 15).astype(np.float32)
+    q = np.clip(np.round(g / safe) + zero, 0, 15).astype(np.uint8)
+    return q.reshape(rows, cols), scale[..., 0], zero[..., 0]
+
+
+def pack_nibbles(q: np.ndarray) -> np.ndarray:
+    """Even column -> low nibble, odd column -> high nibble
+    (siliconfer/kernels/neon/__init__.py:57-62, 76-80)."""
+    lo = q[:, 0::2].astype(np.uint8) & 0x0F
+    hi = q[:, 1::2].astype(np.uint8) & 0x0F
+    return (lo | (hi << 4)).astype(np.uint8)
+
+
+def pack_weights_sym(w: np.ndarray, group_size: int = 128):
+    """siliconfer/kernels/neon/__init__.py:42-63."""
+    q, s = quantize_sym(np.asarray(w, np.float32), group_size)
+    return pack_nibbles(q), s
+
+
+def pack_weights_asym(w: np.ndarray, group_size: int = 128):
+    """siliconfer/kernels/neon/__init__.py:66-81."""
+    q, s, z = quantize_asym(np.asarray(w, np.float32), group_size)
+    return pack_nibbles(q), s, z
+
+
+def unpack_nibbles(packed: np.ndarray, signed: bool) -> np.ndarray:
+    """Inverse of pack_nibbles; signed nibbles are two's complement
+    (siliconfer/quant/primitives.py:353-376, kernels/neon/q4_gemv.h:5-12)."""
+    n, kh = packed.shape
+    lo = (packed & 0x0F).astype(np.int16)
+    hi = (packed >> 4).astype(np.int16)
+    out = np.empty((n, 2 * kh), np.int16)
+    out[:, 0::2] = lo
+    out[:, 1::2] = hi
+    if signed:
+        out = np.where(out > 7, out - 16, out)
+    return out
+
+
+def dequantize(packed, scales, zeros=None, group_size: int = 128) -> np.ndarray:
+    """fp32 dequant: q*s (sym) or (q - z)*s (asym), one rounding each
+    (siliconfer/quant/primitives.py:54-75, 117-140).  This is the bit-exact
+    target for the device dequant."""
+    q = unpack_nibbles(packed, signed=zeros is None).astype(np.float32)
+    n, k = q.shape
+    qg = q.reshape(n, k // group_size, group_size)
+    if zeros is None:
+        w = qg * scales[..., None].astype(np.float32)
+    else:
+        w = (qg - zeros[..., None].astype(np.float32)) * scales[..., None].astype(np.float32)
+    return w.reshape(n, k).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# GEMV / GEMM (siliconfer/kernels/neon/__init__.py:88-124, 179-227)
+# ---------------------------------------------------------------------------
+
+def gemv_sym(packed, scales, x, group_size: int = 128) -> np.ndarray:
+    """Per group: y += (W_g @ x_g) * s[:, g] with sign-extended nibbles
+    (siliconfer/kernels/neon/__init__.py:88-106)."""
+    q = unpack_nibbles(packed, signed=True).astype(np.float32)
+    x = np.asarray(x, np.float32)
+    n, k = q.shape
+    y = np.zeros(n, np.float32)
+    for g in range(k // group_size):
+        sl = slice(g * group_size, (g + 1) * group_size)
+        y += (q[:, sl] @ x[sl]) * scales[:, g]
+    return y
+
+
+def gemv_asym(packed, scales, zeros, x, group_size: int = 128) -> np.ndarray:
+    """Per group: y += (W_g @ x_g - z[:, g] * sum(x_g)) * s[:, g] with unsigned
+    nibbles (siliconfer/kernels/neon/__init__.py:109-124)."""
+    q = unpack_nibbles(packed, signed=False).astype(np.float32)
+    x = np.asarray(x, np.float32)
+    n, k = q.shape
+    y = np.zeros(n, np.float32)
+    for g in range(k // group_size):
+        sl = slice(g * group_size, (g + 1) * group_size)
+        y += (q[:, sl] @ x[sl] - zeros[:, g] * x[sl].sum()) * scales[:, g]
+    return y
+
+
+def gemm(packed, scales, zeros, X, group_size: int = 128) -> np.ndarray:
+    """Y[T, N] for T tokens.  The reference loops the GEMV per token
+    (siliconfer/kernels/neon/__init__.py:191-197, 221-227); this restatement
+    evaluates all tokens per group at once with the same per-group algebra."""
+    X = np.atleast_2d(np.asarray(X, np.float32))
+    signed = zeros is None
+    q = unpack_nibbles(packed, signed=signed).astype(np.float32)
+    n, k = q.shape
+    Y = np.zeros((X.shape[0], n), np.float32)
+    for g in range(k // group_size):
+        sl = slice(g * group_size, (g + 1) * group_size)
+        part = X[:, sl] @ q[:, sl].T
+        if not signed:
+            part -= X[:, sl].sum(axis=1, keepdims=True) * zeros[:, g][None, :]
+        Y += part * scales[:, g][None, :]
+    return Y
+
+
+def q4linear_forward(packed, scales, zeros, bias, x, group_size: int = 128):
+    """Q4Linear.__call__ restated (siliconfer/model/q4_linear.py:49-68):
+    reshape [..., K] -> [T, K] fp32, gemm_{sym,asym}, reshape, + bias."""
+    x = np.asarray(x, np.float32)
+    k = packed.shape[1] * 2
+    y = gemm(packed, scales, zeros, x.reshape(-1, k), group_size)
+    y = y.reshape(*x.shape[:-1], packed.shape[0])
+    if bias is not None:
+        y = y + np.asarray(bias, np.float32)
+    return y
+
+
+def normwise_rel_err(y, y_ref) -> float:
+    """max|y - y_ref| / max|y_ref| -- the tolerance measure the parity tests use."""
+    y = np.asarray(y, np.float64)
+    y_ref = np.asarray(y_ref, np.float64)
+    den = np.max(np.abs(y_ref))
+    if den == 0:
+        return float(np.max(np.abs(y)))
+    return float(np.max(np.abs(y - y_ref)) / den)
+
+
+def algorithmic_bytes(n: int, k: int, t: int, group_size: int, asym: bool,
+                      x_bytes: int = 4, y_bytes: int = 4, zero_bytes: int = 4) -> int:
+    """Bytes one GEMV/GEMM must move (scripts/benchmark.py:97-102, extended with
+    zeros and the output)."""
+    g = k // group_size
+    return (n * k // 2 + n * g * 4 + (n * g * zero_bytes if asym else 0)
+            + t * k * x_bytes + t * n * y_bytes)

@@ -1,0 +1,73 @@
+"""ctypes binding of the C ABI in include/sf_q4.h (libsf_q4.so).
+
+There is no CPU fallback: if the library is missing or no CUDA device is
+present, every compute call raises.  Status codes map to RuntimeError with the
+library's message, as the reference's pybind layer raises std::runtime_error
+(siliconfer/kernels/neon/bindings.cpp:24-40).
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+
+_PKG = pathlib.Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libsf_q4.so"
+
+SF_F32, SF_F16, SF_BF16 = 0, 1, 2
+SF_FLAG_PDL = 1
+SF_OK = 0
+
+_P, _I, _LL = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
+
+# name -> argtypes (restype is int unless listed in _RESTYPES)
+SIGNATURES = {
+    "sf_status_string": [_I],
+    "sf_last_error": [],
+    "sf_version": [],
+    "sf_q4_gemv_sym": [_P, _P, _P, _P, _I, _I, _I, _P],
+    "sf_q4_gemv_scalar": [_P, _P, _P, _P, _I, _I, _I, _P],
+    "sf_q4_gemv_asym": [_P, _P, _P, _P, _P, _I, _I, _I, _P],
+    "sf_q4_gemm_sym": [_P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "sf_q4_gemm_asym": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "sf_q4_linear": [_P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _P],
+    "sf_q4_dequant": [_P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "sf_q4_quantize_pack": [_P, _P, _P, _P, _I, _I, _I, _P],
+    "sf_q4_check_device_error": [],
+    "sf_q4_launch_count": [],
+}
+_RESTYPES = {"sf_status_string": ctypes.c_char_p, "sf_last_error": ctypes.c_char_p,
+             "sf_q4_launch_count": _LL}
+
+_lib = None
+
+
+def load():
+    """Load libsf_q4.so (building it first if nvcc is available here)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    from . import build as _build
+    if _build.needs_build():
+        try:
+            _build.build()
+        except Exception as exc:  # no nvcc on this host and no prebuilt library
+            if not LIB_PATH.exists():
+                raise RuntimeError(f"{LIB_PATH} is missing and could not be built: {exc}") from exc
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, args in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = _RESTYPES.get(name, _I)
+    _lib = lib
+    return lib
+
+
+def check(rc: int) -> None:
+    if rc != SF_OK:
+        lib = load()
+        msg = lib.sf_last_error().decode() or lib.sf_status_string(rc).decode()
+        raise RuntimeError(msg)
+
+
+def launch_count() -> int:
+    return int(load().sf_q4_launch_count())

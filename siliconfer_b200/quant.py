@@ -1,0 +1,140 @@
+"""Format producers for the Q4Linear storage (host numpy + device CUDA).
+
+The packed triple (packed uint8 [N, K/2], fp32 scales [N, G], fp32 zeros
+[N, G] or None) is siliconfer's storage format, so the outputs of its
+RTN/GPTQ/AWQ/HQQ/SINQ pipelines load unchanged.  The host functions restate
+the reference's packers bit for bit:
+
+* ``quantize_sym``  -- siliconfer/quant/primitives.py:24-51
+* ``quantize_asym`` -- siliconfer/quant/primitives.py:82-114
+* ``pack_weights_sym`` / ``pack_weights_asym`` --
+  siliconfer/kernels/neon/__init__.py:42-81 (low nibble = even column)
+* ``hqq_quantize_weight`` -- siliconfer/quant/hqq.py:84-164, used here only to
+  produce asymmetric synthetic weights with the reference's grid choice.
+
+``pack_weights_*_device`` run the same RTN arithmetic on the GPU
+(``sf_q4_quantize_pack``), for weights too large to quantize on the host.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import _lib
+
+
+def _grouped(w: np.ndarray, group_size: int) -> np.ndarray:
+    rows, cols = w.shape
+    if cols % group_size != 0:
+        raise ValueError(f"cols={cols} not divisible by group_size={group_size}")
+    return w.reshape(rows, cols // group_size, group_size)
+
+
+def quantize_sym(w: np.ndarray, group_size: int = 128):
+    """int4 in [-8, 7] and fp32 scale = absmax / 7 per group."""
+    g = _grouped(np.asarray(w, np.float32), group_size)
+    scale = (np.abs(g).max(axis=-1, keepdims=True) / np.float32(7)).astype(np.float32)
+    div = np.where(scale == 0.0, np.float32(1.0), scale)
+    q = np.round(g / div).clip(-8, 7).astype(np.int8)
+    return q.reshape(w.shape), scale[..., 0]
+
+
+def quantize_asym(w: np.ndarray, group_size: int = 128):
+    """uint4 in [0, 15], fp32 scale = (max - min) / 15, integer-valued fp32 zero."""
+    g = _grouped(np.asarray(w, np.float32), group_size)
+    lo, hi = g.min(axis=-1, keepdims=True), g.max(axis=-1, keepdims=True)
+    scale = ((hi - lo) / np.float32(15)).astype(np.float32)
+    div = np.where(scale == 0.0, np.float32(1.0), scale)
+    zero = np.round(-lo / div).clip(0, 15).astype(np.float32)
+    q = (np.round(g / div) + zero).clip(0, 15).astype(np.uint8)
+    return q.reshape(w.shape), scale[..., 0], zero[..., 0]
+
+
+def _pack(q: np.ndarray) -> np.ndarray:
+    nib = q.astype(np.uint8) & np.uint8(0x0F)
+    return (nib[:, 0::2] | (nib[:, 1::2] << 4)).astype(np.uint8)
+
+
+def pack_weights_sym(W: np.ndarray, group_size: int = 128):
+    """-> (packed uint8 [out, in/2], scales fp32 [out, in/group_size])."""
+    q, s = quantize_sym(np.asarray(W, np.float32), group_size)
+    return _pack(q), s
+
+
+def pack_weights_asym(W: np.ndarray, group_size: int = 128):
+    """-> (packed uint8 [out, in/2], scales fp32, zeros fp32 [out, in/group_size])."""
+    q, s, z = quantize_asym(np.asarray(W, np.float32), group_size)
+    return _pack(q), s, z
+
+
+def pack_weights_device(W, group_size: int = 128, sym: bool = True):
+    """RTN quantize + pack an fp32 CUDA tensor [N, K] on its device.
+
+    Bit-exact with ``pack_weights_sym`` / ``pack_weights_asym``; returns torch
+    tensors (packed, scales[, zeros]) on the same device."""
+    import torch
+    if not (isinstance(W, torch.Tensor) and W.is_cuda):
+        raise TypeError("pack_weights_device needs a CUDA tensor")
+    W = W.contiguous().float()
+    n, k = W.shape
+    if k % group_size or group_size % 2:
+        raise ValueError(f"cols={k} not divisible by group_size={group_size}")
+    packed = torch.empty((n, k // 2), dtype=torch.uint8, device=W.device)
+    scales = torch.empty((n, k // group_size), dtype=torch.float32, device=W.device)
+    zeros = None if sym else torch.empty_like(scales)
+    lib = _lib.load()
+    with torch.cuda.device(W.device):
+        _lib.check(lib.sf_q4_quantize_pack(
+            W.data_ptr(), packed.data_ptr(), scales.data_ptr(),
+            None if zeros is None else zeros.data_ptr(), n, k, group_size,
+            torch.cuda.current_stream(W.device).cuda_stream))
+    return (packed, scales) if sym else (packed, scales, zeros)
+
+
+# ---------------------------------------------------------------------------
+# HQQ grid search (asymmetric, calibration-free), for synthetic asym weights.
+# ---------------------------------------------------------------------------
+_EPS = 1e-8
+DEFAULT_K_GRID = (150.0, 100.0, 80.0, None)
+
+
+def hqq_quantize_weight(W: np.ndarray, group_size: int = 128, p: float = 0.7,
+                        k_grid=DEFAULT_K_GRID, bits: int = 4) -> np.ndarray:
+    """Fake-quantized fp32 weights on the HQQ-chosen asymmetric grid.
+
+    For each group, candidate clip ranges [median - k*1.4826*MAD,
+    median + k*1.4826*MAD] (k = None: the full min-max range) are quantized in
+    float64 and the one with the lowest mean (|w - recon| + 1e-8)^p wins
+    (first best kept on ties).  Restates siliconfer/quant/hqq.py:84-164.
+    """
+    qmax = float(2 ** bits - 1)
+    n, k = W.shape
+    if k < group_size:
+        q, s, z = quantize_asym(np.asarray(W, np.float32), k)   # one group per row
+        return ((q.astype(np.float32) - z) * s).astype(np.float32)
+    g = W.reshape(n, k // group_size, group_size).astype(np.float64)
+    lo_full = g.min(axis=-1, keepdims=True)
+    hi_full = g.max(axis=-1, keepdims=True)
+    med = np.median(g, axis=-1, keepdims=True)
+    mad = np.median(np.abs(g - med), axis=-1, keepdims=True)
+    rstd = np.where(mad == 0.0, _EPS, mad) * 1.4826
+    best = None
+    for kk in k_grid:
+        if kk is None:
+            lo, hi = lo_full, hi_full
+        else:
+            lo = np.maximum(lo_full, med - kk * rstd)
+            hi = np.minimum(hi_full, med + kk * rstd)
+        scale = (hi - lo) / qmax
+        scale = np.where(scale <= 0, 1.0, scale)
+        zero = np.clip(np.round(-lo / scale), 0, qmax)
+        q = np.clip(np.round(g / scale + zero), 0, qmax)
+        loss = ((np.abs(g - scale * (q - zero)) + _EPS) ** p).mean(axis=-1, keepdims=True)
+        if best is None:
+            best = [loss, scale, zero]
+        else:
+            better = loss < best[0]
+            best = [np.where(better, loss, best[0]), np.where(better, scale, best[1]),
+                    np.where(better, zero, best[2])]
+    _, scale, zero = best
+    q = np.clip(np.round(g / scale + zero), 0, qmax)
+    return (scale * (q - zero)).reshape(n, k).astype(np.float32)

@@ -1,0 +1,69 @@
+"""The C-ABI library loads and exports every symbol include/sf_q4.h declares;
+host-side validation runs without a GPU (no kernel is launched)."""
+import ctypes
+import pathlib
+import re
+
+import pytest
+
+from siliconfer_b200 import _lib
+
+HEADER = pathlib.Path(__file__).resolve().parent.parent / "include"
+
+
+def declared_symbols():
+    names = set()
+    for h in HEADER.glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names |= set(re.findall(r"\b(sf_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    syms = declared_symbols()
+    assert "sf_q4_gemv_sym" in syms and "sf_q4_linear" in syms
+    for s in syms:
+        assert hasattr(lib, s), s
+
+
+def test_every_declared_symbol_has_a_ctypes_signature():
+    missing = [s for s in declared_symbols() if s not in _lib.SIGNATURES]
+    assert not missing, missing
+
+
+def test_status_strings():
+    lib = _lib.load()
+    assert lib.sf_status_string(0) == b"ok"
+    assert lib.sf_status_string(2) == b"shape mismatch"
+    assert lib.sf_version() >= 10000
+
+
+FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: validation fails first
+
+
+@pytest.mark.parametrize("args,msg", [
+    ((FAKE, FAKE, None, None, FAKE, 0, FAKE, 0, 8, 96, 1, 64, 0, None), "divisible"),
+    ((FAKE, FAKE, None, None, FAKE, 0, FAKE, 0, 8, 128, 1, 3, 0, None), "even"),
+    ((None, FAKE, None, None, FAKE, 0, FAKE, 0, 8, 128, 1, 64, 0, None), "null"),
+    ((FAKE, FAKE, None, None, FAKE, 7, FAKE, 0, 8, 128, 1, 64, 0, None), "dtype"),
+])
+def test_linear_validation_without_gpu(args, msg):
+    lib = _lib.load()
+    rc = lib.sf_q4_linear(*args)
+    assert rc != 0
+    assert msg in lib.sf_last_error().decode()
+
+
+def test_asym_entry_requires_zeros():
+    lib = _lib.load()
+    rc = lib.sf_q4_gemv_asym(FAKE, FAKE, None, FAKE, FAKE, 8, 128, 64, None)
+    assert rc == 1
+    with pytest.raises(RuntimeError, match="zeros"):
+        _lib.check(rc)
+
+
+def test_empty_problem_is_a_noop():
+    lib = _lib.load()
+    assert lib.sf_q4_linear(FAKE, FAKE, None, None, FAKE, 0, FAKE, 0, 0, 128, 1, 64, 0, None) == 0
+    assert lib.sf_q4_linear(FAKE, FAKE, None, None, FAKE, 0, FAKE, 0, 8, 128, 0, 64, 0, None) == 0

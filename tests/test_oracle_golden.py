@@ -1,0 +1,75 @@
+"""Pin the CPU oracle to the reference's own outputs (golden vectors)."""
+import numpy as np
+import pytest
+
+import cases as C
+from oracle import cref
+from oracle import q4_oracle as O
+
+
+@pytest.mark.parametrize("name", list(C.UNIT_CASES))
+def test_oracle_packers_match_reference(name, golden):
+    g, meta = golden
+    w, x, gs = C.unit_case(name)
+    if C.is_asym(name):
+        p, s, z = O.pack_weights_asym(w, gs)
+        assert np.array_equal(z, g[f"{name}/zeros"])
+    else:
+        p, s = O.pack_weights_sym(w, gs)
+        z = None
+    assert C.sha(p) == meta["hashes"][f"{name}/packed"]
+    assert C.sha(s) == meta["hashes"][f"{name}/scales"]
+    if f"{name}/dequant" in g:
+        # bit-exact dequant target
+        assert np.array_equal(O.dequantize(p, s, z, gs), g[f"{name}/dequant"])
+        assert np.array_equal(cref.oracle_dequant(p, s, z, gs), g[f"{name}/dequant"])
+    y = O.gemm(p, s, z, x, gs)
+    np.testing.assert_allclose(y, g[f"{name}/y"], rtol=1e-5, atol=1e-5)
+    yc = cref.oracle_gemm(p, s, z, x, gs)
+    assert O.normwise_rel_err(yc, g[f"{name}/y"]) < 1e-6
+
+
+def test_oracle_zero_input_and_boundaries(golden):
+    g, _ = golden
+    w = np.random.default_rng(0).normal(0, 1, (32, 128)).astype(np.float32)
+    p, s = O.pack_weights_sym(w)
+    assert np.all(O.gemv_sym(p, s, np.zeros(128, np.float32)) == g["zero_input/y"])
+    qs = np.arange(-8, 8, dtype=np.int8)[None, :]
+    assert np.array_equal(O.pack_nibbles(qs)[0], g["boundary/packed_sym"])
+    assert np.array_equal(O.unpack_nibbles(O.pack_nibbles(qs), True)[0], g["boundary/unpacked_sym"])
+    qa = np.arange(16, dtype=np.uint8)[None, :]
+    assert np.array_equal(O.pack_nibbles(qa)[0], g["boundary/packed_asym"])
+
+
+@pytest.mark.parametrize("proj", list(C.QWEN05B))
+def test_oracle_config1_layer(proj, golden):
+    g, meta = golden
+    n, k = C.QWEN05B[proj]
+    w = C.weights(C.layer_seed(1, 0, proj), n, k)
+    x = C.acts(C.layer_seed(1, 0, proj) + 7, 1, k)
+    p, s = O.pack_weights_sym(w, 128)
+    assert C.sha(p) == meta["hashes"][f"c1/{proj}/packed"]
+    assert C.sha(s) == meta["hashes"][f"c1/{proj}/scales"]
+    assert O.normwise_rel_err(O.gemm(p, s, None, x), g[f"c1/{proj}/y"]) < 1e-6
+
+
+def test_oracle_matches_compiled_reference_sym():
+    """The reference's own scalar/NEON sym kernel, compiled from its sources."""
+    if not cref.ref_available():
+        pytest.skip("oracle/_ref not built (reference sources absent)")
+    rng = np.random.default_rng(11)
+    w = rng.normal(0, 0.02, (257, 1024)).astype(np.float32)
+    x = rng.normal(0, 1, (3, 1024)).astype(np.float32)
+    for gs in (64, 128):
+        p, s = O.pack_weights_sym(w, gs)
+        assert O.normwise_rel_err(cref.ref_gemm(p, s, None, x, gs), O.gemm(p, s, None, x, gs)) < 1e-5
+
+
+def test_compiled_reference_asym_is_flagged():
+    """On x86 the reference's asym C entry runs the sym kernel
+    (q4_gemv.cpp:249-255); the wrapper must refuse to use it."""
+    if not cref.ref_available() or cref.ref_available(asym=True):
+        pytest.skip("not applicable on this host")
+    with pytest.raises(RuntimeError):
+        cref.ref_gemm(np.zeros((1, 64), np.uint8), np.ones((1, 1), np.float32),
+                      np.zeros((1, 1), np.float32), np.zeros((1, 128), np.float32))
