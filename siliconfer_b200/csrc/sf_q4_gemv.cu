@@ -1,0 +1,620 @@
+// sf_q4_gemv.cu -- decode GEMV (T <= 8 tokens) on the sm_100a tensor cores with
+// exact integer arithmetic.
+//
+// Reference semantics (siliconfer/kernels/neon/q4_gemv.cpp:37-140, 145-238;
+// siliconfer/kernels/neon/__init__.py:88-124): per output row i and group g,
+//   sym : y += s[i,g] * sum_k sext(q[i,k]) * x[k]
+//   asym: y += s[i,g] * (sum_k q[i,k] * x[k] - z[i,g] * sum_k x[k])
+//
+// How it is computed here:
+//  * Weights: the nibbles are UNSIGNED int8 A operands.  Symmetric nibbles
+//    are flipped (u ^ 8 = q + 8) by the same LOP3 that masks them, so both
+//    layouts become  s * (sum u*x - zeff * sum x)  with zeff = 8 (sym) or z
+//    (asym).  Unpacking costs 3 integer instructions per 8 weights.
+//  * Activations: per (token, group) the values are put on a fixed-point grid
+//    x_fix = rint(x * 2^(22-E)), E the binary exponent of the group's max |x|
+//    (|x_fix| <= 2^22: every value keeps 22 bits relative to the group max),
+//    split into three signed int8 digits x_fix = d0 + 256*d1 + 65536*d2.
+//  * mma.sync m16n8k32 u8 x s8 -> s32 accumulates sum u*d EXACTLY; one fp32
+//    epilogue per (row, group, token) recombines the digits, subtracts
+//    zeff * sum(x_fix) and applies s * 2^(E-22).  The only roundings are the
+//    fixed-point rounding of x and the fp32 epilogue and reduction.
+//  * Data movement: the producer warp streams W HBM->SMEM with cp.async.bulk
+//    into an mbarrier-guarded ring.  When a stage holds whole rows the row
+//    block is one contiguous region, copied as >= 4 KB pieces spread over the
+//    32 producer lanes (the bulk-copy engine has a per-copy cost, so small
+//    copies from one thread cannot keep HBM busy); otherwise each row's slice
+//    is one copy into a padded, bank-conflict-free layout.  Each row block's
+//    scales and zeros are bulk-copied into a 2-slot ring.
+//  * Consumer warps own (K-slice, row-group) pairs; K-slices are whole groups
+//    and are reduced through shared memory once per row block.
+//  * Programmatic dependent launch: the next kernel may start streaming its
+//    own weights while this one finishes; activations are read only after
+//    griddepcontrol.wait.
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+#include <cstdint>
+#include <cstdlib>
+
+#include "sf_q4.h"
+#include "sf_q4_internal.h"
+
+namespace sf {
+
+SF_DEFINE_ERROR_READER(take_dev_error_gemv_tc)
+
+namespace {
+
+constexpr int kMT = 2;                 // m16 tiles per warp per row block
+constexpr int kImmaMaxThreads = 512;   // 15 consumer warps + 1 producer warp
+constexpr uint32_t kPiece = 4096;      // contiguous bulk-copy piece (bytes)
+
+__device__ __forceinline__ void ld_x8(const void* x, size_t idx, int dt, float* v) {
+  if (dt == SF_F32) {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + idx);
+    const float4 a = __ldg(p), b = __ldg(p + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + idx));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f;
+      if (dt == SF_F16) f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      else f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ void st_y(void* y, size_t idx, float v, int dt) {
+  if (dt == SF_F32) reinterpret_cast<float*>(y)[idx] = v;
+  else if (dt == SF_F16) reinterpret_cast<__half*>(y)[idx] = __float2half_rn(v);
+  else reinterpret_cast<__nv_bfloat16*>(y)[idx] = __float2bfloat16_rn(v);
+}
+
+// D += A(u8, 16x32) * B(s8, 32x8), s32 accumulate.
+__device__ __forceinline__ void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                     uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Low / high nibble of every byte as unsigned bytes; symmetric nibbles are
+// flipped to u ^ 8 (= q + 8) in the same instruction.
+template <bool ASYM>
+__device__ __forceinline__ uint32_t nib_lo(uint32_t w) {
+  return (w & 0x0F0F0F0Fu) ^ (ASYM ? 0u : 0x08080808u);
+}
+template <bool ASYM>
+__device__ __forceinline__ uint32_t nib_hi(uint32_t w) {
+  return ((w >> 4) & 0x0F0F0F0Fu) ^ (ASYM ? 0u : 0x08080808u);
+}
+
+// Low bytes of d[0..7] in B-operand order: word 0 = k offsets {0,2,4,6},
+// word 1 = {1,3,5,7} (the A operand's low / high nibbles of one byte run).
+__device__ __forceinline__ uint2 pack_digits(const int* d) {
+  uint2 r;
+  r.x = (uint32_t)(d[0] & 255) | ((uint32_t)(d[2] & 255) << 8) | ((uint32_t)(d[4] & 255) << 16) |
+        ((uint32_t)(d[6] & 255) << 24);
+  r.y = (uint32_t)(d[1] & 255) | ((uint32_t)(d[3] & 255) << 8) | ((uint32_t)(d[5] & 255) << 16) |
+        ((uint32_t)(d[7] & 255) << 24);
+  return r;
+}
+
+template <int LB>
+__device__ __forceinline__ void lds_words(const uint8_t* p, uint32_t* w) {
+  if constexpr (LB == 16) {
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else if constexpr (LB == 8) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    w[0] = v.x; w[1] = v.y;
+  } else {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  }
+}
+
+// B digits of one segment for one lane: 2*LB bytes.
+template <int LB>
+__device__ __forceinline__ void lds_digits(const uint8_t* p, uint32_t* b) {
+  if constexpr (LB == 16) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint4 v = *reinterpret_cast<const uint4*>(p + 16);
+    b[0] = u.x; b[1] = u.y; b[2] = u.z; b[3] = u.w; b[4] = v.x; b[5] = v.y; b[6] = v.z; b[7] = v.w;
+  } else if constexpr (LB == 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    b[0] = u.x; b[1] = u.y; b[2] = u.z; b[3] = u.w;
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    b[0] = u.x; b[1] = u.y;
+  }
+}
+
+}  // namespace
+
+// Optional timeline (build with -DSF_GEMV_TRACE): per CTA 16 slots of
+// %globaltimer (ns) written to the buffer given to sf_q4_gemv_set_trace.
+#ifdef SF_GEMV_TRACE
+__device__ unsigned long long* g_gtrace = nullptr;
+#define GT(slot)                                                                        \
+  do {                                                                                  \
+    if (g_gtrace)                                                                       \
+      g_gtrace[((size_t)p.trace_id * gridDim.x + blockIdx.x) * 16 + (slot)] = globaltimer_ns(); \
+  } while (0)
+#else
+#define GT(slot) do { } while (0)
+#endif
+
+// ---------------------------------------------------------------------------
+template <int T, bool ASYM, int LB>
+__global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const ImmaParams p) {
+  constexpr int NTG = (T + 3) / 4;    // token groups of 4 (one token per lane t)
+  constexpr int NT = 2 * NTG;         // n8 tiles: (d0,d1) and (d2,-) per token group
+  constexpr int WPL = LB / 4;         // 32-bit words per lane per row per segment
+  constexpr int SEGK = 8 * LB;        // k values per segment (4 lanes x 2*LB)
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* sfull = empty + kMaxStages;
+  uint64_t* sempty = sfull + 2;
+  float* red = reinterpret_cast<float*>(smem + p.red_base);
+  float* xgsc = reinterpret_cast<float*>(smem + p.xs_base);
+  float* xsum = xgsc + T * p.G;
+  uint8_t* xb = smem + p.xb_base;
+  uint8_t* sring = smem + p.sring_base;
+  uint8_t* stages = smem + p.stage_base;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int ncons = p.KS * p.RG;
+  const int rb = (int)((long long)p.N * blockIdx.x / gridDim.x);
+  const int re = (int)((long long)p.N * (blockIdx.x + 1) / gridDim.x);
+  const int nrb = (re - rb + p.R - 1) / p.R;                // row blocks
+  const int nkc = (p.K + p.KC - 1) / p.KC;                   // k-chunks per row block
+  const int KH = p.K >> 1;
+
+  if (threadIdx.x == 0) {
+    GT(0);
+    for (int i = 0; i < p.nst; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], ncons); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&sfull[i], 1); mbar_init(&sempty[i], ncons); }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  griddep_launch_dependents();
+
+  if (warp == ncons) {
+    // ------------------------------ producer ------------------------------
+    int c = 0;
+    for (int b = 0; b < nrb; ++b) {
+      const int r0 = rb + b * p.R;
+      const int rows = min(p.R, re - r0);
+      const int sl = b & 1;
+      int ok = 1;
+      if (lane == 0 && b >= 2) ok = mbar_wait(&sempty[sl], ((b >> 1) - 1) & 1);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+      if (lane == 0) {  // scales (+ zeros) of the row block, from the 16-byte boundary below
+        const uintptr_t src = reinterpret_cast<uintptr_t>(p.S + (size_t)r0 * p.G);
+        const uint32_t pre = (uint32_t)(src & 15);
+        const uint32_t nb = (pre + (uint32_t)rows * p.G * 4) & ~15u;
+        uint8_t* dst = sring + (size_t)sl * p.sring_bytes;
+        mbar_arrive_expect_tx(&sfull[sl], ASYM ? 2 * nb : nb);
+        if (nb) {
+          bulk_g2s(dst, reinterpret_cast<const void*>(src - pre), nb, &sfull[sl]);
+          if (ASYM)
+            bulk_g2s(dst + p.sring_bytes / 2,
+                     reinterpret_cast<const uint8_t*>(p.Z + (size_t)r0 * p.G) - pre, nb, &sfull[sl]);
+        }
+      }
+      for (int kc = 0; kc < nkc; ++kc, ++c) {
+        const int st = c % p.nst, use = c / p.nst;
+        ok = 1;
+        if (lane == 0 && use > 0) ok = mbar_wait(&empty[st], (use - 1) & 1);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+        const int k0 = kc * p.KC;
+        const uint32_t cb = (uint32_t)(min(p.KC, p.K - k0) >> 1);
+        uint8_t* buf = stages + (size_t)st * p.stage_bytes;
+        if (lane == 0) mbar_arrive_expect_tx(&full[st], cb * rows);
+        __syncwarp();
+        const uint8_t* src = p.W + (size_t)r0 * KH + (k0 >> 1);
+        if (p.contiguous) {
+          const uint32_t total = cb * rows;   // multiple of 16
+          const uint32_t npc = (total + kPiece - 1) / kPiece;
+          for (uint32_t j = lane; j < npc; j += 32) {
+            const uint32_t off = j * kPiece;
+            const uint32_t n = total - off < kPiece ? total - off : kPiece;
+            bulk_g2s(buf + off, src + off, n, &full[st]);
+          }
+        } else {
+          for (int r = lane; r < rows; r += 32)
+            bulk_g2s(buf + (size_t)r * p.RS, src + (size_t)r * KH, cb, &full[st]);
+        }
+      }
+    }
+    return;
+  }
+
+  // ------------------------------ consumers -------------------------------
+  const int nthr = ncons * 32;
+  griddep_wait();
+  if (threadIdx.x == 0) GT(1);
+
+  // (1) activations -> per-(token, group) fixed point, three int8 digits.
+  //     All of a thread's loads are issued before any of them is used.
+  {
+    const int octs_tok = p.K >> 3;
+    const int total = T * octs_tok;
+    const int lpg = p.gs >> 3;  // octets (lanes) per group: 4, 8, 16 or 32
+    constexpr int NB = 4;
+    for (int base = warp * 32; base < total; base += nthr * NB) {
+      float v[NB][8];
+#pragma unroll
+      for (int i = 0; i < NB; ++i) {
+        const int o = base + i * nthr + lane;
+        if (o < total) {
+          const int tok = o / octs_tok;
+          ld_x8(p.X, (size_t)tok * p.K + (size_t)(o - tok * octs_tok) * 8, p.xdt, v[i]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < NB; ++i) {
+        const int ob = base + i * nthr;
+        if (ob >= total) break;                       // uniform across the warp
+        const int o = ob + lane;
+        const bool ok = o < total;
+        float m = 0.f;
+        bool bad = false;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          m = fmaxf(m, fabsf(v[i][j]));
+          bad |= !(fabsf(v[i][j]) <= 3.402823466e38f);
+        }
+        int badi = bad;
+        for (int off = 1; off < lpg; off <<= 1) {
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+          badi |= __shfl_xor_sync(0xffffffffu, badi, off);
+        }
+        // binary exponent field of the group max; groups below 2^-105 are zero
+        const int be = (int)(__float_as_uint(m) >> 23);
+        const bool zero = badi || be < 22;
+        const float scl = zero ? 0.f : __uint_as_float((uint32_t)(275 - be) << 23);   // 2^(22-E)
+        int d[3][8];
+        int s = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int xf = __float2int_rn(v[i][j] * scl);
+          s += xf;
+          const int d0 = (xf << 24) >> 24;
+          const int r1 = (xf - d0) >> 8;
+          const int d1 = (r1 << 24) >> 24;
+          d[0][j] = d0;
+          d[1][j] = d1;
+          d[2][j] = (r1 - d1) >> 8;
+        }
+        for (int off = 1; off < lpg; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        if (ok) {
+          const int tok = o / octs_tok;
+          const int ko = (o - tok * octs_tok) * 8;
+          uint8_t* col = xb + (size_t)tok * p.TS + ko;
+#pragma unroll
+          for (int dg = 0; dg < 3; ++dg)
+            *reinterpret_cast<uint2*>(col + (size_t)dg * p.CSB) = pack_digits(d[dg]);
+          if ((lane & (lpg - 1)) == 0) {
+            const int gi = ko / p.gs;
+            xgsc[tok * p.G + gi] = badi ? __int_as_float(0x7fc00000)
+                                        : (zero ? 0.f : __uint_as_float((uint32_t)(be - 21) << 23));
+            xsum[tok * p.G + gi] = (float)s;
+          }
+        }
+      }
+    }
+  }
+  named_barrier_sync(1, nthr);
+  if (threadIdx.x == 0) GT(2);
+
+  // (2) stream the row blocks
+  const int ks = warp % p.KS, rgp = warp / p.KS;
+  const uint8_t* bcol[NT];   // B columns this lane supplies, per n8 tile
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int tok = (nt >> 1) * 4 + (g >> 1);
+    const int dg = (nt & 1) ? ((g & 1) ? -1 : 2) : (g & 1);
+    bcol[nt] = (tok < T && dg >= 0) ? xb + (size_t)tok * p.TS + (size_t)dg * p.CSB + t * 2 * LB
+                                    : nullptr;
+  }
+
+  int c = 0;
+  bool ok_wait = true;
+  for (int b = 0; b < nrb; ++b) {
+    const int r0 = rb + b * p.R;
+    const int rows = min(p.R, re - r0);
+    float acc[kMT][NTG][2];
+#pragma unroll
+    for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+      for (int tg = 0; tg < NTG; ++tg) acc[mt][tg][0] = acc[mt][tg][1] = 0.f;
+    const int sl = b & 1;
+    if (ok_wait) ok_wait = mbar_wait(&sfull[sl], (b >> 1) & 1);
+    const uintptr_t s_src = reinterpret_cast<uintptr_t>(p.S + (size_t)r0 * p.G);
+    const int s_pre = (int)(s_src & 15) >> 2;
+    const int s_cnt = (int)(((s_src & 15) + (uint32_t)rows * p.G * 4) & ~15u) >> 2;
+    const float* ssm = reinterpret_cast<const float*>(sring + (size_t)sl * p.sring_bytes);
+    const float* zsm = ssm + p.sring_bytes / 8;
+
+    for (int kc = 0; kc < nkc; ++kc, ++c) {
+      const int st = c % p.nst, use = c / p.nst;
+      const int k0 = kc * p.KC;
+      const int gc0 = k0 / p.gs;
+      const int gcn = min(p.KC, p.K - k0) / p.gs;
+      const int ga = gc0 + min(gcn, ks * p.GPS);
+      const int gb = gc0 + min(gcn, (ks + 1) * p.GPS);
+      if (ok_wait) ok_wait = mbar_wait(&full[st], use & 1);
+      if (threadIdx.x == 0 && c < 8) GT(3 + c);
+      const uint8_t* buf = stages + (size_t)st * p.stage_bytes;
+
+      for (int gi = ga; gi < gb && ok_wait; ++gi) {
+        float sc[kMT][2], zp[kMT][2];
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int lr = (rgp * kMT + mt) * 16 + g + 8 * h;
+            const int si = s_pre + lr * p.G + gi;
+            if (lr >= rows) {
+              sc[mt][h] = 0.f;
+              zp[mt][h] = 8.f;
+            } else if (si < s_cnt) {
+              sc[mt][h] = ssm[si];
+              zp[mt][h] = ASYM ? zsm[si] : 8.f;
+            } else {  // the last few values of the block were not bulk-copied
+              const size_t gix = (size_t)(r0 + lr) * p.G + gi;
+              sc[mt][h] = __ldg(p.S + gix);
+              zp[mt][h] = ASYM ? __ldg(p.Z + gix) : 8.f;
+            }
+          }
+        int C[kMT][NT][4];
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) C[mt][nt][0] = C[mt][nt][1] = C[mt][nt][2] = C[mt][nt][3] = 0;
+
+        for (int kseg = gi * p.gs; kseg < (gi + 1) * p.gs; kseg += SEGK) {
+          uint32_t bq[NT][2 * WPL];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            if (bcol[nt]) lds_digits<LB>(bcol[nt] + kseg, bq[nt]);
+            else {
+#pragma unroll
+              for (int i = 0; i < 2 * WPL; ++i) bq[nt][i] = 0u;
+            }
+          }
+          const int boff = ((kseg - k0) >> 1) + t * LB;
+#pragma unroll
+          for (int mt = 0; mt < kMT; ++mt) {
+            if ((rgp * kMT + mt) * 16 >= rows) continue;   // whole tile past the end
+            const int lr = (rgp * kMT + mt) * 16 + g;
+            uint32_t w0[WPL], w1[WPL];
+            lds_words<LB>(buf + (size_t)lr * p.RS + boff, w0);
+            lds_words<LB>(buf + (size_t)(lr + 8) * p.RS + boff, w1);
+#pragma unroll
+            for (int q = 0; q < WPL; ++q) {
+              const uint32_t a0 = nib_lo<ASYM>(w0[q]), a2 = nib_hi<ASYM>(w0[q]);
+              const uint32_t a1 = nib_lo<ASYM>(w1[q]), a3 = nib_hi<ASYM>(w1[q]);
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+                imma(C[mt][nt], a0, a1, a2, a3, bq[nt][2 * q], bq[nt][2 * q + 1]);
+            }
+          }
+        }
+        // epilogue of group gi: recombine digits, remove zeff * sum(x), scale
+#pragma unroll
+        for (int tg = 0; tg < NTG; ++tg) {
+          const int tok = tg * 4 + t;
+          if (tok < T) {
+            const float gsc = xgsc[tok * p.G + gi];
+            const float xs = xsum[tok * p.G + gi];
+#pragma unroll
+            for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int i01 = C[mt][2 * tg][2 * h] + 256 * C[mt][2 * tg][2 * h + 1];
+                float f = fmaf(65536.f, (float)C[mt][2 * tg + 1][2 * h], (float)i01);
+                f = fmaf(-zp[mt][h], xs, f);
+                acc[mt][tg][h] = fmaf(f, sc[mt][h] * gsc, acc[mt][tg][h]);
+              }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+
+    // (3) reduce the K-slices of this row block and write y
+    float* rbuf = red + (b & 1) * (p.KS * T * p.R);
+#pragma unroll
+    for (int tg = 0; tg < NTG; ++tg) {
+      const int tok = tg * 4 + t;
+      if (tok < T) {
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            rbuf[(ks * T + tok) * p.R + (rgp * kMT + mt) * 16 + g + 8 * h] = acc[mt][tg][h];
+      }
+    }
+    named_barrier_sync(1, nthr);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sempty[sl]);
+    for (int idx = threadIdx.x; idx < rows * T; idx += nthr) {
+      const int tok = idx / rows, r = idx - tok * rows;
+      float a = 0.f;
+      for (int k = 0; k < p.KS; ++k) a += rbuf[(k * T + tok) * p.R + r];
+      if (p.bias) a += __ldg(p.bias + r0 + r);
+      st_y(p.Y, (size_t)tok * p.N + r0 + r, a, p.ydt);
+    }
+    if (threadIdx.x == 0 && b < 2) GT(12 + b);
+  }
+  if (threadIdx.x == 0) GT(15);
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+namespace {
+
+int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return v && *v ? atoi(v) : dflt;
+}
+
+// smallest y >= x with y % mod == target
+size_t pad_to(size_t x, size_t mod, size_t target) {
+  const size_t r = x % mod;
+  return x + ((target + mod - r) % mod);
+}
+
+template <int T, bool ASYM, int LB>
+cudaError_t launch_t(const ImmaParams& p, int grid, int threads, size_t smem, cudaStream_t st,
+                     bool pdl) {
+  auto* fn = q4_gemv_imma_kernel<T, ASYM, LB>;
+  static int configured[kMaxDevices] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < kMaxDevices && configured[dev] < (int)smem) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = (int)smem;
+  }
+  return launch_kernel(fn, grid, threads, smem, st, pdl, p);
+}
+
+template <bool ASYM, int LB>
+cudaError_t launch_lb(int T, const ImmaParams& p, int grid, int threads, size_t smem,
+                      cudaStream_t st, bool pdl) {
+  switch (T) {
+    case 1: return launch_t<1, ASYM, LB>(p, grid, threads, smem, st, pdl);
+    case 2: return launch_t<2, ASYM, LB>(p, grid, threads, smem, st, pdl);
+    case 3: return launch_t<3, ASYM, LB>(p, grid, threads, smem, st, pdl);
+    case 4: return launch_t<4, ASYM, LB>(p, grid, threads, smem, st, pdl);
+    case 5: return launch_t<5, ASYM, LB>(p, grid, threads, smem, st, pdl);
+    case 6: return launch_t<6, ASYM, LB>(p, grid, threads, smem, st, pdl);
+    case 7: return launch_t<7, ASYM, LB>(p, grid, threads, smem, st, pdl);
+    default: return launch_t<8, ASYM, LB>(p, grid, threads, smem, st, pdl);
+  }
+}
+
+#ifdef SF_GEMV_TRACE
+int g_trace_counter = 0;
+#endif
+
+}  // namespace
+
+#ifdef SF_GEMV_TRACE
+extern "C" int sf_q4_gemv_set_trace(unsigned long long* buf) {
+  g_trace_counter = 0;
+  return cudaMemcpyToSymbol(g_gtrace, &buf, sizeof(buf)) == cudaSuccess ? 0 : 5;
+}
+#endif
+
+bool plan_gemv_imma(int N, int K, int T, int gs, bool asym, ImmaPlan& pl) {
+  if (T < 1 || T > kMaxGemvT || N < 1 || K % 32 || gs % 32 || gs > 256) return false;
+  const DeviceInfo& di = device_info();
+  const int LB = (gs % 128 == 0) ? 16 : (gs % 64 == 0 ? 8 : 4);
+  const int G = K / gs;
+  int grid = di.sms * env_int("SF_GEMV_CTAS_PER_SM", 1);
+  const int max_grid = (N + 15) / 16;                  // at least one 16-row tile per CTA
+  if (grid > max_grid) grid = max_grid;
+  const int rows_cta = (N + grid - 1) / grid;
+  const int max_cons = kImmaMaxThreads / 32 - 1;
+  int RG = (rows_cta + 16 * kMT - 1) / (16 * kMT);
+  if (RG > 2) RG = 2;
+  int KS = env_int("SF_GEMV_WARPS", 8) / RG;
+  if (KS < 1) KS = 1;
+  if (KS > G) KS = G;
+  if (KS * RG > max_cons) KS = max_cons / RG;
+  const int R = RG * kMT * 16;
+  // Stage: whole rows (one contiguous region) when a row block fits, else
+  // whole groups of every row with one copy per row.
+  const size_t stage_cap = (size_t)env_int("SF_GEMV_STAGE_KB", 64) * 1024;
+  int KC, contiguous;
+  size_t RS;
+  if ((size_t)R * (K / 2) <= stage_cap) {
+    KC = K;
+    RS = K / 2;
+    contiguous = 1;
+  } else {
+    long long kc = (long long)(stage_cap / R) * 2;
+    kc = (kc / gs) * gs;
+    if (kc < gs) kc = gs;
+    if (kc > K) kc = K;
+    KC = (int)kc;
+    RS = pad_to((size_t)KC / 2, 128, (size_t)4 * LB);
+    contiguous = 0;
+  }
+  const int GC = KC / gs;
+  const int GPS = (GC + KS - 1) / KS;
+  const size_t stage = ((size_t)R * RS + 127) & ~(size_t)127;
+  const size_t csb_target = LB == 16 ? 16 : (LB == 8 ? 64 : 32);
+  const size_t CSB = pad_to((size_t)K, 128, csb_target);
+  const size_t TS = pad_to(3 * CSB, 128, LB == 4 ? 64 : 0);
+  const size_t red_base = 128;
+  const size_t red_bytes = (size_t)2 * KS * T * R * 4;
+  const size_t xs_base = (red_base + red_bytes + 15) & ~(size_t)15;
+  const size_t xb_base = (xs_base + (size_t)2 * T * G * 4 + 127) & ~(size_t)127;
+  const size_t sring_half = ((size_t)R * G * 4 + 16 + 127) & ~(size_t)127;
+  const size_t sring_bytes = 2 * sring_half;
+  const size_t sring_base = (xb_base + (size_t)T * TS + 127) & ~(size_t)127;
+  const size_t stage_base = sring_base + 2 * sring_bytes;
+  const size_t budget = (size_t)env_int("SF_GEMV_SMEM_KB", 220) * 1024;
+  const size_t cap = budget < (size_t)di.smem_optin ? budget : (size_t)di.smem_optin;
+  const int nrb = (rows_cta + R - 1) / R;
+  const int nkc = (K + KC - 1) / KC;
+  const long long nchunks = (long long)nrb * nkc;
+  if (stage_base + (nchunks > 1 ? 2 : 1) * stage > cap) return false;
+  long long S = (long long)((cap - stage_base) / stage);
+  const int want_st = env_int("SF_GEMV_STAGES", 3);
+  if (S > want_st) S = want_st;
+  if (S > kMaxStages) S = kMaxStages;
+  if (S > nchunks) S = nchunks;
+  if (S < 1) S = 1;
+  pl.LB = LB;
+  pl.grid = grid;
+  pl.threads = (KS * RG + 1) * 32;
+  pl.smem = stage_base + (size_t)S * stage;
+  ImmaParams& q = pl.p;
+  q.N = N; q.K = K; q.G = G; q.gs = gs;
+  q.KS = KS; q.RG = RG; q.R = R; q.KC = KC; q.nst = (int)S; q.GPS = GPS; q.contiguous = contiguous;
+  q.RS = (uint32_t)RS; q.stage_bytes = (uint32_t)stage; q.stage_base = (uint32_t)stage_base;
+  q.xb_base = (uint32_t)xb_base; q.CSB = (uint32_t)CSB; q.TS = (uint32_t)TS;
+  q.xs_base = (uint32_t)xs_base; q.red_base = (uint32_t)red_base;
+  q.sring_base = (uint32_t)sring_base; q.sring_bytes = (uint32_t)sring_bytes;
+  q.trace_id = 0;
+  return pl.threads <= kImmaMaxThreads;
+}
+
+cudaError_t launch_gemv_imma(int T, bool asym, const ImmaPlan& pl0, cudaStream_t st, bool pdl) {
+  ImmaPlan pl = pl0;
+#ifdef SF_GEMV_TRACE
+  pl.p.trace_id = g_trace_counter++;
+#endif
+  if (asym) {
+    if (pl.LB == 16) return launch_lb<true, 16>(T, pl.p, pl.grid, pl.threads, pl.smem, st, pdl);
+    if (pl.LB == 8) return launch_lb<true, 8>(T, pl.p, pl.grid, pl.threads, pl.smem, st, pdl);
+    return launch_lb<true, 4>(T, pl.p, pl.grid, pl.threads, pl.smem, st, pdl);
+  }
+  if (pl.LB == 16) return launch_lb<false, 16>(T, pl.p, pl.grid, pl.threads, pl.smem, st, pdl);
+  if (pl.LB == 8) return launch_lb<false, 8>(T, pl.p, pl.grid, pl.threads, pl.smem, st, pdl);
+  return launch_lb<false, 4>(T, pl.p, pl.grid, pl.threads, pl.smem, st, pdl);
+}
+
+}  // namespace sf

@@ -7,11 +7,13 @@
 namespace sf {
 
 constexpr int kMaxDevices = 16;
-constexpr int kMaxStages = 8;
-constexpr int kRedOffset = 256;        // barriers live in [0, 128)
+constexpr int kMaxStages = 6;          // + 2 scale-ring slots: 16 barriers below 128 B
 constexpr int kMaxGemvT = 8;           // decode GEMV handles up to 8 tokens per launch
 constexpr int kGemvMaxThreads = 512;   // keeps up to 128 registers per thread
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s bound on every device wait
+// Bound on every device-side wait, in SM clock cycles (about 2 s at 2 GHz).
+// clock64 is read only after a failed poll; it is a cheap per-SM counter
+// (%globaltimer is far slower to read and must not sit in a poll loop).
+constexpr long long kWaitCycles = 4000000000ll;
 
 struct DeviceInfo {
   bool ready = false;
@@ -32,10 +34,30 @@ struct GemvParams {
   uint32_t stage_bytes, s_off, z_off, stage_base;
 };
 
-struct GemvPlan {
-  int KS, RG, R, S, grid, threads;
-  size_t stage_bytes, s_off, z_off, stage_base, smem;
+// Decode GEMV on the tensor cores (sf_q4_gemv.cu).
+struct ImmaParams {
+  const uint8_t* W;
+  const float* S;
+  const float* Z;
+  const float* bias;
+  const void* X;
+  void* Y;
+  int N, K, G, gs, xdt, ydt;
+  int KS, RG, R, KC, nst, GPS;   // K-slices, row groups, rows per block, k per chunk, stages, groups per slice
+  int contiguous;                // 1: a stage holds whole rows (one contiguous region)
+  uint32_t RS, stage_bytes, stage_base, xb_base, CSB, TS, xs_base, red_base;
+  uint32_t sring_base, sring_bytes;  // scale/zero ring: 2 slots, zeros in the upper half
+  int trace_id;                  // launch index for the optional timeline trace
 };
+
+struct ImmaPlan {
+  ImmaParams p;
+  int LB, grid, threads;
+  size_t smem;
+};
+
+bool plan_gemv_imma(int N, int K, int T, int gs, bool asym, ImmaPlan& pl);
+cudaError_t launch_gemv_imma(int T, bool asym, const ImmaPlan& pl, cudaStream_t st, bool pdl);
 
 int fail(int code, const char* fmt, ...);
 int cuda_fail(cudaError_t e, const char* what);
@@ -57,6 +79,7 @@ static __device__ unsigned int g_dev_error = 0;
     return v;                                                             \
   }
 unsigned int take_dev_error_gemv();
+unsigned int take_dev_error_gemv_tc();
 unsigned int take_dev_error_tc();
 
 // ---------------------------------------------------------------------------
@@ -122,13 +145,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after kWaitNs, records the failure in the sticky
+// Bounded wait: gives up after kWaitCycles, records the failure in the sticky
 // device error word and returns false so that the caller can wind down.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
+  const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - t0 > kWaitNs) {
+    if (clock64() - t0 > kWaitCycles) {
       atomicOr(&g_dev_error, 1u);
       return false;
     }
