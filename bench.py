@@ -75,9 +75,9 @@ class ClockSampler:
              "clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
                  "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except FileNotFoundError:
@@ -111,8 +111,11 @@ class ClockSampler:
             for n, v in zip(names, parts[4:8]):
                 if v.lower() == "active":
                     reasons.add(n)
-        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": maxm,
-                "reasons": sorted(reasons), "samples": len(mhz)}
+        out = {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": maxm,
+               "reasons": sorted(reasons), "samples": len(mhz)}
+        if not mhz:
+            out["sampler_output"] = " | ".join(self.lines[:3])[:300]
+        return out
 
 
 # ---------------------------------------------------------------------------
@@ -179,11 +182,23 @@ def run_ours(args, rank, world, local_rank):
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = _lib.launch_count()
     with ClockSampler(local_rank) as clocks:
+        # keep the GPU under the same load until the sampler is producing
+        t_end = time.perf_counter() + 5.0
+        while len(clocks.lines) < 2 and time.perf_counter() < t_end:
+            for _ in range(20):
+                runner.run()
+            runner.stream.synchronize()
+        n_before = len(clocks.lines)
         start.record(runner.stream)
         for _ in range(args.steps):
             runner.run()
         stop.record(runner.stream)
         stop.synchronize()
+        t_end = time.perf_counter() + 2.0
+        while len(clocks.lines) <= n_before and time.perf_counter() < t_end:
+            for _ in range(20):
+                runner.run()
+            runner.stream.synchronize()
     barrier()
     torch.cuda.synchronize(device)
     ms = start.elapsed_time(stop) / args.steps
@@ -241,7 +256,7 @@ def run_ours(args, rank, world, local_rank):
         "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(per_gpu / peak, 4),
                      "peak_kind": peak_kind,
-                     "kernel": "q4_gemv_kernel<1,false> (all launches of the step)",
+                     "kernel": "q4_gemv_imma_kernel<1,sym,16> (all 224 launches of the step)",
                      "bytes_per_launch_avg": step_bytes // runner.kernels_per_step,
                      "launch_us_avg": round(ms * 1e3 / runner.kernels_per_step, 3),
                      "traffic": traffic_from_profile(args.workload, args.batch)},
@@ -361,7 +376,7 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="7b", choices=sorted(HIDDEN))

@@ -144,13 +144,23 @@ __device__ __forceinline__ void lds_digits(const uint8_t* p, uint32_t* b) {
 // %globaltimer (ns) written to the buffer given to sf_q4_gemv_set_trace.
 #ifdef SF_GEMV_TRACE
 __device__ unsigned long long* g_gtrace = nullptr;
+__device__ volatile float g_trace_sink;
 #define GT(slot)                                                                        \
   do {                                                                                  \
     if (g_gtrace)                                                                       \
-      g_gtrace[((size_t)p.trace_id * gridDim.x + blockIdx.x) * 16 + (slot)] = globaltimer_ns(); \
+      g_gtrace[((size_t)p.trace_id * gridDim.x + blockIdx.x) * 32 + (slot)] = globaltimer_ns(); \
+  } while (0)
+// cycle stamp after v is available (in-order issue: the store waits for v)
+#define CT(slot, v)                                                                     \
+  do {                                                                                  \
+    if (g_gtrace && threadIdx.x == 0) {                                                 \
+      g_trace_sink = (v);                                                               \
+      g_gtrace[((size_t)p.trace_id * gridDim.x + blockIdx.x) * 32 + 16 + (slot)] = clock64(); \
+    }                                                                                   \
   } while (0)
 #else
 #define GT(slot) do { } while (0)
+#define CT(slot, v) do { } while (0)
 #endif
 
 // ---------------------------------------------------------------------------
@@ -245,6 +255,7 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
   const int nthr = ncons * 32;
   griddep_wait();
   if (threadIdx.x == 0) GT(1);
+  CT(10, 0.f);
 
   // (1) activations -> per-(token, group) fixed point, three int8 digits.
   //     All of a thread's loads are issued before any of them is used.
@@ -266,6 +277,7 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
           for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
         }
       }
+      CT(0, v[0][0]);
 #pragma unroll
       for (int i = 0; i < NB; ++i) {
         const int ob = base + i * nthr;
@@ -319,7 +331,9 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
       }
     }
   }
+  CT(1, 0.f);
   named_barrier_sync(1, nthr);
+  CT(2, 0.f);
   if (threadIdx.x == 0) GT(2);
 
   // (2) stream the row blocks
@@ -382,6 +396,7 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
               zp[mt][h] = ASYM ? __ldg(p.Z + gix) : 8.f;
             }
           }
+        if (c == 0 && gi == ga) CT(3, sc[0][0] + sc[1][1]);
         int C[kMT][NT][4];
 #pragma unroll
         for (int mt = 0; mt < kMT; ++mt)
@@ -416,6 +431,8 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
             }
           }
         }
+        if (c == 0 && gi == ga) CT(4, (float)(C[0][0][0] + C[1][NT - 1][3]));
+        if (c == 0 && gi == ga + 1) CT(6, (float)(C[0][0][0] + C[1][NT - 1][3]));
         // epilogue of group gi: recombine digits, remove zeff * sum(x), scale
 #pragma unroll
         for (int tg = 0; tg < NTG; ++tg) {
@@ -434,7 +451,9 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
               }
           }
         }
+        if (c == 0 && gi == ga) CT(5, acc[0][0][0] + acc[1][0][1]);
       }
+      if (c == 0) CT(7, acc[0][0][0] + acc[1][0][1]);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
@@ -452,7 +471,9 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
             rbuf[(ks * T + tok) * p.R + (rgp * kMT + mt) * 16 + g + 8 * h] = acc[mt][tg][h];
       }
     }
+    if (b == 0) CT(8, 0.f);
     named_barrier_sync(1, nthr);
+    if (b == 0) CT(9, 0.f);
     __syncwarp();
     if (lane == 0) mbar_arrive(&sempty[sl]);
     for (int idx = threadIdx.x; idx < rows * T; idx += nthr) {
