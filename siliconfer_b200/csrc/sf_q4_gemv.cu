@@ -48,7 +48,7 @@ SF_DEFINE_ERROR_READER(take_dev_error_gemv_tc)
 namespace {
 
 constexpr int kMT = 2;                 // m16 tiles per warp per row block
-constexpr int kImmaMaxThreads = 512;   // 15 consumer warps + 1 producer warp
+constexpr int kImmaMaxThreads = 544;   // up to 16 consumer warps + 1 producer warp
 constexpr uint32_t kPiece = 4096;      // contiguous bulk-copy piece (bytes)
 
 __device__ __forceinline__ void ld_x8(const void* x, size_t idx, int dt, float* v) {
@@ -77,10 +77,11 @@ __device__ __forceinline__ void st_y(void* y, size_t idx, float v, int dt) {
   else reinterpret_cast<__nv_bfloat16*>(y)[idx] = __float2bfloat16_rn(v);
 }
 
-// D += A(u8, 16x32) * B(s8, 32x8), s32 accumulate.
+// D += A(u8, 16x32) * B(s8, 32x8), s32 accumulate.  Not volatile: it has no
+// side effects, so the compiler may interleave independent accumulator chains.
 __device__ __forceinline__ void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                      uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
@@ -414,22 +415,28 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
             }
           }
           const int boff = ((kseg - k0) >> 1) + t * LB;
+          uint32_t w0[kMT][WPL], w1[kMT][WPL];
 #pragma unroll
           for (int mt = 0; mt < kMT; ++mt) {
-            if ((rgp * kMT + mt) * 16 >= rows) continue;   // whole tile past the end
             const int lr = (rgp * kMT + mt) * 16 + g;
-            uint32_t w0[WPL], w1[WPL];
-            lds_words<LB>(buf + (size_t)lr * p.RS + boff, w0);
-            lds_words<LB>(buf + (size_t)(lr + 8) * p.RS + boff, w1);
+            if ((rgp * kMT + mt) * 16 < rows) {
+              lds_words<LB>(buf + (size_t)lr * p.RS + boff, w0[mt]);
+              lds_words<LB>(buf + (size_t)(lr + 8) * p.RS + boff, w1[mt]);
+            } else {
 #pragma unroll
-            for (int q = 0; q < WPL; ++q) {
-              const uint32_t a0 = nib_lo<ASYM>(w0[q]), a2 = nib_hi<ASYM>(w0[q]);
-              const uint32_t a1 = nib_lo<ASYM>(w1[q]), a3 = nib_hi<ASYM>(w1[q]);
+              for (int q = 0; q < WPL; ++q) w0[mt][q] = w1[mt][q] = 0u;
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < WPL; ++q)
+#pragma unroll
+            for (int mt = 0; mt < kMT; ++mt) {
+              const uint32_t a0 = nib_lo<ASYM>(w0[mt][q]), a2 = nib_hi<ASYM>(w0[mt][q]);
+              const uint32_t a1 = nib_lo<ASYM>(w1[mt][q]), a3 = nib_hi<ASYM>(w1[mt][q]);
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt)
                 imma(C[mt][nt], a0, a1, a2, a3, bq[nt][2 * q], bq[nt][2 * q + 1]);
             }
-          }
         }
         if (c == 0 && gi == ga) CT(4, (float)(C[0][0][0] + C[1][NT - 1][3]));
         if (c == 0 && gi == ga + 1) CT(6, (float)(C[0][0][0] + C[1][NT - 1][3]));
@@ -559,7 +566,7 @@ bool plan_gemv_imma(int N, int K, int T, int gs, bool asym, ImmaPlan& pl) {
   const int max_cons = kImmaMaxThreads / 32 - 1;
   int RG = (rows_cta + 16 * kMT - 1) / (16 * kMT);
   if (RG > 2) RG = 2;
-  int KS = env_int("SF_GEMV_WARPS", 8) / RG;
+  int KS = env_int("SF_GEMV_WARPS", 16) / RG;
   if (KS < 1) KS = 1;
   if (KS > G) KS = G;
   if (KS * RG > max_cons) KS = max_cons / RG;
