@@ -85,6 +85,36 @@ int sf_q4_linear(const uint8_t* W, const float* scales, const float* zeros,
                  int N, int K, int T, int group_size, int flags, void* stream);
 #define SF_FLAG_PDL 1
 
+/* ---- a decode step: many GEMVs in one persistent launch -------------------
+ * The reference calls Q4Linear once per projection, seven times per layer
+ * (siliconfer/model/layers.py:93-95, 133, 144; q4_linear.py:49-68).  Here a
+ * caller describes the whole sequence once and replays it: one cooperative
+ * launch streams every task's weights back to back, so HBM stays busy across
+ * projection boundaries.  A task with wait_before != 0 reads X only after
+ * every earlier task has finished writing (a grid-wide barrier, bounded in
+ * time), which is how a dependency such as o_proj <- attention(q, k, v) is
+ * expressed; tasks without it may overlap with the previous ones.
+ * All tasks must share T (1..8), the layout (zeros NULL or not) and the group
+ * class (group_size % 128, % 64 or % 32 == 0).  `workspace` is caller-owned
+ * device memory of sf_q4_step_workspace_bytes(ntasks) bytes, 256-byte aligned,
+ * kept alive until sf_q4_step_destroy; it holds the task table and the
+ * barrier counter, so two handles that run concurrently need two workspaces.
+ * create() uploads the table synchronously; run() is asynchronous. */
+typedef struct {
+  const uint8_t* W;
+  const float* scales;
+  const float* zeros;   /* NULL: symmetric */
+  const float* bias;    /* NULL: none */
+  const void* X;        /* [T, K] of x_dtype */
+  void* Y;              /* [T, N] of y_dtype */
+  int N, K, T, group_size, x_dtype, y_dtype, wait_before;
+} sf_q4_task;
+size_t sf_q4_step_workspace_bytes(int ntasks);
+int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size_t workspace_bytes,
+                      void** handle_out);
+int sf_q4_step_run(void* handle, void* stream);
+void sf_q4_step_destroy(void* handle);
+
 /* Device dequant to fp32/fp16/bf16 [N, K].  fp32 output is bit-exact with
    dequantize_sym / dequantize_asym (siliconfer/quant/primitives.py:54-75,
    117-140); fp16/bf16 are that value rounded to nearest even. */

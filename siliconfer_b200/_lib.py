@@ -18,6 +18,14 @@ SF_FLAG_PDL = 1
 SF_OK = 0
 
 _P, _I, _LL = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
+_SZ = ctypes.c_size_t
+
+
+class Q4Task(ctypes.Structure):
+    """Mirror of sf_q4_task (include/sf_q4.h)."""
+    _fields_ = [("W", _P), ("scales", _P), ("zeros", _P), ("bias", _P), ("X", _P), ("Y", _P),
+                ("N", _I), ("K", _I), ("T", _I), ("group_size", _I), ("x_dtype", _I),
+                ("y_dtype", _I), ("wait_before", _I)]
 
 # name -> argtypes (restype is int unless listed in _RESTYPES)
 SIGNATURES = {
@@ -34,9 +42,14 @@ SIGNATURES = {
     "sf_q4_quantize_pack": [_P, _P, _P, _P, _I, _I, _I, _P],
     "sf_q4_check_device_error": [],
     "sf_q4_launch_count": [],
+    "sf_q4_step_workspace_bytes": [_I],
+    "sf_q4_step_create": [ctypes.POINTER(Q4Task), _I, _P, _SZ, ctypes.POINTER(_P)],
+    "sf_q4_step_run": [_P, _P],
+    "sf_q4_step_destroy": [_P],
 }
 _RESTYPES = {"sf_status_string": ctypes.c_char_p, "sf_last_error": ctypes.c_char_p,
-             "sf_q4_launch_count": _LL}
+             "sf_q4_launch_count": _LL, "sf_q4_step_workspace_bytes": _SZ,
+             "sf_q4_step_destroy": None}
 
 _lib = None
 

@@ -253,17 +253,17 @@ int run_linear(const uint8_t* W, const float* S, const float* Z, const float* bi
     // Decode GEMV on the tensor cores.  Larger T that the GEMM path declined
     // is split into launches of at most kMaxGemvT tokens (weights re-read).
     int tmax = T < kMaxGemvT ? T : kMaxGemvT;
-    ImmaPlan pl;
+    StepPlan pl;
     while (tmax > 0 && !plan_gemv_imma(N, K, tmax, gs, Z != nullptr, pl)) tmax >>= 1;
     for (int t0 = 0; tmax > 0 && t0 < T; t0 += tmax) {
       const int tc = T - t0 < tmax ? T - t0 : tmax;
       if (!plan_gemv_imma(N, K, tc, gs, Z != nullptr, pl)) break;
-      ImmaParams& q = pl.p;
+      ImmaParams& q = pl.sp.single;
       q.W = W; q.S = S; q.Z = Z; q.bias = bias;
       q.X = static_cast<const uint8_t*>(X) + (size_t)t0 * K * xe;
       q.Y = static_cast<uint8_t*>(Y) + (size_t)t0 * N * ye;
       q.xdt = xdt; q.ydt = ydt;
-      cudaError_t e = launch_gemv_imma(tc, Z != nullptr, pl, stream, pdl);
+      cudaError_t e = launch_gemv_imma(pl, stream, pdl);
       if (e != cudaSuccess) return cuda_fail(e, "q4_gemv_imma_kernel launch");
       g_launches.fetch_add(1, std::memory_order_relaxed);
       if (t0 + tc == T) return SF_OK;

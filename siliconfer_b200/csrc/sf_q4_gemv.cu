@@ -37,11 +37,15 @@
 
 #include <cstdint>
 #include <cstdlib>
+#include <vector>
+#include <atomic>
 
 #include "sf_q4.h"
 #include "sf_q4_internal.h"
 
 namespace sf {
+extern std::atomic<long long> g_launches;
+int fail(int code, const char* fmt, ...);
 
 SF_DEFINE_ERROR_READER(take_dev_error_gemv_tc)
 
@@ -54,11 +58,11 @@ constexpr uint32_t kPiece = 4096;      // contiguous bulk-copy piece (bytes)
 __device__ __forceinline__ void ld_x8(const void* x, size_t idx, int dt, float* v) {
   if (dt == SF_F32) {
     const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + idx);
-    const float4 a = __ldg(p), b = __ldg(p + 1);
+    const float4 a = __ldcg(p), b = __ldcg(p + 1);
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
     v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
   } else {
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + idx));
+    const uint4 u = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + idx));
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -145,28 +149,55 @@ __device__ __forceinline__ void lds_digits(const uint8_t* p, uint32_t* b) {
 // %globaltimer (ns) written to the buffer given to sf_q4_gemv_set_trace.
 #ifdef SF_GEMV_TRACE
 __device__ unsigned long long* g_gtrace = nullptr;
-__device__ volatile float g_trace_sink;
-#define GT(slot)                                                                        \
-  do {                                                                                  \
-    if (g_gtrace)                                                                       \
-      g_gtrace[((size_t)p.trace_id * gridDim.x + blockIdx.x) * 32 + (slot)] = globaltimer_ns(); \
-  } while (0)
-// cycle stamp after v is available (in-order issue: the store waits for v)
-#define CT(slot, v)                                                                     \
-  do {                                                                                  \
-    if (g_gtrace && threadIdx.x == 0) {                                                 \
-      g_trace_sink = (v);                                                               \
-      g_gtrace[((size_t)p.trace_id * gridDim.x + blockIdx.x) * 32 + 16 + (slot)] = clock64(); \
-    }                                                                                   \
+#define GT(slot)                                                                         \
+  do {                                                                                   \
+    if (g_gtrace)                                                                        \
+      g_gtrace[((size_t)sp.trace_id * gridDim.x + blockIdx.x) * 16 + (slot)] = globaltimer_ns(); \
   } while (0)
 #else
 #define GT(slot) do { } while (0)
-#define CT(slot, v) do { } while (0)
 #endif
 
 // ---------------------------------------------------------------------------
+// Task-list kernel.  A task is one GEMV (ImmaParams); StepParams carries the
+// launch-wide shared-memory layout.  The producer warp walks every task's row
+// blocks and k-chunks without waiting on anything but ring slots; consumers
+// walk the same sequence, so both sides agree on every ring slot and phase.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ const ImmaParams& task_at(const StepParams& sp, int i) {
+  return sp.tasks ? sp.tasks[i] : sp.single;
+}
+
+// Grid-wide barrier among the consumer threads of every CTA (cooperative
+// launch, so all CTAs are resident).  Bounded: on timeout the sticky error
+// word is set and the caller stops waiting.
+__device__ __forceinline__ bool grid_barrier(unsigned int* ctr, unsigned int target, int nthr) {
+  named_barrier_sync(1, nthr);
+  __shared__ int ok_s;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(ctr, 1u);
+    const long long t0 = clock64();
+    int ok = 1;
+    while (true) {
+      unsigned int v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+      if (v >= target) break;
+      if (clock64() - t0 > kWaitCycles) {
+        atomicOr(&g_dev_error, 2u);
+        ok = 0;
+        break;
+      }
+      __nanosleep(64);
+    }
+    ok_s = ok;
+  }
+  named_barrier_sync(1, nthr);
+  return ok_s != 0;
+}
+
 template <int T, bool ASYM, int LB>
-__global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const ImmaParams p) {
+__global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const __grid_constant__ StepParams sp) {
   constexpr int NTG = (T + 3) / 4;    // token groups of 4 (one token per lane t)
   constexpr int NT = 2 * NTG;         // n8 tiles: (d0,d1) and (d2,-) per token group
   constexpr int WPL = LB / 4;         // 32-bit words per lane per row per segment
@@ -176,25 +207,19 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
   uint64_t* empty = full + kMaxStages;
   uint64_t* sfull = empty + kMaxStages;
   uint64_t* sempty = sfull + 2;
-  float* red = reinterpret_cast<float*>(smem + p.red_base);
-  float* xgsc = reinterpret_cast<float*>(smem + p.xs_base);
-  float* xsum = xgsc + T * p.G;
-  uint8_t* xb = smem + p.xb_base;
-  uint8_t* sring = smem + p.sring_base;
-  uint8_t* stages = smem + p.stage_base;
+  float* red = reinterpret_cast<float*>(smem + sp.red_base);
+  float* xgsc = reinterpret_cast<float*>(smem + sp.xs_base);
+  uint8_t* xb = smem + sp.xb_base;
+  uint8_t* sring = smem + sp.sring_base;
+  uint8_t* stages = smem + sp.stage_base;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int ncons = p.KS * p.RG;
-  const int rb = (int)((long long)p.N * blockIdx.x / gridDim.x);
-  const int re = (int)((long long)p.N * (blockIdx.x + 1) / gridDim.x);
-  const int nrb = (re - rb + p.R - 1) / p.R;                // row blocks
-  const int nkc = (p.K + p.KC - 1) / p.KC;                   // k-chunks per row block
-  const int KH = p.K >> 1;
+  const int ncons = sp.ncons;
 
   if (threadIdx.x == 0) {
     GT(0);
-    for (int i = 0; i < p.nst; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], ncons); }
+    for (int i = 0; i < sp.nst; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], ncons); }
     for (int i = 0; i < 2; ++i) { mbar_init(&sfull[i], 1); mbar_init(&sempty[i], ncons); }
     fence_mbar_init();
   }
@@ -203,49 +228,58 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
 
   if (warp == ncons) {
     // ------------------------------ producer ------------------------------
-    int c = 0;
-    for (int b = 0; b < nrb; ++b) {
-      const int r0 = rb + b * p.R;
-      const int rows = min(p.R, re - r0);
-      const int sl = b & 1;
-      int ok = 1;
-      if (lane == 0 && b >= 2) ok = mbar_wait(&sempty[sl], ((b >> 1) - 1) & 1);
-      if (!__shfl_sync(0xffffffffu, ok, 0)) return;
-      if (lane == 0) {  // scales (+ zeros) of the row block, from the 16-byte boundary below
-        const uintptr_t src = reinterpret_cast<uintptr_t>(p.S + (size_t)r0 * p.G);
-        const uint32_t pre = (uint32_t)(src & 15);
-        const uint32_t nb = (pre + (uint32_t)rows * p.G * 4) & ~15u;
-        uint8_t* dst = sring + (size_t)sl * p.sring_bytes;
-        mbar_arrive_expect_tx(&sfull[sl], ASYM ? 2 * nb : nb);
-        if (nb) {
-          bulk_g2s(dst, reinterpret_cast<const void*>(src - pre), nb, &sfull[sl]);
-          if (ASYM)
-            bulk_g2s(dst + p.sring_bytes / 2,
-                     reinterpret_cast<const uint8_t*>(p.Z + (size_t)r0 * p.G) - pre, nb, &sfull[sl]);
-        }
-      }
-      for (int kc = 0; kc < nkc; ++kc, ++c) {
-        const int st = c % p.nst, use = c / p.nst;
-        ok = 1;
-        if (lane == 0 && use > 0) ok = mbar_wait(&empty[st], (use - 1) & 1);
+    int c = 0, b = 0;
+    for (int ti = 0; ti < sp.ntasks; ++ti) {
+      const ImmaParams& p = task_at(sp, ti);
+      const int rb = (int)((long long)p.N * blockIdx.x / gridDim.x);
+      const int re = (int)((long long)p.N * (blockIdx.x + 1) / gridDim.x);
+      const int nrb = (re - rb + p.R - 1) / p.R;
+      const int nkc = (p.K + p.KC - 1) / p.KC;
+      const int KH = p.K >> 1;
+      for (int bb = 0; bb < nrb; ++bb, ++b) {
+        const int r0 = rb + bb * p.R;
+        const int rows = min(p.R, re - r0);
+        const int sl = b & 1;
+        int ok = 1;
+        if (lane == 0 && b >= 2) ok = mbar_wait(&sempty[sl], ((b >> 1) - 1) & 1);
         if (!__shfl_sync(0xffffffffu, ok, 0)) return;
-        const int k0 = kc * p.KC;
-        const uint32_t cb = (uint32_t)(min(p.KC, p.K - k0) >> 1);
-        uint8_t* buf = stages + (size_t)st * p.stage_bytes;
-        if (lane == 0) mbar_arrive_expect_tx(&full[st], cb * rows);
-        __syncwarp();
-        const uint8_t* src = p.W + (size_t)r0 * KH + (k0 >> 1);
-        if (p.contiguous) {
-          const uint32_t total = cb * rows;   // multiple of 16
-          const uint32_t npc = (total + kPiece - 1) / kPiece;
-          for (uint32_t j = lane; j < npc; j += 32) {
-            const uint32_t off = j * kPiece;
-            const uint32_t n = total - off < kPiece ? total - off : kPiece;
-            bulk_g2s(buf + off, src + off, n, &full[st]);
+        if (lane == 0) {  // scales (+ zeros) of the row block, from the 16-byte boundary below
+          const uintptr_t src = reinterpret_cast<uintptr_t>(p.S + (size_t)r0 * p.G);
+          const uint32_t pre = (uint32_t)(src & 15);
+          const uint32_t nb = (pre + (uint32_t)rows * p.G * 4) & ~15u;
+          uint8_t* dst = sring + (size_t)sl * sp.sring_bytes;
+          mbar_arrive_expect_tx(&sfull[sl], ASYM ? 2 * nb : nb);
+          if (nb) {
+            bulk_g2s(dst, reinterpret_cast<const void*>(src - pre), nb, &sfull[sl]);
+            if (ASYM)
+              bulk_g2s(dst + sp.sring_bytes / 2,
+                       reinterpret_cast<const uint8_t*>(p.Z + (size_t)r0 * p.G) - pre, nb,
+                       &sfull[sl]);
           }
-        } else {
-          for (int r = lane; r < rows; r += 32)
-            bulk_g2s(buf + (size_t)r * p.RS, src + (size_t)r * KH, cb, &full[st]);
+        }
+        for (int kc = 0; kc < nkc; ++kc, ++c) {
+          const int st = c % sp.nst, use = c / sp.nst;
+          ok = 1;
+          if (lane == 0 && use > 0) ok = mbar_wait(&empty[st], (use - 1) & 1);
+          if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+          const int k0 = kc * p.KC;
+          const uint32_t cb = (uint32_t)(min(p.KC, p.K - k0) >> 1);
+          uint8_t* buf = stages + (size_t)st * sp.stage_bytes;
+          if (lane == 0) mbar_arrive_expect_tx(&full[st], cb * rows);
+          __syncwarp();
+          const uint8_t* src = p.W + (size_t)r0 * KH + (k0 >> 1);
+          if (p.contiguous) {
+            const uint32_t total = cb * rows;   // multiple of 16
+            const uint32_t npc = (total + kPiece - 1) / kPiece;
+            for (uint32_t j = lane; j < npc; j += 32) {
+              const uint32_t off = j * kPiece;
+              const uint32_t n = total - off < kPiece ? total - off : kPiece;
+              bulk_g2s(buf + off, src + off, n, &full[st]);
+            }
+          } else {
+            for (int r = lane; r < rows; r += 32)
+              bulk_g2s(buf + (size_t)r * p.RS, src + (size_t)r * KH, cb, &full[st]);
+          }
         }
       }
     }
@@ -256,241 +290,244 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
   const int nthr = ncons * 32;
   griddep_wait();
   if (threadIdx.x == 0) GT(1);
-  CT(10, 0.f);
+  int c = 0, b = 0;
+  unsigned int nbar = 0;
+  bool ok_wait = true;
 
-  // (1) activations -> per-(token, group) fixed point, three int8 digits.
-  //     All of a thread's loads are issued before any of them is used.
-  {
-    const int octs_tok = p.K >> 3;
-    const int total = T * octs_tok;
-    const int lpg = p.gs >> 3;  // octets (lanes) per group: 4, 8, 16 or 32
-    constexpr int NB = 4;
-    for (int base = warp * 32; base < total; base += nthr * NB) {
-      float v[NB][8];
+  for (int ti = 0; ti < sp.ntasks; ++ti) {
+    const ImmaParams& p = task_at(sp, ti);
+    if (ti > 0 && p.wait_before && ok_wait)
+      ok_wait = grid_barrier(sp.bar, (++nbar) * gridDim.x, nthr);
+    float* xsum = xgsc + T * p.G;
+
+    // (1) activations -> per-(token, group) fixed point, three int8 digits.
+    //     All of a thread's loads are issued before any of them is used; the
+    //     loads go through L2 (an earlier task of this launch may have written x).
+    {
+      const int octs_tok = p.K >> 3;
+      const int total = T * octs_tok;
+      const int lpg = p.gs >> 3;  // octets (lanes) per group: 4, 8, 16 or 32
+      constexpr int NB = 4;
+      for (int base = warp * 32; base < total; base += nthr * NB) {
+        float v[NB][8];
 #pragma unroll
-      for (int i = 0; i < NB; ++i) {
-        const int o = base + i * nthr + lane;
-        if (o < total) {
-          const int tok = o / octs_tok;
-          ld_x8(p.X, (size_t)tok * p.K + (size_t)(o - tok * octs_tok) * 8, p.xdt, v[i]);
-        } else {
+        for (int i = 0; i < NB; ++i) {
+          const int o = base + i * nthr + lane;
+          if (o < total) {
+            const int tok = o / octs_tok;
+            ld_x8(p.X, (size_t)tok * p.K + (size_t)(o - tok * octs_tok) * 8, p.xdt, v[i]);
+          } else {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+            for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+          }
         }
-      }
-      CT(0, v[0][0]);
 #pragma unroll
-      for (int i = 0; i < NB; ++i) {
-        const int ob = base + i * nthr;
-        if (ob >= total) break;                       // uniform across the warp
-        const int o = ob + lane;
-        const bool ok = o < total;
-        float m = 0.f;
-        bool bad = false;
+        for (int i = 0; i < NB; ++i) {
+          const int ob = base + i * nthr;
+          if (ob >= total) break;                       // uniform across the warp
+          const int o = ob + lane;
+          const bool ok = o < total;
+          float m = 0.f;
+          bool bad = false;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          m = fmaxf(m, fabsf(v[i][j]));
-          bad |= !(fabsf(v[i][j]) <= 3.402823466e38f);
-        }
-        int badi = bad;
-        for (int off = 1; off < lpg; off <<= 1) {
-          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-          badi |= __shfl_xor_sync(0xffffffffu, badi, off);
-        }
-        // binary exponent field of the group max; groups below 2^-105 are zero
-        const int be = (int)(__float_as_uint(m) >> 23);
-        const bool zero = badi || be < 22;
-        const float scl = zero ? 0.f : __uint_as_float((uint32_t)(275 - be) << 23);   // 2^(22-E)
-        int d[3][8];
-        int s = 0;
+          for (int j = 0; j < 8; ++j) {
+            m = fmaxf(m, fabsf(v[i][j]));
+            bad |= !(fabsf(v[i][j]) <= 3.402823466e38f);
+          }
+          int badi = bad;
+          for (int off = 1; off < lpg; off <<= 1) {
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+            badi |= __shfl_xor_sync(0xffffffffu, badi, off);
+          }
+          // binary exponent field of the group max; groups below 2^-105 are zero
+          const int be = (int)(__float_as_uint(m) >> 23);
+          const bool zero = badi || be < 22;
+          const float scl = zero ? 0.f : __uint_as_float((uint32_t)(275 - be) << 23);   // 2^(22-E)
+          int d[3][8];
+          int s = 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int xf = __float2int_rn(v[i][j] * scl);
-          s += xf;
-          const int d0 = (xf << 24) >> 24;
-          const int r1 = (xf - d0) >> 8;
-          const int d1 = (r1 << 24) >> 24;
-          d[0][j] = d0;
-          d[1][j] = d1;
-          d[2][j] = (r1 - d1) >> 8;
-        }
-        for (int off = 1; off < lpg; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-        if (ok) {
-          const int tok = o / octs_tok;
-          const int ko = (o - tok * octs_tok) * 8;
-          uint8_t* col = xb + (size_t)tok * p.TS + ko;
+          for (int j = 0; j < 8; ++j) {
+            const int xf = __float2int_rn(v[i][j] * scl);
+            s += xf;
+            const int d0 = (xf << 24) >> 24;
+            const int r1 = (xf - d0) >> 8;
+            const int d1 = (r1 << 24) >> 24;
+            d[0][j] = d0;
+            d[1][j] = d1;
+            d[2][j] = (r1 - d1) >> 8;
+          }
+          for (int off = 1; off < lpg; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+          if (ok) {
+            const int tok = o / octs_tok;
+            const int ko = (o - tok * octs_tok) * 8;
+            uint8_t* col = xb + (size_t)tok * p.TS + ko;
 #pragma unroll
-          for (int dg = 0; dg < 3; ++dg)
-            *reinterpret_cast<uint2*>(col + (size_t)dg * p.CSB) = pack_digits(d[dg]);
-          if ((lane & (lpg - 1)) == 0) {
-            const int gi = ko / p.gs;
-            xgsc[tok * p.G + gi] = badi ? __int_as_float(0x7fc00000)
-                                        : (zero ? 0.f : __uint_as_float((uint32_t)(be - 21) << 23));
-            xsum[tok * p.G + gi] = (float)s;
+            for (int dg = 0; dg < 3; ++dg)
+              *reinterpret_cast<uint2*>(col + (size_t)dg * p.CSB) = pack_digits(d[dg]);
+            if ((lane & (lpg - 1)) == 0) {
+              const int gi = ko / p.gs;
+              xgsc[tok * p.G + gi] = badi ? __int_as_float(0x7fc00000)
+                                          : (zero ? 0.f : __uint_as_float((uint32_t)(be - 21) << 23));
+              xsum[tok * p.G + gi] = (float)s;
+            }
           }
         }
       }
     }
-  }
-  CT(1, 0.f);
-  named_barrier_sync(1, nthr);
-  CT(2, 0.f);
-  if (threadIdx.x == 0) GT(2);
+    named_barrier_sync(1, nthr);
+    if (threadIdx.x == 0 && ti == 0) GT(2);
 
-  // (2) stream the row blocks
-  const int ks = warp % p.KS, rgp = warp / p.KS;
-  const uint8_t* bcol[NT];   // B columns this lane supplies, per n8 tile
+    // (2) stream the row blocks of this task
+    const int rb = (int)((long long)p.N * blockIdx.x / gridDim.x);
+    const int re = (int)((long long)p.N * (blockIdx.x + 1) / gridDim.x);
+    const int nrb = (re - rb + p.R - 1) / p.R;
+    const int nkc = (p.K + p.KC - 1) / p.KC;
+    const int ks = warp % p.KS, rgp = warp / p.KS;
+    const bool active = rgp < p.RG;   // warps beyond KS*RG only keep the barriers moving
+    const uint8_t* bcol[NT];          // B columns this lane supplies, per n8 tile
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const int tok = (nt >> 1) * 4 + (g >> 1);
-    const int dg = (nt & 1) ? ((g & 1) ? -1 : 2) : (g & 1);
-    bcol[nt] = (tok < T && dg >= 0) ? xb + (size_t)tok * p.TS + (size_t)dg * p.CSB + t * 2 * LB
-                                    : nullptr;
-  }
+    for (int nt = 0; nt < NT; ++nt) {
+      const int tok = (nt >> 1) * 4 + (g >> 1);
+      const int dg = (nt & 1) ? ((g & 1) ? -1 : 2) : (g & 1);
+      bcol[nt] = (tok < T && dg >= 0) ? xb + (size_t)tok * p.TS + (size_t)dg * p.CSB + t * 2 * LB
+                                      : nullptr;
+    }
 
-  int c = 0;
-  bool ok_wait = true;
-  for (int b = 0; b < nrb; ++b) {
-    const int r0 = rb + b * p.R;
-    const int rows = min(p.R, re - r0);
-    float acc[kMT][NTG][2];
+    for (int bb = 0; bb < nrb; ++bb, ++b) {
+      const int r0 = rb + bb * p.R;
+      const int rows = min(p.R, re - r0);
+      float acc[kMT][NTG][2];
 #pragma unroll
-    for (int mt = 0; mt < kMT; ++mt)
+      for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
-      for (int tg = 0; tg < NTG; ++tg) acc[mt][tg][0] = acc[mt][tg][1] = 0.f;
-    const int sl = b & 1;
-    if (ok_wait) ok_wait = mbar_wait(&sfull[sl], (b >> 1) & 1);
-    const uintptr_t s_src = reinterpret_cast<uintptr_t>(p.S + (size_t)r0 * p.G);
-    const int s_pre = (int)(s_src & 15) >> 2;
-    const int s_cnt = (int)(((s_src & 15) + (uint32_t)rows * p.G * 4) & ~15u) >> 2;
-    const float* ssm = reinterpret_cast<const float*>(sring + (size_t)sl * p.sring_bytes);
-    const float* zsm = ssm + p.sring_bytes / 8;
+        for (int tg = 0; tg < NTG; ++tg) acc[mt][tg][0] = acc[mt][tg][1] = 0.f;
+      const int sl = b & 1;
+      if (ok_wait) ok_wait = mbar_wait(&sfull[sl], (b >> 1) & 1);
+      const uintptr_t s_src = reinterpret_cast<uintptr_t>(p.S + (size_t)r0 * p.G);
+      const int s_pre = (int)(s_src & 15) >> 2;
+      const int s_cnt = (int)(((s_src & 15) + (uint32_t)rows * p.G * 4) & ~15u) >> 2;
+      const float* ssm = reinterpret_cast<const float*>(sring + (size_t)sl * sp.sring_bytes);
+      const float* zsm = ssm + sp.sring_bytes / 8;
 
-    for (int kc = 0; kc < nkc; ++kc, ++c) {
-      const int st = c % p.nst, use = c / p.nst;
-      const int k0 = kc * p.KC;
-      const int gc0 = k0 / p.gs;
-      const int gcn = min(p.KC, p.K - k0) / p.gs;
-      const int ga = gc0 + min(gcn, ks * p.GPS);
-      const int gb = gc0 + min(gcn, (ks + 1) * p.GPS);
-      if (ok_wait) ok_wait = mbar_wait(&full[st], use & 1);
-      if (threadIdx.x == 0 && c < 8) GT(3 + c);
-      const uint8_t* buf = stages + (size_t)st * p.stage_bytes;
+      for (int kc = 0; kc < nkc; ++kc, ++c) {
+        const int st = c % sp.nst, use = c / sp.nst;
+        const int k0 = kc * p.KC;
+        const int gc0 = k0 / p.gs;
+        const int gcn = min(p.KC, p.K - k0) / p.gs;
+        const int ga = active ? gc0 + min(gcn, ks * p.GPS) : 0;
+        const int gb = active ? gc0 + min(gcn, (ks + 1) * p.GPS) : 0;
+        if (ok_wait) ok_wait = mbar_wait(&full[st], use & 1);
+        const uint8_t* buf = stages + (size_t)st * sp.stage_bytes;
 
-      for (int gi = ga; gi < gb && ok_wait; ++gi) {
-        float sc[kMT][2], zp[kMT][2];
+        for (int gi = ga; gi < gb && ok_wait; ++gi) {
+          float sc[kMT][2], zp[kMT][2];
 #pragma unroll
-        for (int mt = 0; mt < kMT; ++mt)
+          for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int lr = (rgp * kMT + mt) * 16 + g + 8 * h;
-            const int si = s_pre + lr * p.G + gi;
-            if (lr >= rows) {
-              sc[mt][h] = 0.f;
-              zp[mt][h] = 8.f;
-            } else if (si < s_cnt) {
-              sc[mt][h] = ssm[si];
-              zp[mt][h] = ASYM ? zsm[si] : 8.f;
-            } else {  // the last few values of the block were not bulk-copied
-              const size_t gix = (size_t)(r0 + lr) * p.G + gi;
-              sc[mt][h] = __ldg(p.S + gix);
-              zp[mt][h] = ASYM ? __ldg(p.Z + gix) : 8.f;
+            for (int h = 0; h < 2; ++h) {
+              const int lr = (rgp * kMT + mt) * 16 + g + 8 * h;
+              const int si = s_pre + lr * p.G + gi;
+              if (lr >= rows) {
+                sc[mt][h] = 0.f;
+                zp[mt][h] = 8.f;
+              } else if (si < s_cnt) {
+                sc[mt][h] = ssm[si];
+                zp[mt][h] = ASYM ? zsm[si] : 8.f;
+              } else {  // the last few values of the block were not bulk-copied
+                const size_t gix = (size_t)(r0 + lr) * p.G + gi;
+                sc[mt][h] = __ldg(p.S + gix);
+                zp[mt][h] = ASYM ? __ldg(p.Z + gix) : 8.f;
+              }
             }
-          }
-        if (c == 0 && gi == ga) CT(3, sc[0][0] + sc[1][1]);
-        int C[kMT][NT][4];
+          int C[kMT][NT][4];
 #pragma unroll
-        for (int mt = 0; mt < kMT; ++mt)
+          for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) C[mt][nt][0] = C[mt][nt][1] = C[mt][nt][2] = C[mt][nt][3] = 0;
+            for (int nt = 0; nt < NT; ++nt) C[mt][nt][0] = C[mt][nt][1] = C[mt][nt][2] = C[mt][nt][3] = 0;
 
-        for (int kseg = gi * p.gs; kseg < (gi + 1) * p.gs; kseg += SEGK) {
-          uint32_t bq[NT][2 * WPL];
+          for (int kseg = gi * p.gs; kseg < (gi + 1) * p.gs; kseg += SEGK) {
+            uint32_t bq[NT][2 * WPL];
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            if (bcol[nt]) lds_digits<LB>(bcol[nt] + kseg, bq[nt]);
-            else {
+            for (int nt = 0; nt < NT; ++nt) {
+              if (bcol[nt]) lds_digits<LB>(bcol[nt] + kseg, bq[nt]);
+              else {
 #pragma unroll
-              for (int i = 0; i < 2 * WPL; ++i) bq[nt][i] = 0u;
+                for (int i = 0; i < 2 * WPL; ++i) bq[nt][i] = 0u;
+              }
             }
-          }
-          const int boff = ((kseg - k0) >> 1) + t * LB;
-          uint32_t w0[kMT][WPL], w1[kMT][WPL];
-#pragma unroll
-          for (int mt = 0; mt < kMT; ++mt) {
-            const int lr = (rgp * kMT + mt) * 16 + g;
-            if ((rgp * kMT + mt) * 16 < rows) {
-              lds_words<LB>(buf + (size_t)lr * p.RS + boff, w0[mt]);
-              lds_words<LB>(buf + (size_t)(lr + 8) * p.RS + boff, w1[mt]);
-            } else {
-#pragma unroll
-              for (int q = 0; q < WPL; ++q) w0[mt][q] = w1[mt][q] = 0u;
-            }
-          }
-#pragma unroll
-          for (int q = 0; q < WPL; ++q)
+            const int boff = ((kseg - k0) >> 1) + t * LB;
+            uint32_t w0[kMT][WPL], w1[kMT][WPL];
 #pragma unroll
             for (int mt = 0; mt < kMT; ++mt) {
-              const uint32_t a0 = nib_lo<ASYM>(w0[mt][q]), a2 = nib_hi<ASYM>(w0[mt][q]);
-              const uint32_t a1 = nib_lo<ASYM>(w1[mt][q]), a3 = nib_hi<ASYM>(w1[mt][q]);
+              const int lr = (rgp * kMT + mt) * 16 + g;
+              if ((rgp * kMT + mt) * 16 < rows) {
+                lds_words<LB>(buf + (size_t)lr * p.RS + boff, w0[mt]);
+                lds_words<LB>(buf + (size_t)(lr + 8) * p.RS + boff, w1[mt]);
+              } else {
 #pragma unroll
-              for (int nt = 0; nt < NT; ++nt)
-                imma(C[mt][nt], a0, a1, a2, a3, bq[nt][2 * q], bq[nt][2 * q + 1]);
+                for (int q = 0; q < WPL; ++q) w0[mt][q] = w1[mt][q] = 0u;
+              }
             }
+#pragma unroll
+            for (int q = 0; q < WPL; ++q)
+#pragma unroll
+              for (int mt = 0; mt < kMT; ++mt) {
+                const uint32_t a0 = nib_lo<ASYM>(w0[mt][q]), a2 = nib_hi<ASYM>(w0[mt][q]);
+                const uint32_t a1 = nib_lo<ASYM>(w1[mt][q]), a3 = nib_hi<ASYM>(w1[mt][q]);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                  imma(C[mt][nt], a0, a1, a2, a3, bq[nt][2 * q], bq[nt][2 * q + 1]);
+              }
+          }
+          // epilogue of group gi: recombine digits, remove zeff * sum(x), scale
+#pragma unroll
+          for (int tg = 0; tg < NTG; ++tg) {
+            const int tok = tg * 4 + t;
+            if (tok < T) {
+              const float gsc = xgsc[tok * p.G + gi];
+              const float xs = xsum[tok * p.G + gi];
+#pragma unroll
+              for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const int i01 = C[mt][2 * tg][2 * h] + 256 * C[mt][2 * tg][2 * h + 1];
+                  float f = fmaf(65536.f, (float)C[mt][2 * tg + 1][2 * h], (float)i01);
+                  f = fmaf(-zp[mt][h], xs, f);
+                  acc[mt][tg][h] = fmaf(f, sc[mt][h] * gsc, acc[mt][tg][h]);
+                }
+            }
+          }
         }
-        if (c == 0 && gi == ga) CT(4, (float)(C[0][0][0] + C[1][NT - 1][3]));
-        if (c == 0 && gi == ga + 1) CT(6, (float)(C[0][0][0] + C[1][NT - 1][3]));
-        // epilogue of group gi: recombine digits, remove zeff * sum(x), scale
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+      }
+
+      // (3) reduce the K-slices of this row block and write y
+      float* rbuf = red + (b & 1) * sp.red_half;
+      if (active) {
 #pragma unroll
         for (int tg = 0; tg < NTG; ++tg) {
           const int tok = tg * 4 + t;
           if (tok < T) {
-            const float gsc = xgsc[tok * p.G + gi];
-            const float xs = xsum[tok * p.G + gi];
 #pragma unroll
             for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int i01 = C[mt][2 * tg][2 * h] + 256 * C[mt][2 * tg][2 * h + 1];
-                float f = fmaf(65536.f, (float)C[mt][2 * tg + 1][2 * h], (float)i01);
-                f = fmaf(-zp[mt][h], xs, f);
-                acc[mt][tg][h] = fmaf(f, sc[mt][h] * gsc, acc[mt][tg][h]);
-              }
+              for (int h = 0; h < 2; ++h)
+                rbuf[(ks * T + tok) * p.R + (rgp * kMT + mt) * 16 + g + 8 * h] = acc[mt][tg][h];
           }
         }
-        if (c == 0 && gi == ga) CT(5, acc[0][0][0] + acc[1][0][1]);
       }
-      if (c == 0) CT(7, acc[0][0][0] + acc[1][0][1]);
+      named_barrier_sync(1, nthr);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-    }
-
-    // (3) reduce the K-slices of this row block and write y
-    float* rbuf = red + (b & 1) * (p.KS * T * p.R);
-#pragma unroll
-    for (int tg = 0; tg < NTG; ++tg) {
-      const int tok = tg * 4 + t;
-      if (tok < T) {
-#pragma unroll
-        for (int mt = 0; mt < kMT; ++mt)
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-            rbuf[(ks * T + tok) * p.R + (rgp * kMT + mt) * 16 + g + 8 * h] = acc[mt][tg][h];
+      if (lane == 0) mbar_arrive(&sempty[sl]);
+      for (int idx = threadIdx.x; idx < rows * T; idx += nthr) {
+        const int tok = idx / rows, r = idx - tok * rows;
+        float a = 0.f;
+        for (int k = 0; k < p.KS; ++k) a += rbuf[(k * T + tok) * p.R + r];
+        if (p.bias) a += __ldg(p.bias + r0 + r);
+        st_y(p.Y, (size_t)tok * p.N + r0 + r, a, p.ydt);
       }
     }
-    if (b == 0) CT(8, 0.f);
-    named_barrier_sync(1, nthr);
-    if (b == 0) CT(9, 0.f);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sempty[sl]);
-    for (int idx = threadIdx.x; idx < rows * T; idx += nthr) {
-      const int tok = idx / rows, r = idx - tok * rows;
-      float a = 0.f;
-      for (int k = 0; k < p.KS; ++k) a += rbuf[(k * T + tok) * p.R + r];
-      if (p.bias) a += __ldg(p.bias + r0 + r);
-      st_y(p.Y, (size_t)tok * p.N + r0 + r, a, p.ydt);
-    }
-    if (threadIdx.x == 0 && b < 2) GT(12 + b);
   }
   if (threadIdx.x == 0) GT(15);
 }
@@ -511,33 +548,141 @@ size_t pad_to(size_t x, size_t mod, size_t target) {
   return x + ((target + mod - r) % mod);
 }
 
+int lb_for(int gs) { return (gs % 128 == 0) ? 16 : (gs % 64 == 0 ? 8 : 4); }
+
+struct Need {
+  size_t red_half = 0, xs = 0, xb = 0, sring_half = 0;
+};
+
+// Per-task plan.  `stage` is the launch-wide stage size in bytes.
+bool plan_task(int N, int K, int T, int gs, int ncons, int grid, size_t stage, ImmaParams& q,
+               Need& need) {
+  if (N < 1 || K % 32 || gs % 32 || gs > 256 || K % gs) return false;
+  const int LB = lb_for(gs);
+  const int G = K / gs;
+  const int rows_cta = (N + grid - 1) / grid;
+  int KS = ncons < G ? ncons : G;
+  int RG = ncons / KS;
+  const int rg_need = (rows_cta + 16 * kMT - 1) / (16 * kMT);
+  if (RG > rg_need) RG = rg_need;
+  if (RG > 2) RG = 2;
+  if (RG < 1) RG = 1;
+  const int R = RG * kMT * 16;
+  int KC, contiguous;
+  size_t RS;
+  if ((size_t)R * (K / 2) <= stage) {
+    KC = K; RS = K / 2; contiguous = 1;
+  } else {
+    long long kc = (long long)(stage / R) * 2;
+    kc = (kc / gs) * gs;
+    if (kc < gs) return false;
+    for (;;) {   // padded rows must still fit the stage
+      RS = pad_to((size_t)kc / 2, 128, (size_t)4 * LB);
+      if ((size_t)R * RS <= stage || kc <= gs) break;
+      kc -= gs;
+    }
+    if ((size_t)R * RS > stage) return false;
+    KC = (int)kc; contiguous = 0;
+  }
+  const size_t csb_target = LB == 16 ? 16 : (LB == 8 ? 64 : 32);
+  const size_t CSB = pad_to((size_t)K, 128, csb_target);
+  const size_t TS = pad_to(3 * CSB, 128, LB == 4 ? 64 : 0);
+  q.N = N; q.K = K; q.G = G; q.gs = gs;
+  q.KS = KS; q.RG = RG; q.R = R; q.KC = KC; q.GPS = (KC / gs + KS - 1) / KS;
+  q.contiguous = contiguous; q.RS = (uint32_t)RS; q.CSB = (uint32_t)CSB; q.TS = (uint32_t)TS;
+  const size_t rh = (size_t)KS * T * R * 4;
+  const size_t xs = (size_t)2 * T * G * 4;
+  const size_t xb = (size_t)T * TS;
+  const size_t sh = ((size_t)R * G * 4 + 16 + 127) & ~(size_t)127;
+  if (rh > need.red_half) need.red_half = rh;
+  if (xs > need.xs) need.xs = xs;
+  if (xb > need.xb) need.xb = xb;
+  if (sh > need.sring_half) need.sring_half = sh;
+  return true;
+}
+
+// Lay out shared memory; false when it does not fit.
+bool finish_plan(const Need& need, size_t stage, long long nchunks_max, StepPlan& pl) {
+  const DeviceInfo& di = device_info();
+  StepParams& sp = pl.sp;
+  const size_t red_base = 128;
+  const size_t xs_base = (red_base + 2 * need.red_half + 15) & ~(size_t)15;
+  const size_t xb_base = (xs_base + need.xs + 127) & ~(size_t)127;
+  const size_t sring_bytes = 2 * need.sring_half;
+  const size_t sring_base = (xb_base + need.xb + 127) & ~(size_t)127;
+  const size_t stage_base = sring_base + 2 * sring_bytes;
+  const size_t budget = (size_t)env_int("SF_GEMV_SMEM_KB", 220) * 1024;
+  const size_t cap = budget < (size_t)di.smem_optin ? budget : (size_t)di.smem_optin;
+  if (stage_base + (nchunks_max > 1 ? 2 : 1) * stage > cap) return false;
+  long long S = (long long)((cap - stage_base) / stage);
+  const int want_st = env_int("SF_GEMV_STAGES", 3);
+  if (S > want_st) S = want_st;
+  if (S > kMaxStages) S = kMaxStages;
+  if (S > nchunks_max) S = nchunks_max;
+  if (S < 1) S = 1;
+  sp.nst = (int)S;
+  sp.stage_bytes = (uint32_t)stage;
+  sp.stage_base = (uint32_t)stage_base;
+  sp.red_base = (uint32_t)red_base;
+  sp.red_half = (uint32_t)(need.red_half / 4);
+  sp.xs_base = (uint32_t)xs_base;
+  sp.xb_base = (uint32_t)xb_base;
+  sp.sring_base = (uint32_t)sring_base;
+  sp.sring_bytes = (uint32_t)sring_bytes;
+  pl.smem = stage_base + (size_t)S * stage;
+  pl.threads = (sp.ncons + 1) * 32;
+  return pl.threads <= kImmaMaxThreads;
+}
+
+long long task_chunks(const ImmaParams& q, int grid) {
+  const int rows_cta = (q.N + grid - 1) / grid;
+  return (long long)((rows_cta + q.R - 1) / q.R) * ((q.K + q.KC - 1) / q.KC);
+}
+
 template <int T, bool ASYM, int LB>
-cudaError_t launch_t(const ImmaParams& p, int grid, int threads, size_t smem, cudaStream_t st,
-                     bool pdl) {
+cudaError_t launch_t(const StepPlan& pl, cudaStream_t st, bool pdl) {
   auto* fn = q4_gemv_imma_kernel<T, ASYM, LB>;
   static int configured[kMaxDevices] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < kMaxDevices && configured[dev] < (int)smem) {
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (dev >= 0 && dev < kMaxDevices && configured[dev] < (int)pl.smem) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
     if (e != cudaSuccess) return e;
-    configured[dev] = (int)smem;
+    configured[dev] = (int)pl.smem;
   }
-  return launch_kernel(fn, grid, threads, smem, st, pdl, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)pl.grid);
+  cfg.blockDim = dim3((unsigned)pl.threads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (pl.coop) {
+    attr[na].id = cudaLaunchAttributeCooperative;
+    attr[na].val.cooperative = 1;
+    ++na;
+  }
+  cfg.attrs = na ? attr : nullptr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, fn, pl.sp);
 }
 
 template <bool ASYM, int LB>
-cudaError_t launch_lb(int T, const ImmaParams& p, int grid, int threads, size_t smem,
-                      cudaStream_t st, bool pdl) {
-  switch (T) {
-    case 1: return launch_t<1, ASYM, LB>(p, grid, threads, smem, st, pdl);
-    case 2: return launch_t<2, ASYM, LB>(p, grid, threads, smem, st, pdl);
-    case 3: return launch_t<3, ASYM, LB>(p, grid, threads, smem, st, pdl);
-    case 4: return launch_t<4, ASYM, LB>(p, grid, threads, smem, st, pdl);
-    case 5: return launch_t<5, ASYM, LB>(p, grid, threads, smem, st, pdl);
-    case 6: return launch_t<6, ASYM, LB>(p, grid, threads, smem, st, pdl);
-    case 7: return launch_t<7, ASYM, LB>(p, grid, threads, smem, st, pdl);
-    default: return launch_t<8, ASYM, LB>(p, grid, threads, smem, st, pdl);
+cudaError_t launch_lb(const StepPlan& pl, cudaStream_t st, bool pdl) {
+  switch (pl.T) {
+    case 1: return launch_t<1, ASYM, LB>(pl, st, pdl);
+    case 2: return launch_t<2, ASYM, LB>(pl, st, pdl);
+    case 3: return launch_t<3, ASYM, LB>(pl, st, pdl);
+    case 4: return launch_t<4, ASYM, LB>(pl, st, pdl);
+    case 5: return launch_t<5, ASYM, LB>(pl, st, pdl);
+    case 6: return launch_t<6, ASYM, LB>(pl, st, pdl);
+    case 7: return launch_t<7, ASYM, LB>(pl, st, pdl);
+    default: return launch_t<8, ASYM, LB>(pl, st, pdl);
   }
 }
 
@@ -554,95 +699,133 @@ extern "C" int sf_q4_gemv_set_trace(unsigned long long* buf) {
 }
 #endif
 
-bool plan_gemv_imma(int N, int K, int T, int gs, bool asym, ImmaPlan& pl) {
-  if (T < 1 || T > kMaxGemvT || N < 1 || K % 32 || gs % 32 || gs > 256) return false;
+bool plan_gemv_imma(int N, int K, int T, int gs, bool asym, StepPlan& pl) {
+  if (T < 1 || T > kMaxGemvT) return false;
   const DeviceInfo& di = device_info();
-  const int LB = (gs % 128 == 0) ? 16 : (gs % 64 == 0 ? 8 : 4);
-  const int G = K / gs;
   int grid = di.sms * env_int("SF_GEMV_CTAS_PER_SM", 1);
   const int max_grid = (N + 15) / 16;                  // at least one 16-row tile per CTA
   if (grid > max_grid) grid = max_grid;
-  const int rows_cta = (N + grid - 1) / grid;
-  const int max_cons = kImmaMaxThreads / 32 - 1;
-  int RG = (rows_cta + 16 * kMT - 1) / (16 * kMT);
-  if (RG > 2) RG = 2;
-  int KS = env_int("SF_GEMV_WARPS", 16) / RG;
-  if (KS < 1) KS = 1;
-  if (KS > G) KS = G;
-  if (KS * RG > max_cons) KS = max_cons / RG;
-  const int R = RG * kMT * 16;
-  // Stage: whole rows (one contiguous region) when a row block fits, else
-  // whole groups of every row with one copy per row.
-  const size_t stage_cap = (size_t)env_int("SF_GEMV_STAGE_KB", 64) * 1024;
-  int KC, contiguous;
-  size_t RS;
-  if ((size_t)R * (K / 2) <= stage_cap) {
-    KC = K;
-    RS = K / 2;
-    contiguous = 1;
-  } else {
-    long long kc = (long long)(stage_cap / R) * 2;
-    kc = (kc / gs) * gs;
-    if (kc < gs) kc = gs;
-    if (kc > K) kc = K;
-    KC = (int)kc;
-    RS = pad_to((size_t)KC / 2, 128, (size_t)4 * LB);
-    contiguous = 0;
-  }
-  const int GC = KC / gs;
-  const int GPS = (GC + KS - 1) / KS;
-  const size_t stage = ((size_t)R * RS + 127) & ~(size_t)127;
-  const size_t csb_target = LB == 16 ? 16 : (LB == 8 ? 64 : 32);
-  const size_t CSB = pad_to((size_t)K, 128, csb_target);
-  const size_t TS = pad_to(3 * CSB, 128, LB == 4 ? 64 : 0);
-  const size_t red_base = 128;
-  const size_t red_bytes = (size_t)2 * KS * T * R * 4;
-  const size_t xs_base = (red_base + red_bytes + 15) & ~(size_t)15;
-  const size_t xb_base = (xs_base + (size_t)2 * T * G * 4 + 127) & ~(size_t)127;
-  const size_t sring_half = ((size_t)R * G * 4 + 16 + 127) & ~(size_t)127;
-  const size_t sring_bytes = 2 * sring_half;
-  const size_t sring_base = (xb_base + (size_t)T * TS + 127) & ~(size_t)127;
-  const size_t stage_base = sring_base + 2 * sring_bytes;
-  const size_t budget = (size_t)env_int("SF_GEMV_SMEM_KB", 220) * 1024;
-  const size_t cap = budget < (size_t)di.smem_optin ? budget : (size_t)di.smem_optin;
-  const int nrb = (rows_cta + R - 1) / R;
-  const int nkc = (K + KC - 1) / KC;
-  const long long nchunks = (long long)nrb * nkc;
-  if (stage_base + (nchunks > 1 ? 2 : 1) * stage > cap) return false;
-  long long S = (long long)((cap - stage_base) / stage);
-  const int want_st = env_int("SF_GEMV_STAGES", 3);
-  if (S > want_st) S = want_st;
-  if (S > kMaxStages) S = kMaxStages;
-  if (S > nchunks) S = nchunks;
-  if (S < 1) S = 1;
-  pl.LB = LB;
-  pl.grid = grid;
-  pl.threads = (KS * RG + 1) * 32;
-  pl.smem = stage_base + (size_t)S * stage;
-  ImmaParams& q = pl.p;
-  q.N = N; q.K = K; q.G = G; q.gs = gs;
-  q.KS = KS; q.RG = RG; q.R = R; q.KC = KC; q.nst = (int)S; q.GPS = GPS; q.contiguous = contiguous;
-  q.RS = (uint32_t)RS; q.stage_bytes = (uint32_t)stage; q.stage_base = (uint32_t)stage_base;
-  q.xb_base = (uint32_t)xb_base; q.CSB = (uint32_t)CSB; q.TS = (uint32_t)TS;
-  q.xs_base = (uint32_t)xs_base; q.red_base = (uint32_t)red_base;
-  q.sring_base = (uint32_t)sring_base; q.sring_bytes = (uint32_t)sring_bytes;
-  q.trace_id = 0;
-  return pl.threads <= kImmaMaxThreads;
+  if (grid < 1) grid = 1;
+  pl = StepPlan{};
+  pl.T = T; pl.asym = asym; pl.LB = lb_for(gs); pl.grid = grid; pl.coop = false;
+  StepParams& sp = pl.sp;
+  sp.ncons = env_int("SF_GEMV_WARPS", 16);
+  if (sp.ncons > kImmaMaxThreads / 32 - 1) sp.ncons = kImmaMaxThreads / 32 - 1;
+  sp.ntasks = 1; sp.tasks = nullptr; sp.bar = nullptr;
+  const size_t stage = (size_t)env_int("SF_GEMV_STAGE_KB", 64) * 1024;
+  Need need;
+  if (!plan_task(N, K, T, gs, sp.ncons, grid, stage, sp.single, need)) return false;
+  sp.single.wait_before = 0;
+  return finish_plan(need, stage, task_chunks(sp.single, grid), pl);
 }
 
-cudaError_t launch_gemv_imma(int T, bool asym, const ImmaPlan& pl0, cudaStream_t st, bool pdl) {
-  ImmaPlan pl = pl0;
+cudaError_t launch_gemv_imma(const StepPlan& pl0, cudaStream_t st, bool pdl) {
+  StepPlan pl = pl0;
 #ifdef SF_GEMV_TRACE
-  pl.p.trace_id = g_trace_counter++;
+  pl.sp.trace_id = g_trace_counter++;
 #endif
-  if (asym) {
-    if (pl.LB == 16) return launch_lb<true, 16>(T, pl.p, pl.grid, pl.threads, pl.smem, st, pdl);
-    if (pl.LB == 8) return launch_lb<true, 8>(T, pl.p, pl.grid, pl.threads, pl.smem, st, pdl);
-    return launch_lb<true, 4>(T, pl.p, pl.grid, pl.threads, pl.smem, st, pdl);
+  if (pl.asym) {
+    if (pl.LB == 16) return launch_lb<true, 16>(pl, st, pdl);
+    if (pl.LB == 8) return launch_lb<true, 8>(pl, st, pdl);
+    return launch_lb<true, 4>(pl, st, pdl);
   }
-  if (pl.LB == 16) return launch_lb<false, 16>(T, pl.p, pl.grid, pl.threads, pl.smem, st, pdl);
-  if (pl.LB == 8) return launch_lb<false, 8>(T, pl.p, pl.grid, pl.threads, pl.smem, st, pdl);
-  return launch_lb<false, 4>(T, pl.p, pl.grid, pl.threads, pl.smem, st, pdl);
+  if (pl.LB == 16) return launch_lb<false, 16>(pl, st, pdl);
+  if (pl.LB == 8) return launch_lb<false, 8>(pl, st, pdl);
+  return launch_lb<false, 4>(pl, st, pdl);
 }
 
 }  // namespace sf
+
+// ===========================================================================
+// C ABI: a prepared list of GEMVs run as one persistent launch.
+// ===========================================================================
+using namespace sf;
+
+namespace {
+constexpr size_t kStepHeader = 256;   // grid-barrier counter lives here
+struct StepHandle {
+  StepPlan plan;
+  void* workspace;
+  int device;
+};
+}  // namespace
+
+extern "C" {
+
+size_t sf_q4_step_workspace_bytes(int ntasks) {
+  return kStepHeader + (size_t)(ntasks > 0 ? ntasks : 0) * sizeof(ImmaParams);
+}
+
+int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size_t workspace_bytes,
+                      void** handle_out) {
+  if (!tasks || !workspace || !handle_out) return fail(SF_ERR_NULL, "null pointer argument");
+  if (ntasks < 1) return fail(SF_ERR_SHAPE, "ntasks must be >= 1");
+  if (workspace_bytes < sf_q4_step_workspace_bytes(ntasks))
+    return fail(SF_ERR_SHAPE, "workspace too small: need %zu bytes",
+                sf_q4_step_workspace_bytes(ntasks));
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return fail(SF_ERR_ALIGN, "workspace must be 256-byte aligned");
+  const int T = tasks[0].T, gs0 = tasks[0].group_size;
+  const bool asym = tasks[0].zeros != nullptr;
+  if (T < 1 || T > kMaxGemvT) return fail(SF_ERR_UNSUPPORTED, "step tasks need 1 <= T <= %d", kMaxGemvT);
+  const DeviceInfo& di = device_info();
+  StepPlan pl{};
+  pl.T = T; pl.asym = asym; pl.LB = lb_for(gs0); pl.grid = di.sms;
+  StepParams& sp = pl.sp;
+  sp.ncons = env_int("SF_GEMV_WARPS", 16);
+  if (sp.ncons > kImmaMaxThreads / 32 - 1) sp.ncons = kImmaMaxThreads / 32 - 1;
+  const size_t stage = (size_t)env_int("SF_GEMV_STAGE_KB", 64) * 1024;
+  Need need;
+  std::vector<ImmaParams> h(ntasks);
+  long long nch = 1;
+  bool any_wait = false;
+  for (int i = 0; i < ntasks; ++i) {
+    const sf_q4_task& a = tasks[i];
+    if (!a.W || !a.scales || !a.X || !a.Y) return fail(SF_ERR_NULL, "task %d: null pointer", i);
+    if (a.T != T || (a.zeros != nullptr) != asym || lb_for(a.group_size) != pl.LB)
+      return fail(SF_ERR_UNSUPPORTED, "task %d: all tasks need the same T, layout and group class", i);
+    if (a.x_dtype < 0 || a.x_dtype > 2 || a.y_dtype < 0 || a.y_dtype > 2)
+      return fail(SF_ERR_DTYPE, "task %d: unknown dtype code", i);
+    if ((reinterpret_cast<uintptr_t>(a.W) | reinterpret_cast<uintptr_t>(a.scales) |
+         reinterpret_cast<uintptr_t>(a.zeros) | reinterpret_cast<uintptr_t>(a.X)) & 15)
+      return fail(SF_ERR_ALIGN, "task %d: W, scales, zeros and X must be 16-byte aligned", i);
+    ImmaParams& q = h[i];
+    q = ImmaParams{};
+    if (!plan_task(a.N, a.K, T, a.group_size, sp.ncons, pl.grid, stage, q, need))
+      return fail(SF_ERR_UNSUPPORTED, "task %d: shape N=%d K=%d gs=%d not supported by the step kernel",
+                  i, a.N, a.K, a.group_size);
+    q.W = a.W; q.S = a.scales; q.Z = a.zeros; q.bias = a.bias; q.X = a.X; q.Y = a.Y;
+    q.xdt = a.x_dtype; q.ydt = a.y_dtype;
+    q.wait_before = i > 0 ? (a.wait_before ? 1 : 0) : 0;
+    any_wait |= q.wait_before != 0;
+    nch += task_chunks(q, pl.grid);
+  }
+  pl.coop = any_wait;
+  if (!finish_plan(need, stage, nch, pl)) return fail(SF_ERR_UNSUPPORTED, "step does not fit shared memory");
+  sp.ntasks = ntasks;
+  sp.bar = static_cast<unsigned int*>(workspace);
+  sp.tasks = reinterpret_cast<const ImmaParams*>(static_cast<uint8_t*>(workspace) + kStepHeader);
+  cudaError_t e = cudaMemcpy(const_cast<ImmaParams*>(sp.tasks), h.data(), sizeof(ImmaParams) * ntasks,
+                             cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(e, "uploading the task table");
+  StepHandle* hd = new StepHandle{pl, workspace, 0};
+  cudaGetDevice(&hd->device);
+  *handle_out = hd;
+  return SF_OK;
+}
+
+int sf_q4_step_run(void* handle, void* stream) {
+  if (!handle) return fail(SF_ERR_NULL, "null handle");
+  StepHandle* hd = static_cast<StepHandle*>(handle);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(hd->workspace, 0, kStepHeader, st);
+  if (e != cudaSuccess) return cuda_fail(e, "clearing the barrier counter");
+  e = launch_gemv_imma(hd->plan, st, false);
+  if (e != cudaSuccess) return cuda_fail(e, "q4 step launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return SF_OK;
+}
+
+void sf_q4_step_destroy(void* handle) { delete static_cast<StepHandle*>(handle); }
+
+}  // extern "C"

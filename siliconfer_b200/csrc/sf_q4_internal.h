@@ -34,7 +34,7 @@ struct GemvParams {
   uint32_t stage_bytes, s_off, z_off, stage_base;
 };
 
-// Decode GEMV on the tensor cores (sf_q4_gemv.cu).
+// Decode GEMV on the tensor cores (sf_q4_gemv.cu).  One task = one GEMV.
 struct ImmaParams {
   const uint8_t* W;
   const float* S;
@@ -43,21 +43,33 @@ struct ImmaParams {
   const void* X;
   void* Y;
   int N, K, G, gs, xdt, ydt;
-  int KS, RG, R, KC, nst, GPS;   // K-slices, row groups, rows per block, k per chunk, stages, groups per slice
-  int contiguous;                // 1: a stage holds whole rows (one contiguous region)
-  uint32_t RS, stage_bytes, stage_base, xb_base, CSB, TS, xs_base, red_base;
-  uint32_t sring_base, sring_bytes;  // scale/zero ring: 2 slots, zeros in the upper half
-  int trace_id;                  // launch index for the optional timeline trace
+  int KS, RG, R, KC, GPS;   // K-slices, row groups, rows per block, k per chunk, groups per slice
+  int contiguous;           // 1: a stage holds whole rows (one contiguous region)
+  int wait_before;          // grid barrier before reading X (X depends on earlier tasks)
+  uint32_t RS, CSB, TS;     // stage row stride, digit column stride, token stride
 };
 
-struct ImmaPlan {
-  ImmaParams p;
-  int LB, grid, threads;
+// Launch-wide parameters: shared-memory layout sized for the largest task.
+struct StepParams {
+  const ImmaParams* tasks;  // device array, or nullptr: use `single`
+  ImmaParams single;
+  int ntasks, ncons, nst;
+  unsigned int* bar;        // grid-barrier counter (zeroed before every launch)
+  uint32_t stage_bytes, stage_base, red_base, red_half, xs_base, xb_base;
+  uint32_t sring_base, sring_bytes;
+  int trace_id;
+};
+
+struct StepPlan {
+  StepParams sp;
+  int T, LB, grid, threads;
+  bool asym, coop;
   size_t smem;
 };
 
-bool plan_gemv_imma(int N, int K, int T, int gs, bool asym, ImmaPlan& pl);
-cudaError_t launch_gemv_imma(int T, bool asym, const ImmaPlan& pl, cudaStream_t st, bool pdl);
+// Plans one GEMV as a 1-task launch; false when the shape needs another kernel.
+bool plan_gemv_imma(int N, int K, int T, int gs, bool asym, StepPlan& pl);
+cudaError_t launch_gemv_imma(const StepPlan& pl, cudaStream_t st, bool pdl);
 
 int fail(int code, const char* fmt, ...);
 int cuda_fail(cudaError_t e, const char* what);

@@ -1,16 +1,21 @@
-"""Q4StepRunner: a decode step's Q4Linear calls captured once as a CUDA graph.
+"""Q4StepRunner: a decode step's Q4Linear calls as one persistent launch.
 
 A decode step calls every projection of every layer once (7 per layer,
 siliconfer/model/layers.py:93-95, 133, 144).  The reference pays a device
-sync and two host copies per call (siliconfer/model/q4_linear.py:51-63); here
-the whole sequence is one graph replay whose launches are chained with
-programmatic dependent launch, so each GEMV starts streaming its weights while
-the previous one finishes.  Inputs and outputs live in two device arenas;
-``run_host`` moves a whole step's activations in with one host->device copy
-from pinned memory and the results out with one device->host copy.
+sync and two host copies per call (siliconfer/model/q4_linear.py:51-63).
+Here the whole sequence is ONE cooperative kernel launch (sf_q4_step_run,
+captured in a CUDA graph): it streams every projection's weights back to back
+and waits at a grid barrier only where the decoder has a data dependency --
+before o_proj (it consumes attention over q/k/v), before gate/up (they
+consume the residual stream after o_proj), before down_proj (SwiGLU of
+gate/up) and before the next layer's q/k/v.  q/k/v share their input, as do
+gate/up, so they run without a barrier between them.
 
-The runner treats every call as reading its own input slot: the data flow
-between projections (attention, SwiGLU) is outside this path.
+Inputs and outputs live in two device arenas; ``run_host`` moves a whole
+step's activations in with one host->device copy from pinned memory and the
+results out with one device->host copy.  Every call still reads its own input
+slot: the ops between projections (attention, norms, SwiGLU) are outside
+this path, only their ordering is kept.
 """
 from __future__ import annotations
 
@@ -33,8 +38,12 @@ class _Call:
 
 
 class Q4StepRunner:
+    # projection order inside a layer and whether each waits for the previous ones
+    LAYER_WAITS = (True, False, False, True, True, False, True)   # q k v o gate up down
+
     def __init__(self, layers, tokens: int = 1, x_dtype=torch.float16,
-                 y_dtype=torch.float32, pdl: bool = True, device=None):
+                 y_dtype=torch.float32, pdl: bool = True, device=None, waits=None,
+                 persistent: bool = True):
         self.layers = list(layers)
         if not self.layers:
             raise ValueError("no layers")
@@ -55,6 +64,52 @@ class Q4StepRunner:
         self.y_host = torch.zeros(yo, dtype=y_dtype, pin_memory=True)
         self.graph = None
         self.stream = torch.cuda.Stream(self.device)
+        if waits is None:
+            waits = [self.LAYER_WAITS[i % 7] if len(self.layers) % 7 == 0 else True
+                     for i in range(len(self.layers))]
+        self.waits = list(waits)
+        self.persistent = persistent
+        self._handle = None
+        self._workspace = None
+        if persistent:
+            self._create_step()
+
+    def _create_step(self):
+        lib = _lib.load()
+        n = len(self.calls)
+        arr = (_lib.Q4Task * n)()
+        xs, ys = _ESIZE[self.x_dtype], _ESIZE[self.y_dtype]
+        xc, yc = K._dtype_code(self.x), K._dtype_code(self.y)
+        for i, c in enumerate(self.calls):
+            m = c.layer
+            arr[i] = _lib.Q4Task(
+                m.packed_d.data_ptr(), m.scales_d.data_ptr(),
+                None if m.zeros_d is None else m.zeros_d.data_ptr(),
+                None if m.bias_d is None else m.bias_d.data_ptr(),
+                self.x.data_ptr() + c.x_off * xs, self.y.data_ptr() + c.y_off * ys,
+                m.out_features, m.in_features, self.tokens, m.group_size, xc, yc,
+                1 if self.waits[i] else 0)
+        nbytes = int(lib.sf_q4_step_workspace_bytes(n))
+        self._workspace = torch.zeros(nbytes + 256, dtype=torch.uint8, device=self.device)
+        base = self._workspace.data_ptr()
+        aligned = (base + 255) & ~255
+        h = _lib.ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            rc = lib.sf_q4_step_create(arr, n, aligned, nbytes, _lib.ctypes.byref(h))
+        if rc != 0:
+            # shapes the persistent kernel does not take fall back to one launch per call
+            self.persistent = False
+            self._workspace = None
+            return
+        self._handle = h
+
+    def __del__(self):
+        if getattr(self, "_handle", None) is not None:
+            try:
+                _lib.load().sf_q4_step_destroy(self._handle)
+            except Exception:
+                pass
+            self._handle = None
 
     # -- views -------------------------------------------------------------
     def x_slot(self, i: int, host: bool = False):
@@ -71,7 +126,7 @@ class Q4StepRunner:
 
     @property
     def kernels_per_step(self) -> int:
-        return len(self.calls)
+        return 1 if self.persistent else len(self.calls)
 
     def algorithmic_bytes(self) -> int:
         """Bytes one step must move: packed weights, fp32 scales (and zeros),
@@ -92,6 +147,9 @@ class Q4StepRunner:
     # -- launches ------------------------------------------------------------
     def _launch_all(self, stream) -> None:
         lib = _lib.load()
+        if self.persistent:
+            _lib.check(lib.sf_q4_step_run(self._handle, stream.cuda_stream))
+            return
         xs = _ESIZE[self.x_dtype]
         ys = _ESIZE[self.y_dtype]
         xc, yc = K._dtype_code(self.x), K._dtype_code(self.y)
