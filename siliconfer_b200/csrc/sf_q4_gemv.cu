@@ -35,6 +35,7 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
+#include <cstddef>
 #include <cstdint>
 #include <cstdlib>
 #include <vector>
@@ -52,8 +53,16 @@ SF_DEFINE_ERROR_READER(take_dev_error_gemv_tc)
 namespace {
 
 constexpr int kMT = 2;                 // m16 tiles per warp per row block
-constexpr int kImmaMaxThreads = 544;   // up to 16 consumer warps + 1 producer warp
+constexpr int kImmaMaxThreads = 512;   // up to 15 consumer warps + 1 producer warp (128 regs)
 constexpr uint32_t kPiece = 4096;      // contiguous bulk-copy piece (bytes)
+constexpr int kSS = 4;                 // scale-ring slots (row blocks of scales in flight)
+// shared-memory header: [0,192) mbarriers, [192,256) zero block, then two task slots
+constexpr int kZeroOff = 192;
+constexpr int kTaskOff = 256;
+constexpr int kTaskBytes = (int)sizeof(ImmaParams);
+static_assert(sizeof(ImmaParams) % 16 == 0 && alignof(ImmaParams) == 16,
+              "descriptors are copied as uint4");
+static_assert(offsetof(StepParams, single) % 16 == 0, "embedded descriptor must be 16-byte aligned");
 
 __device__ __forceinline__ void ld_x8(const void* x, size_t idx, int dt, float* v) {
   if (dt == SF_F32) {
@@ -143,6 +152,52 @@ __device__ __forceinline__ void lds_digits(const uint8_t* p, uint32_t* b) {
   }
 }
 
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float ldsf(uint32_t a) { return __uint_as_float(lds32(a)); }
+
+// LB packed bytes of one A row at shared address a.
+template <int LB>
+__device__ __forceinline__ void lds_words_s(uint32_t a, uint32_t* w) {
+  if constexpr (LB == 16) {
+    const uint4 v = lds128(a);
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else if constexpr (LB == 8) {
+    const uint2 v = lds64(a);
+    w[0] = v.x; w[1] = v.y;
+  } else {
+    w[0] = lds32(a);
+  }
+}
+
+// 2*LB digit bytes of one B column at shared address a.
+template <int LB>
+__device__ __forceinline__ void lds_digits_s(uint32_t a, uint32_t* b) {
+  if constexpr (LB == 16) {
+    const uint4 u = lds128(a), v = lds128(a + 16);
+    b[0] = u.x; b[1] = u.y; b[2] = u.z; b[3] = u.w; b[4] = v.x; b[5] = v.y; b[6] = v.z; b[7] = v.w;
+  } else if constexpr (LB == 8) {
+    const uint4 u = lds128(a);
+    b[0] = u.x; b[1] = u.y; b[2] = u.z; b[3] = u.w;
+  } else {
+    const uint2 u = lds64(a);
+    b[0] = u.x; b[1] = u.y;
+  }
+}
+
 }  // namespace
 
 // Optional timeline (build with -DSF_GEMV_TRACE): per CTA 16 slots of
@@ -154,8 +209,15 @@ __device__ unsigned long long* g_gtrace = nullptr;
     if (g_gtrace)                                                                        \
       g_gtrace[((size_t)sp.trace_id * gridDim.x + blockIdx.x) * 16 + (slot)] = globaltimer_ns(); \
   } while (0)
+// per-task stamps: slot = task * 4 + k, 1024 slots per CTA
+#define GTT(ti, k)                                                                       \
+  do {                                                                                   \
+    if (g_gtrace && (ti) < 128)                                                          \
+      g_gtrace[(size_t)blockIdx.x * 1024 + (ti) * 8 + (k)] = globaltimer_ns();           \
+  } while (0)
 #else
 #define GT(slot) do { } while (0)
+#define GTT(ti, k) do { } while (0)
 #endif
 
 // ---------------------------------------------------------------------------
@@ -206,23 +268,28 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
   uint64_t* sfull = empty + kMaxStages;
-  uint64_t* sempty = sfull + 2;
+  uint64_t* sempty = sfull + kSS;
   float* red = reinterpret_cast<float*>(smem + sp.red_base);
   float* xgsc = reinterpret_cast<float*>(smem + sp.xs_base);
   uint8_t* xb = smem + sp.xb_base;
   uint8_t* sring = smem + sp.sring_base;
   uint8_t* stages = smem + sp.stage_base;
+  const uint8_t* zblk = smem + kZeroOff;   // 64 zero bytes (B operand of unused columns)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int ncons = sp.ncons;
 
   if (threadIdx.x == 0) {
-    GT(0);
     for (int i = 0; i < sp.nst; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], ncons); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&sfull[i], 1); mbar_init(&sempty[i], ncons); }
+    for (int i = 0; i < kSS; ++i) { mbar_init(&sfull[i], 1); mbar_init(&sempty[i], ncons); }
     fence_mbar_init();
   }
+  if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(smem + kZeroOff)[threadIdx.x] = 0u;
+  // task slot 0 <- task 0 (consumers read task descriptors from shared memory)
+  if (threadIdx.x < kTaskBytes / 16)
+    reinterpret_cast<uint4*>(smem + kTaskOff)[threadIdx.x] =
+        reinterpret_cast<const uint4*>(&task_at(sp, 0))[threadIdx.x];
   __syncthreads();
   griddep_launch_dependents();
 
@@ -231,18 +298,19 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
     int c = 0, b = 0;
     for (int ti = 0; ti < sp.ntasks; ++ti) {
       const ImmaParams& p = task_at(sp, ti);
-      const int rb = (int)((long long)p.N * blockIdx.x / gridDim.x);
-      const int re = (int)((long long)p.N * (blockIdx.x + 1) / gridDim.x);
+      const int rb = (int)((unsigned)p.N * blockIdx.x / gridDim.x);
+      const int re = (int)((unsigned)p.N * (blockIdx.x + 1) / gridDim.x);
       const int nrb = (re - rb + p.R - 1) / p.R;
       const int nkc = (p.K + p.KC - 1) / p.KC;
       const int KH = p.K >> 1;
       for (int bb = 0; bb < nrb; ++bb, ++b) {
         const int r0 = rb + bb * p.R;
         const int rows = min(p.R, re - r0);
-        const int sl = b & 1;
+        const int sl = b % kSS;
         int ok = 1;
-        if (lane == 0 && b >= 2) ok = mbar_wait(&sempty[sl], ((b >> 1) - 1) & 1);
+        if (lane == 0 && b >= kSS) ok = mbar_wait(&sempty[sl], ((b / kSS) - 1) & 1);
         if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+        if (lane == 0 && bb == 0) GTT(ti, 4);
         if (lane == 0) {  // scales (+ zeros) of the row block, from the 16-byte boundary below
           const uintptr_t src = reinterpret_cast<uintptr_t>(p.S + (size_t)r0 * p.G);
           const uint32_t pre = (uint32_t)(src & 15);
@@ -265,6 +333,11 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
           const int k0 = kc * p.KC;
           const uint32_t cb = (uint32_t)(min(p.KC, p.K - k0) >> 1);
           uint8_t* buf = stages + (size_t)st * sp.stage_bytes;
+          if (lane == 0 && bb == 0 && kc == 0) GTT(ti, 5);
+          if (sp.dbg & 1) {   // development: stage completes without data
+            if (lane == 0) mbar_arrive_expect_tx(&full[st], 0);
+            continue;
+          }
           if (lane == 0) mbar_arrive_expect_tx(&full[st], cb * rows);
           __syncwarp();
           const uint8_t* src = p.W + (size_t)r0 * KH + (k0 >> 1);
@@ -289,135 +362,179 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
   // ------------------------------ consumers -------------------------------
   const int nthr = ncons * 32;
   griddep_wait();
-  if (threadIdx.x == 0) GT(1);
   int c = 0, b = 0;
   unsigned int nbar = 0;
   bool ok_wait = true;
 
   for (int ti = 0; ti < sp.ntasks; ++ti) {
-    const ImmaParams& p = task_at(sp, ti);
+    named_barrier_sync(1, nthr);   // task slot ti & 1 is complete and visible
+    const ImmaParams& p = *reinterpret_cast<const ImmaParams*>(smem + kTaskOff + (ti & 1) * kTaskBytes);
+    // prefetch the next descriptor now; it is stored into the other slot at the end of this task
+    uint4 tnext = make_uint4(0, 0, 0, 0);
+    const bool tpre = ti + 1 < sp.ntasks && threadIdx.x < kTaskBytes / 16;
+    if (tpre) tnext = __ldg(reinterpret_cast<const uint4*>(&task_at(sp, ti + 1)) + threadIdx.x);
     if (ti > 0 && p.wait_before && ok_wait)
       ok_wait = grid_barrier(sp.bar, (++nbar) * gridDim.x, nthr);
     float* xsum = xgsc + T * p.G;
+    if (threadIdx.x == 0) GTT(ti, 0);
 
     // (1) activations -> per-(token, group) fixed point, three int8 digits.
-    //     All of a thread's loads are issued before any of them is used; the
-    //     loads go through L2 (an earlier task of this launch may have written x).
-    {
-      const int octs_tok = p.K >> 3;
-      const int total = T * octs_tok;
-      const int lpg = p.gs >> 3;  // octets (lanes) per group: 4, 8, 16 or 32
+    //     Token-major; all of a thread's loads for a pass are issued before
+    //     any is used; loads go through L2 (an earlier task may have written x).
+    const int lg2gs = p.lg2gs, G = p.G;
+    if (!(sp.dbg & 2)) {
+      const int octs = p.K >> 3;
+      const int lpg = 1 << (lg2gs - 3);  // octets (lanes) per group: 4, 8, 16 or 32
+      const void* X = p.X;
+      const int xdt = p.xdt, Kx = p.K;
+      const uint32_t TSx = p.TS, CSBx = p.CSB;
       constexpr int NB = 4;
-      for (int base = warp * 32; base < total; base += nthr * NB) {
-        float v[NB][8];
+      for (int tok = 0; tok < T; ++tok) {
+        for (int base = warp * 32; base < octs; base += nthr * NB) {
+          float v[NB][8];
 #pragma unroll
-        for (int i = 0; i < NB; ++i) {
-          const int o = base + i * nthr + lane;
-          if (o < total) {
-            const int tok = o / octs_tok;
-            ld_x8(p.X, (size_t)tok * p.K + (size_t)(o - tok * octs_tok) * 8, p.xdt, v[i]);
-          } else {
+          for (int i = 0; i < NB; ++i) {
+            const int o = base + i * nthr + lane;
+            if (o < octs) ld_x8(X, (size_t)tok * Kx + (size_t)o * 8, xdt, v[i]);
+            else {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+              for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+            }
           }
-        }
 #pragma unroll
-        for (int i = 0; i < NB; ++i) {
-          const int ob = base + i * nthr;
-          if (ob >= total) break;                       // uniform across the warp
-          const int o = ob + lane;
-          const bool ok = o < total;
-          float m = 0.f;
-          bool bad = false;
+          for (int i = 0; i < NB; ++i) {
+            const int ob = base + i * nthr;
+            if (ob >= octs) break;                         // uniform across the warp
+            const int o = ob + lane;
+            float m = 0.f;
+            bool bad = false;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            m = fmaxf(m, fabsf(v[i][j]));
-            bad |= !(fabsf(v[i][j]) <= 3.402823466e38f);
-          }
-          int badi = bad;
-          for (int off = 1; off < lpg; off <<= 1) {
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-            badi |= __shfl_xor_sync(0xffffffffu, badi, off);
-          }
-          // binary exponent field of the group max; groups below 2^-105 are zero
-          const int be = (int)(__float_as_uint(m) >> 23);
-          const bool zero = badi || be < 22;
-          const float scl = zero ? 0.f : __uint_as_float((uint32_t)(275 - be) << 23);   // 2^(22-E)
-          int d[3][8];
-          int s = 0;
+            for (int j = 0; j < 8; ++j) {
+              m = fmaxf(m, fabsf(v[i][j]));
+              bad |= !(fabsf(v[i][j]) <= 3.402823466e38f);
+            }
+            int badi = bad;
+            for (int off = 1; off < lpg; off <<= 1) {
+              m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+              badi |= __shfl_xor_sync(0xffffffffu, badi, off);
+            }
+            // binary exponent field of the group max; groups below 2^-105 are zero
+            const int be = (int)(__float_as_uint(m) >> 23);
+            const bool zero = badi || be < 22;
+            const float scl = zero ? 0.f : __uint_as_float((uint32_t)(275 - be) << 23);   // 2^(22-E)
+            int d[3][8];
+            int s = 0;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int xf = __float2int_rn(v[i][j] * scl);
-            s += xf;
-            const int d0 = (xf << 24) >> 24;
-            const int r1 = (xf - d0) >> 8;
-            const int d1 = (r1 << 24) >> 24;
-            d[0][j] = d0;
-            d[1][j] = d1;
-            d[2][j] = (r1 - d1) >> 8;
-          }
-          for (int off = 1; off < lpg; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-          if (ok) {
-            const int tok = o / octs_tok;
-            const int ko = (o - tok * octs_tok) * 8;
-            uint8_t* col = xb + (size_t)tok * p.TS + ko;
+            for (int j = 0; j < 8; ++j) {
+              const int xf = __float2int_rn(v[i][j] * scl);
+              s += xf;
+              const int d0 = (xf << 24) >> 24;
+              const int r1 = (xf - d0) >> 8;
+              const int d1 = (r1 << 24) >> 24;
+              d[0][j] = d0;
+              d[1][j] = d1;
+              d[2][j] = (r1 - d1) >> 8;
+            }
+            for (int off = 1; off < lpg; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+            if (o < octs) {
+              uint8_t* col = xb + (size_t)tok * TSx + (size_t)o * 8;
 #pragma unroll
-            for (int dg = 0; dg < 3; ++dg)
-              *reinterpret_cast<uint2*>(col + (size_t)dg * p.CSB) = pack_digits(d[dg]);
-            if ((lane & (lpg - 1)) == 0) {
-              const int gi = ko / p.gs;
-              xgsc[tok * p.G + gi] = badi ? __int_as_float(0x7fc00000)
+              for (int dg = 0; dg < 3; ++dg)
+                *reinterpret_cast<uint2*>(col + (size_t)dg * CSBx) = pack_digits(d[dg]);
+              if ((lane & (lpg - 1)) == 0) {
+                const int gi = (o * 8) >> lg2gs;
+                xgsc[tok * G + gi] = badi ? __int_as_float(0x7fc00000)
                                           : (zero ? 0.f : __uint_as_float((uint32_t)(be - 21) << 23));
-              xsum[tok * p.G + gi] = (float)s;
+                xsum[tok * G + gi] = (float)s;
+              }
             }
           }
         }
       }
     }
     named_barrier_sync(1, nthr);
-    if (threadIdx.x == 0 && ti == 0) GT(2);
+    if (threadIdx.x == 0) GTT(ti, 1);
 
-    // (2) stream the row blocks of this task
-    const int rb = (int)((long long)p.N * blockIdx.x / gridDim.x);
-    const int re = (int)((long long)p.N * (blockIdx.x + 1) / gridDim.x);
-    const int nrb = (re - rb + p.R - 1) / p.R;
-    const int nkc = (p.K + p.KC - 1) / p.KC;
-    const int ks = warp % p.KS, rgp = warp / p.KS;
+    // (2) stream the row blocks of this task.  Task fields are copied into
+    //     registers once; the hot loop uses 32-bit shared-memory addresses.
+    const int N = p.N, KS = p.KS, R = p.R, KC = p.KC, GPS = p.GPS;
+    const int Kt = p.K;
+    const uint32_t RS = p.RS;
+    const float* __restrict__ Sg = p.S;
+    const float* __restrict__ Zg = p.Z;
+    const float* __restrict__ biasg = p.bias;
+    void* Yg = p.Y;
+    const int ydt = p.ydt;
+    const int rb = (int)((unsigned)N * blockIdx.x / gridDim.x);
+    const int re = (int)((unsigned)N * (blockIdx.x + 1) / gridDim.x);
+    const int nrb = (re - rb + R - 1) / R;
+    const int nkc = (Kt + KC - 1) / KC;
+    const int ks = warp % KS, rgp = warp / KS;
     const bool active = rgp < p.RG;   // warps beyond KS*RG only keep the barriers moving
-    const uint8_t* bcol[NT];          // B columns this lane supplies, per n8 tile
+    const uint32_t smem_s = smem_u32(smem);
+    // B columns this lane supplies, per n8 tile; lanes without a column read a
+    // zero block (no divergence, a broadcast read).
+    uint32_t bcs[NT], binc[NT];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int tok = (nt >> 1) * 4 + (g >> 1);
       const int dg = (nt & 1) ? ((g & 1) ? -1 : 2) : (g & 1);
-      bcol[nt] = (tok < T && dg >= 0) ? xb + (size_t)tok * p.TS + (size_t)dg * p.CSB + t * 2 * LB
-                                      : nullptr;
+      const bool v = tok < T && dg >= 0;
+      bcs[nt] = v ? smem_s + sp.xb_base + (uint32_t)tok * p.TS + (uint32_t)dg * p.CSB + t * 2 * LB
+                  : smem_s + kZeroOff;
+      binc[nt] = v ? 1u : 0u;
     }
+    const int row0 = rgp * kMT * 16 + g;   // this lane's first A row inside a row block
+    const uint32_t mo1 = 8 * RS, mo2 = 16 * RS, mo3 = 24 * RS;
+    const uint32_t gsc_s = smem_s + sp.xs_base;
+    const uint32_t xsum_s = gsc_s + (uint32_t)T * G * 4;
 
     for (int bb = 0; bb < nrb; ++bb, ++b) {
-      const int r0 = rb + bb * p.R;
-      const int rows = min(p.R, re - r0);
+      const int r0 = rb + bb * R;
+      const int rows = min(R, re - r0);
       float acc[kMT][NTG][2];
 #pragma unroll
       for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
         for (int tg = 0; tg < NTG; ++tg) acc[mt][tg][0] = acc[mt][tg][1] = 0.f;
-      const int sl = b & 1;
-      if (ok_wait) ok_wait = mbar_wait(&sfull[sl], (b >> 1) & 1);
-      const uintptr_t s_src = reinterpret_cast<uintptr_t>(p.S + (size_t)r0 * p.G);
-      const int s_pre = (int)(s_src & 15) >> 2;
-      const int s_cnt = (int)(((s_src & 15) + (uint32_t)rows * p.G * 4) & ~15u) >> 2;
-      const float* ssm = reinterpret_cast<const float*>(sring + (size_t)sl * sp.sring_bytes);
-      const float* zsm = ssm + sp.sring_bytes / 8;
+      const int sl = b % kSS;
+      if (threadIdx.x == 0 && bb == 0) GTT(ti, 6);
+      if (ok_wait) ok_wait = mbar_wait(&sfull[sl], (b / kSS) & 1);
+      if (threadIdx.x == 0 && bb == 0) GTT(ti, 7);
+      float* ssm = reinterpret_cast<float*>(sring + (size_t)sl * sp.sring_bytes);
+      float* zsm = ssm + sp.sring_bytes / 8;
+      const int s_pre = (int)(reinterpret_cast<uintptr_t>(Sg + (size_t)r0 * G) & 15) >> 2;
+      const int s_end = s_pre + rows * G;
+      const int s_cnt = s_end & ~3;
+      if (s_cnt < s_end) {   // the last (< 4) values were not bulk-copied: fetch them
+        const int i = threadIdx.x;
+        if (i < s_end - s_cnt) {
+          const size_t gi0 = (size_t)r0 * G - s_pre + s_cnt + i;
+          ssm[s_cnt + i] = __ldg(Sg + gi0);
+          if (ASYM) zsm[s_cnt + i] = __ldg(Zg + gi0);
+        }
+        named_barrier_sync(1, nthr);
+      }
+      // scale / zero addresses of this lane's rows (rows past the block read stale values)
+      const uint32_t ss_s = smem_u32(ssm), zs_s = smem_u32(zsm);
+      uint32_t so[kMT][2];
+#pragma unroll
+      for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) so[mt][h] = (uint32_t)(s_pre + min(row0 + mt * 16 + 8 * h, rows - 1) * G) * 4;
 
       for (int kc = 0; kc < nkc; ++kc, ++c) {
         const int st = c % sp.nst, use = c / sp.nst;
-        const int k0 = kc * p.KC;
-        const int gc0 = k0 / p.gs;
-        const int gcn = min(p.KC, p.K - k0) / p.gs;
-        const int ga = active ? gc0 + min(gcn, ks * p.GPS) : 0;
-        const int gb = active ? gc0 + min(gcn, (ks + 1) * p.GPS) : 0;
+        const int k0 = kc * KC;
+        const int gc0 = k0 >> lg2gs;
+        const int gcn = min(KC, Kt - k0) >> lg2gs;
+        const int ga = active ? gc0 + min(gcn, ks * GPS) : 0;
+        const int gb = active ? gc0 + min(gcn, (ks + 1) * GPS) : 0;
         if (ok_wait) ok_wait = mbar_wait(&full[st], use & 1);
-        const uint8_t* buf = stages + (size_t)st * sp.stage_bytes;
+        if (threadIdx.x == 0 && bb == 0 && kc == 0) GTT(ti, 2);
+        // A address of (row0, k = 0) in this stage
+        const uint32_t a_s = smem_s + sp.stage_base + (uint32_t)st * sp.stage_bytes +
+                             (uint32_t)row0 * RS + t * LB - (uint32_t)(k0 >> 1);
 
         for (int gi = ga; gi < gb && ok_wait; ++gi) {
           float sc[kMT][2], zp[kMT][2];
@@ -425,19 +542,8 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
           for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int lr = (rgp * kMT + mt) * 16 + g + 8 * h;
-              const int si = s_pre + lr * p.G + gi;
-              if (lr >= rows) {
-                sc[mt][h] = 0.f;
-                zp[mt][h] = 8.f;
-              } else if (si < s_cnt) {
-                sc[mt][h] = ssm[si];
-                zp[mt][h] = ASYM ? zsm[si] : 8.f;
-              } else {  // the last few values of the block were not bulk-copied
-                const size_t gix = (size_t)(r0 + lr) * p.G + gi;
-                sc[mt][h] = __ldg(p.S + gix);
-                zp[mt][h] = ASYM ? __ldg(p.Z + gix) : 8.f;
-              }
+              sc[mt][h] = ldsf(ss_s + so[mt][h] + gi * 4);
+              zp[mt][h] = ASYM ? ldsf(zs_s + so[mt][h] + gi * 4) : 8.f;
             }
           int C[kMT][NT][4];
 #pragma unroll
@@ -445,29 +551,17 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) C[mt][nt][0] = C[mt][nt][1] = C[mt][nt][2] = C[mt][nt][3] = 0;
 
-          for (int kseg = gi * p.gs; kseg < (gi + 1) * p.gs; kseg += SEGK) {
+          const int kend = (gi + 1) << lg2gs;
+          for (int kseg = gi << lg2gs; kseg < kend; kseg += SEGK) {
             uint32_t bq[NT][2 * WPL];
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              if (bcol[nt]) lds_digits<LB>(bcol[nt] + kseg, bq[nt]);
-              else {
-#pragma unroll
-                for (int i = 0; i < 2 * WPL; ++i) bq[nt][i] = 0u;
-              }
-            }
-            const int boff = ((kseg - k0) >> 1) + t * LB;
+            for (int nt = 0; nt < NT; ++nt) lds_digits_s<LB>(bcs[nt] + (uint32_t)kseg * binc[nt], bq[nt]);
+            const uint32_t ap = a_s + (uint32_t)(kseg >> 1);
             uint32_t w0[kMT][WPL], w1[kMT][WPL];
-#pragma unroll
-            for (int mt = 0; mt < kMT; ++mt) {
-              const int lr = (rgp * kMT + mt) * 16 + g;
-              if ((rgp * kMT + mt) * 16 < rows) {
-                lds_words<LB>(buf + (size_t)lr * p.RS + boff, w0[mt]);
-                lds_words<LB>(buf + (size_t)(lr + 8) * p.RS + boff, w1[mt]);
-              } else {
-#pragma unroll
-                for (int q = 0; q < WPL; ++q) w0[mt][q] = w1[mt][q] = 0u;
-              }
-            }
+            lds_words_s<LB>(ap, w0[0]);
+            lds_words_s<LB>(ap + mo1, w1[0]);
+            lds_words_s<LB>(ap + mo2, w0[1]);
+            lds_words_s<LB>(ap + mo3, w1[1]);
 #pragma unroll
             for (int q = 0; q < WPL; ++q)
 #pragma unroll
@@ -479,23 +573,22 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
                   imma(C[mt][nt], a0, a1, a2, a3, bq[nt][2 * q], bq[nt][2 * q + 1]);
               }
           }
-          // epilogue of group gi: recombine digits, remove zeff * sum(x), scale
+          // epilogue of group gi: recombine digits, remove zeff * sum(x), scale.
+          // Lanes whose token does not exist compute on token T-1 and are never stored.
 #pragma unroll
           for (int tg = 0; tg < NTG; ++tg) {
-            const int tok = tg * 4 + t;
-            if (tok < T) {
-              const float gsc = xgsc[tok * p.G + gi];
-              const float xs = xsum[tok * p.G + gi];
+            const uint32_t tok = (uint32_t)min(tg * 4 + t, T - 1);
+            const float gsc = ldsf(gsc_s + (tok * G + gi) * 4);
+            const float xs = ldsf(xsum_s + (tok * G + gi) * 4);
 #pragma unroll
-              for (int mt = 0; mt < kMT; ++mt)
+            for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const int i01 = C[mt][2 * tg][2 * h] + 256 * C[mt][2 * tg][2 * h + 1];
-                  float f = fmaf(65536.f, (float)C[mt][2 * tg + 1][2 * h], (float)i01);
-                  f = fmaf(-zp[mt][h], xs, f);
-                  acc[mt][tg][h] = fmaf(f, sc[mt][h] * gsc, acc[mt][tg][h]);
-                }
-            }
+              for (int h = 0; h < 2; ++h) {
+                const int i01 = C[mt][2 * tg][2 * h] + 256 * C[mt][2 * tg][2 * h + 1];
+                float f = fmaf(65536.f, (float)C[mt][2 * tg + 1][2 * h], (float)i01);
+                f = fmaf(-zp[mt][h], xs, f);
+                acc[mt][tg][h] = fmaf(f, sc[mt][h] * gsc, acc[mt][tg][h]);
+              }
           }
         }
         __syncwarp();
@@ -513,7 +606,7 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
             for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
               for (int h = 0; h < 2; ++h)
-                rbuf[(ks * T + tok) * p.R + (rgp * kMT + mt) * 16 + g + 8 * h] = acc[mt][tg][h];
+                rbuf[(ks * T + tok) * R + row0 + mt * 16 + 8 * h] = acc[mt][tg][h];
           }
         }
       }
@@ -523,13 +616,15 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
       for (int idx = threadIdx.x; idx < rows * T; idx += nthr) {
         const int tok = idx / rows, r = idx - tok * rows;
         float a = 0.f;
-        for (int k = 0; k < p.KS; ++k) a += rbuf[(k * T + tok) * p.R + r];
-        if (p.bias) a += __ldg(p.bias + r0 + r);
-        st_y(p.Y, (size_t)tok * p.N + r0 + r, a, p.ydt);
+        for (int k = 0; k < KS; ++k) a += rbuf[(k * T + tok) * R + r];
+        if (biasg) a += __ldg(biasg + r0 + r);
+        st_y(Yg, (size_t)tok * N + r0 + r, a, ydt);
       }
     }
+    if (tpre)
+      reinterpret_cast<uint4*>(smem + kTaskOff + ((ti + 1) & 1) * kTaskBytes)[threadIdx.x] = tnext;
+    if (threadIdx.x == 0) GTT(ti, 3);
   }
-  if (threadIdx.x == 0) GT(15);
 }
 
 // ---------------------------------------------------------------------------
@@ -557,7 +652,7 @@ struct Need {
 // Per-task plan.  `stage` is the launch-wide stage size in bytes.
 bool plan_task(int N, int K, int T, int gs, int ncons, int grid, size_t stage, ImmaParams& q,
                Need& need) {
-  if (N < 1 || K % 32 || gs % 32 || gs > 256 || K % gs) return false;
+  if (N < 1 || K % 32 || gs < 32 || gs > 256 || (gs & (gs - 1)) || K % gs) return false;
   const int LB = lb_for(gs);
   const int G = K / gs;
   const int rows_cta = (N + grid - 1) / grid;
@@ -587,7 +682,7 @@ bool plan_task(int N, int K, int T, int gs, int ncons, int grid, size_t stage, I
   const size_t csb_target = LB == 16 ? 16 : (LB == 8 ? 64 : 32);
   const size_t CSB = pad_to((size_t)K, 128, csb_target);
   const size_t TS = pad_to(3 * CSB, 128, LB == 4 ? 64 : 0);
-  q.N = N; q.K = K; q.G = G; q.gs = gs;
+  q.N = N; q.K = K; q.G = G; q.gs = gs; q.lg2gs = __builtin_ctz((unsigned)gs);
   q.KS = KS; q.RG = RG; q.R = R; q.KC = KC; q.GPS = (KC / gs + KS - 1) / KS;
   q.contiguous = contiguous; q.RS = (uint32_t)RS; q.CSB = (uint32_t)CSB; q.TS = (uint32_t)TS;
   const size_t rh = (size_t)KS * T * R * 4;
@@ -605,12 +700,12 @@ bool plan_task(int N, int K, int T, int gs, int ncons, int grid, size_t stage, I
 bool finish_plan(const Need& need, size_t stage, long long nchunks_max, StepPlan& pl) {
   const DeviceInfo& di = device_info();
   StepParams& sp = pl.sp;
-  const size_t red_base = 128;
+  const size_t red_base = kTaskOff + 2 * kTaskBytes;
   const size_t xs_base = (red_base + 2 * need.red_half + 15) & ~(size_t)15;
   const size_t xb_base = (xs_base + need.xs + 127) & ~(size_t)127;
-  const size_t sring_bytes = 2 * need.sring_half;
+  const size_t sring_bytes = (pl.asym ? 2 : 1) * need.sring_half;   // zeros in the upper half
   const size_t sring_base = (xb_base + need.xb + 127) & ~(size_t)127;
-  const size_t stage_base = sring_base + 2 * sring_bytes;
+  const size_t stage_base = sring_base + kSS * sring_bytes;
   const size_t budget = (size_t)env_int("SF_GEMV_SMEM_KB", 220) * 1024;
   const size_t cap = budget < (size_t)di.smem_optin ? budget : (size_t)di.smem_optin;
   if (stage_base + (nchunks_max > 1 ? 2 : 1) * stage > cap) return false;
@@ -709,8 +804,9 @@ bool plan_gemv_imma(int N, int K, int T, int gs, bool asym, StepPlan& pl) {
   pl = StepPlan{};
   pl.T = T; pl.asym = asym; pl.LB = lb_for(gs); pl.grid = grid; pl.coop = false;
   StepParams& sp = pl.sp;
-  sp.ncons = env_int("SF_GEMV_WARPS", 16);
+  sp.ncons = env_int("SF_GEMV_WARPS", 15);
   if (sp.ncons > kImmaMaxThreads / 32 - 1) sp.ncons = kImmaMaxThreads / 32 - 1;
+  sp.dbg = env_int("SF_GEMV_DBG", 0);
   sp.ntasks = 1; sp.tasks = nullptr; sp.bar = nullptr;
   const size_t stage = (size_t)env_int("SF_GEMV_STAGE_KB", 64) * 1024;
   Need need;
@@ -772,11 +868,15 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
   StepPlan pl{};
   pl.T = T; pl.asym = asym; pl.LB = lb_for(gs0); pl.grid = di.sms;
   StepParams& sp = pl.sp;
-  sp.ncons = env_int("SF_GEMV_WARPS", 16);
+  sp.ncons = env_int("SF_GEMV_WARPS", 15);
   if (sp.ncons > kImmaMaxThreads / 32 - 1) sp.ncons = kImmaMaxThreads / 32 - 1;
-  const size_t stage = (size_t)env_int("SF_GEMV_STAGE_KB", 64) * 1024;
-  Need need;
+  sp.dbg = env_int("SF_GEMV_DBG", 0);
   std::vector<ImmaParams> h(ntasks);
+  // largest stage that fits next to the activations and the scale ring
+  bool planned = false;
+  for (int stage_kb = env_int("SF_GEMV_STAGE_KB", 64); stage_kb >= 16 && !planned; stage_kb -= 16) {
+  const size_t stage = (size_t)stage_kb * 1024;
+  Need need;
   long long nch = 1;
   bool any_wait = false;
   for (int i = 0; i < ntasks; ++i) {
@@ -801,7 +901,9 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
     nch += task_chunks(q, pl.grid);
   }
   pl.coop = any_wait;
-  if (!finish_plan(need, stage, nch, pl)) return fail(SF_ERR_UNSUPPORTED, "step does not fit shared memory");
+  planned = finish_plan(need, stage, nch, pl);
+  }
+  if (!planned) return fail(SF_ERR_UNSUPPORTED, "step does not fit shared memory");
   sp.ntasks = ntasks;
   sp.bar = static_cast<unsigned int*>(workspace);
   sp.tasks = reinterpret_cast<const ImmaParams*>(static_cast<uint8_t*>(workspace) + kStepHeader);

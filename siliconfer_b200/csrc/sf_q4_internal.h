@@ -7,7 +7,7 @@
 namespace sf {
 
 constexpr int kMaxDevices = 16;
-constexpr int kMaxStages = 6;          // + 2 scale-ring slots: 16 barriers below 128 B
+constexpr int kMaxStages = 6;          // + 4 scale-ring slots: 20 mbarriers below 192 B
 constexpr int kMaxGemvT = 8;           // decode GEMV handles up to 8 tokens per launch
 constexpr int kGemvMaxThreads = 512;   // keeps up to 128 registers per thread
 // Bound on every device-side wait, in SM clock cycles (about 2 s at 2 GHz).
@@ -35,7 +35,8 @@ struct GemvParams {
 };
 
 // Decode GEMV on the tensor cores (sf_q4_gemv.cu).  One task = one GEMV.
-struct ImmaParams {
+// 16-byte aligned: kernels copy descriptors with 16-byte vector loads.
+struct alignas(16) ImmaParams {
   const uint8_t* W;
   const float* S;
   const float* Z;
@@ -44,6 +45,7 @@ struct ImmaParams {
   void* Y;
   int N, K, G, gs, xdt, ydt;
   int KS, RG, R, KC, GPS;   // K-slices, row groups, rows per block, k per chunk, groups per slice
+  int lg2gs;                // log2(group size): group sizes of this kernel are powers of two
   int contiguous;           // 1: a stage holds whole rows (one contiguous region)
   int wait_before;          // grid barrier before reading X (X depends on earlier tasks)
   uint32_t RS, CSB, TS;     // stage row stride, digit column stride, token stride
@@ -58,6 +60,7 @@ struct StepParams {
   uint32_t stage_bytes, stage_base, red_base, red_half, xs_base, xb_base;
   uint32_t sring_base, sring_bytes;
   int trace_id;
+  int dbg;                  // development switches (SF_GEMV_DBG): 1 no weight copies, 2 no x staging
 };
 
 struct StepPlan {
