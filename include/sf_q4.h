@@ -110,6 +110,11 @@ typedef struct {
   int N, K, T, group_size, x_dtype, y_dtype, wait_before;
 } sf_q4_task;
 size_t sf_q4_step_workspace_bytes(int ntasks);
+/* Workspace size that also holds the activation pre-pass arena: with this
+   much workspace, tasks whose wait_before is 0 have their activations
+   converted once per run by a small pre-pass kernel and streamed into the
+   GEMV kernel instead of being converted inside it. */
+size_t sf_q4_step_workspace_bytes2(const sf_q4_task* tasks, int ntasks);
 int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size_t workspace_bytes,
                       void** handle_out);
 int sf_q4_step_run(void* handle, void* stream);

@@ -53,7 +53,7 @@ SF_DEFINE_ERROR_READER(take_dev_error_gemv_tc)
 namespace {
 
 constexpr int kMT = 2;                 // m16 tiles per warp per row block
-constexpr int kImmaMaxThreads = 512;   // up to 15 consumer warps + 1 producer warp (128 regs)
+constexpr int kImmaMaxThreads = 512;   // consumer warps + weight producer + activation producer
 constexpr uint32_t kPiece = 4096;      // contiguous bulk-copy piece (bytes)
 constexpr int kSS = 4;                 // scale-ring slots (row blocks of scales in flight)
 // shared-memory header: [0,192) mbarriers, [192,256) zero block, then two task slots
@@ -230,32 +230,33 @@ __device__ __forceinline__ const ImmaParams& task_at(const StepParams& sp, int i
   return sp.tasks ? sp.tasks[i] : sp.single;
 }
 
-// Grid-wide barrier among the consumer threads of every CTA (cooperative
-// launch, so all CTAs are resident).  Bounded: on timeout the sticky error
-// word is set and the caller stops waiting.
-__device__ __forceinline__ bool grid_barrier(unsigned int* ctr, unsigned int target, int nthr) {
-  named_barrier_sync(1, nthr);
-  __shared__ int ok_s;
-  if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(ctr, 1u);
+// Wait until every CTA has finished tasks [from, upto).  done[i] counts the
+// CTAs that finished task i, so this stays correct when the two consumer
+// groups finish out of order.  Cooperative launch: all CTAs are resident.
+// Bounded: on timeout the sticky error word is set and the caller stops waiting.
+__device__ __forceinline__ bool wait_tasks(const unsigned int* done, int from, int upto, int gtid,
+                                           int bid, int nthr, bool enabled) {
+  __shared__ int ok_s[2];
+  if (gtid == 0) {
     const long long t0 = clock64();
-    int ok = 1;
-    while (true) {
-      unsigned int v;
-      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
-      if (v >= target) break;
-      if (clock64() - t0 > kWaitCycles) {
-        atomicOr(&g_dev_error, 2u);
-        ok = 0;
-        break;
+    int ok = enabled ? 1 : 0;
+    for (int i = from; i < upto && ok; ++i) {
+      while (true) {
+        unsigned int v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(done + i) : "memory");
+        if (v >= gridDim.x) break;
+        if (clock64() - t0 > kWaitCycles) {
+          atomicOr(&g_dev_error, 2u);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
       }
-      __nanosleep(64);
     }
-    ok_s = ok;
+    ok_s[bid - 1] = ok;
   }
-  named_barrier_sync(1, nthr);
-  return ok_s != 0;
+  named_barrier_sync(bid, nthr);
+  return ok_s[bid - 1] != 0;
 }
 
 template <int T, bool ASYM, int LB>
@@ -269,9 +270,11 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
   uint64_t* empty = full + kMaxStages;
   uint64_t* sfull = empty + kMaxStages;
   uint64_t* sempty = sfull + kSS;
-  float* red = reinterpret_cast<float*>(smem + sp.red_base);
-  float* xgsc = reinterpret_cast<float*>(smem + sp.xs_base);
-  uint8_t* xb = smem + sp.xb_base;
+  uint64_t* xfull = sempty + kSS;             // per consumer group: its activation buffer
+  uint64_t* xempty = xfull + 2;
+  float* red;
+  float* xgsc;
+  uint8_t* xb;
   uint8_t* sring = smem + sp.sring_base;
   uint8_t* stages = smem + sp.stage_base;
   const uint8_t* zblk = smem + kZeroOff;   // 64 zero bytes (B operand of unused columns)
@@ -281,23 +284,85 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
   const int ncons = sp.ncons;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < sp.nst; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], ncons); }
-    for (int i = 0; i < kSS; ++i) { mbar_init(&sfull[i], 1); mbar_init(&sempty[i], ncons); }
+    // each stage / scale slot is consumed by exactly one consumer group
+    const int gw = ncons / sp.npp;
+    for (int i = 0; i < sp.nst; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], gw); }
+    for (int i = 0; i < kSS; ++i) { mbar_init(&sfull[i], 1); mbar_init(&sempty[i], gw); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&xfull[i], 1); mbar_init(&xempty[i], 1); }
     fence_mbar_init();
   }
   if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(smem + kZeroOff)[threadIdx.x] = 0u;
-  // task slot 0 <- task 0 (consumers read task descriptors from shared memory)
-  if (threadIdx.x < kTaskBytes / 16)
-    reinterpret_cast<uint4*>(smem + kTaskOff)[threadIdx.x] =
-        reinterpret_cast<const uint4*>(&task_at(sp, 0))[threadIdx.x];
+  // first descriptor of each consumer group -> its slot 0
+  for (int gq = 0; gq < sp.npp && gq < sp.ntasks; ++gq)
+    if (threadIdx.x < kTaskBytes / 16)
+      reinterpret_cast<uint4*>(smem + kTaskOff + gq * 2 * kTaskBytes)[threadIdx.x] =
+          reinterpret_cast<const uint4*>(&task_at(sp, gq))[threadIdx.x];
+  // Each consumer group owns a slice of the weight ring (nst / npp stages) and
+  // of the scale ring (kSS / npp slots), so every ring slice has one in-order
+  // consumer and mbarrier parity waits stay unambiguous.  cbase / bbase: the
+  // position in its group's slices at which each task starts in this CTA.
+  int* cbase = reinterpret_cast<int*>(smem + sp.tb_base);
+  int* bbase = cbase + sp.ntasks + 1;
+  for (int i = threadIdx.x; i < sp.ntasks; i += blockDim.x) {
+    const ImmaParams& q = task_at(sp, i);
+    const int rb = (int)((unsigned)q.N * blockIdx.x / gridDim.x);
+    const int re = (int)((unsigned)q.N * (blockIdx.x + 1) / gridDim.x);
+    const int nrb = (re - rb + q.R - 1) / q.R;
+    cbase[i + 1] = nrb * ((q.K + q.KC - 1) / q.KC);
+    bbase[i + 1] = nrb;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {   // per consumer group: exclusive prefix over that group's tasks
+    int rc[2] = {0, 0}, rbk[2] = {0, 0};
+    for (int i = 0; i < sp.ntasks; ++i) {
+      const int gq = i % sp.npp;
+      const int cc = cbase[i + 1], bc = bbase[i + 1];
+      cbase[i] = rc[gq];
+      bbase[i] = rbk[gq];
+      rc[gq] += cc;
+      rbk[gq] += bc;
+    }
+  }
   __syncthreads();
   griddep_launch_dependents();
 
+  if (warp == ncons + 1) {
+    // ------------------------- activation producer -------------------------
+    // Tasks whose activations were pre-converted (p.xd) get them bulk-copied
+    // into their consumer group's buffer once that group has finished its
+    // previous task.  A warp of its own, so the weight stream never waits here.
+    if (lane == 0) {
+      int gown[2] = {0, 0};
+      for (int ti = 0; ti < sp.ntasks; ++ti) {
+        const ImmaParams& p = task_at(sp, ti);
+        const int gq = ti % sp.npp;
+        const int k = gown[gq]++;
+        // wait for the group's previous task on EVERY task, so that this
+        // waiter is never more than one phase ahead of the barrier
+        if (k > 0 && !mbar_wait(&xempty[gq], (k - 1) & 1, 0x100u)) return;
+        if (!p.xd) continue;
+        const uint32_t xsb = (uint32_t)((T * p.G * 8 + 15) & ~15);
+        mbar_arrive_expect_tx(&xfull[gq], (uint32_t)(3 * T * p.K) + xsb);
+        uint8_t* dst = smem + sp.xb_base + gq * sp.xb_half;
+        for (int tok = 0; tok < T; ++tok)
+          for (int dg = 0; dg < 3; ++dg)
+            bulk_g2s(dst + (size_t)tok * p.TS + (size_t)dg * p.CSB,
+                     p.xd + (size_t)(tok * 3 + dg) * p.K, (uint32_t)p.K, &xfull[gq]);
+        bulk_g2s(smem + sp.xs_base + gq * sp.xs_half, p.xd + (size_t)3 * T * p.K, xsb, &xfull[gq]);
+      }
+    }
+    return;
+  }
+
   if (warp == ncons) {
     // ------------------------------ producer ------------------------------
-    int c = 0, b = 0;
+    int cg[2] = {0, 0}, bg[2] = {0, 0};
+    const int nstg = sp.nst / sp.npp, ssg = kSS / sp.npp;
     for (int ti = 0; ti < sp.ntasks; ++ti) {
       const ImmaParams& p = task_at(sp, ti);
+      const int gq = ti % sp.npp;
+      int& c = cg[gq];
+      int& b = bg[gq];
       const int rb = (int)((unsigned)p.N * blockIdx.x / gridDim.x);
       const int re = (int)((unsigned)p.N * (blockIdx.x + 1) / gridDim.x);
       const int nrb = (re - rb + p.R - 1) / p.R;
@@ -306,9 +371,9 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
       for (int bb = 0; bb < nrb; ++bb, ++b) {
         const int r0 = rb + bb * p.R;
         const int rows = min(p.R, re - r0);
-        const int sl = b % kSS;
+        const int sl = gq * ssg + b % ssg;
         int ok = 1;
-        if (lane == 0 && b >= kSS) ok = mbar_wait(&sempty[sl], ((b / kSS) - 1) & 1);
+        if (lane == 0 && b >= ssg) ok = mbar_wait(&sempty[sl], ((b / ssg) - 1) & 1, 0x40u);
         if (!__shfl_sync(0xffffffffu, ok, 0)) return;
         if (lane == 0 && bb == 0) GTT(ti, 4);
         if (lane == 0) {  // scales (+ zeros) of the row block, from the 16-byte boundary below
@@ -326,9 +391,9 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
           }
         }
         for (int kc = 0; kc < nkc; ++kc, ++c) {
-          const int st = c % sp.nst, use = c / sp.nst;
+          const int st = gq * nstg + c % nstg, use = c / nstg;
           ok = 1;
-          if (lane == 0 && use > 0) ok = mbar_wait(&empty[st], (use - 1) & 1);
+          if (lane == 0 && use > 0) ok = mbar_wait(&empty[st], (use - 1) & 1, 0x20u);
           if (!__shfl_sync(0xffffffffu, ok, 0)) return;
           const int k0 = kc * p.KC;
           const uint32_t cb = (uint32_t)(min(p.KC, p.K - k0) >> 1);
@@ -360,29 +425,48 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
   }
 
   // ------------------------------ consumers -------------------------------
-  const int nthr = ncons * 32;
+  // npp consumer groups take alternate tasks (ping-pong): while one group does
+  // a task's fixed work (dependency wait, activation staging, reduction) the
+  // other keeps the tensor cores busy.  Each group owns its activation buffer,
+  // reduction buffer, descriptor slots and named barrier.
+  const int npp = sp.npp;
+  const int GW = ncons / npp;
+  const int grp = warp / GW;
+  const int cw = warp - grp * GW;               // warp index inside the group
+  const int nthr = GW * 32;
+  const int gtid = threadIdx.x - grp * nthr;    // thread index inside the group
+  const int bid = 1 + grp;                      // named barrier of this group
+  xgsc = reinterpret_cast<float*>(smem + sp.xs_base + grp * sp.xs_half);
+  xb = smem + sp.xb_base + grp * sp.xb_half;
+  red = reinterpret_cast<float*>(smem + sp.red_base) + grp * 2 * sp.red_half;
+  uint8_t* tslot = smem + kTaskOff + grp * 2 * kTaskBytes;
   griddep_wait();
-  int c = 0, b = 0;
-  unsigned int nbar = 0;
   bool ok_wait = true;
+  int own = 0, nxpre = 0;
 
-  for (int ti = 0; ti < sp.ntasks; ++ti) {
-    named_barrier_sync(1, nthr);   // task slot ti & 1 is complete and visible
-    const ImmaParams& p = *reinterpret_cast<const ImmaParams*>(smem + kTaskOff + (ti & 1) * kTaskBytes);
-    // prefetch the next descriptor now; it is stored into the other slot at the end of this task
+  for (int ti = grp; ti < sp.ntasks; ti += npp, ++own) {
+    named_barrier_sync(bid, nthr);   // this group's slot own & 1 is complete and visible
+    const ImmaParams& p = *reinterpret_cast<const ImmaParams*>(tslot + (own & 1) * kTaskBytes);
+    int c = cbase[ti], b = bbase[ti];   // positions in this group's ring slices
+    // prefetch the group's next descriptor; stored into the other slot at the end of this task
     uint4 tnext = make_uint4(0, 0, 0, 0);
-    const bool tpre = ti + 1 < sp.ntasks && threadIdx.x < kTaskBytes / 16;
-    if (tpre) tnext = __ldg(reinterpret_cast<const uint4*>(&task_at(sp, ti + 1)) + threadIdx.x);
-    if (ti > 0 && p.wait_before && ok_wait)
-      ok_wait = grid_barrier(sp.bar, (++nbar) * gridDim.x, nthr);
+    const bool tpre = ti + npp < sp.ntasks && gtid < kTaskBytes / 16;
+    if (tpre) tnext = __ldg(reinterpret_cast<const uint4*>(&task_at(sp, ti + npp)) + gtid);
+    if (p.wait_before)   // every thread of the group takes part (named barrier inside)
+      ok_wait = wait_tasks(sp.done, p.wait_from, ti, gtid, bid, nthr, ok_wait) && ok_wait;
     float* xsum = xgsc + T * p.G;
-    if (threadIdx.x == 0) GTT(ti, 0);
+    if (gtid == 0) GTT(ti, 0);
+    const bool xpre = p.xd != nullptr;
+    if (xpre) {   // the phase count advances even after an earlier timeout
+      const uint32_t par = (uint32_t)(nxpre++) & 1;
+      if (ok_wait) ok_wait = mbar_wait(&xfull[grp], par, 0x4u);
+    }
 
     // (1) activations -> per-(token, group) fixed point, three int8 digits.
     //     Token-major; all of a thread's loads for a pass are issued before
     //     any is used; loads go through L2 (an earlier task may have written x).
     const int lg2gs = p.lg2gs, G = p.G;
-    if (!(sp.dbg & 2)) {
+    if (!(sp.dbg & 2) && !xpre) {
       const int octs = p.K >> 3;
       const int lpg = 1 << (lg2gs - 3);  // octets (lanes) per group: 4, 8, 16 or 32
       const void* X = p.X;
@@ -390,7 +474,7 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
       const uint32_t TSx = p.TS, CSBx = p.CSB;
       constexpr int NB = 4;
       for (int tok = 0; tok < T; ++tok) {
-        for (int base = warp * 32; base < octs; base += nthr * NB) {
+        for (int base = cw * 32; base < octs; base += nthr * NB) {
           float v[NB][8];
 #pragma unroll
           for (int i = 0; i < NB; ++i) {
@@ -452,8 +536,8 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
         }
       }
     }
-    named_barrier_sync(1, nthr);
-    if (threadIdx.x == 0) GTT(ti, 1);
+    named_barrier_sync(bid, nthr);
+    if (gtid == 0) GTT(ti, 1);
 
     // (2) stream the row blocks of this task.  Task fields are copied into
     //     registers once; the hot loop uses 32-bit shared-memory addresses.
@@ -469,7 +553,7 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
     const int re = (int)((unsigned)N * (blockIdx.x + 1) / gridDim.x);
     const int nrb = (re - rb + R - 1) / R;
     const int nkc = (Kt + KC - 1) / KC;
-    const int ks = warp % KS, rgp = warp / KS;
+    const int ks = cw % KS, rgp = cw / KS;
     const bool active = rgp < p.RG;   // warps beyond KS*RG only keep the barriers moving
     const uint32_t smem_s = smem_u32(smem);
     // B columns this lane supplies, per n8 tile; lanes without a column read a
@@ -480,13 +564,13 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
       const int tok = (nt >> 1) * 4 + (g >> 1);
       const int dg = (nt & 1) ? ((g & 1) ? -1 : 2) : (g & 1);
       const bool v = tok < T && dg >= 0;
-      bcs[nt] = v ? smem_s + sp.xb_base + (uint32_t)tok * p.TS + (uint32_t)dg * p.CSB + t * 2 * LB
+      bcs[nt] = v ? smem_u32(xb) + (uint32_t)tok * p.TS + (uint32_t)dg * p.CSB + t * 2 * LB
                   : smem_s + kZeroOff;
       binc[nt] = v ? 1u : 0u;
     }
     const int row0 = rgp * kMT * 16 + g;   // this lane's first A row inside a row block
     const uint32_t mo1 = 8 * RS, mo2 = 16 * RS, mo3 = 24 * RS;
-    const uint32_t gsc_s = smem_s + sp.xs_base;
+    const uint32_t gsc_s = smem_u32(xgsc);
     const uint32_t xsum_s = gsc_s + (uint32_t)T * G * 4;
 
     for (int bb = 0; bb < nrb; ++bb, ++b) {
@@ -497,23 +581,23 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
       for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
         for (int tg = 0; tg < NTG; ++tg) acc[mt][tg][0] = acc[mt][tg][1] = 0.f;
-      const int sl = b % kSS;
-      if (threadIdx.x == 0 && bb == 0) GTT(ti, 6);
-      if (ok_wait) ok_wait = mbar_wait(&sfull[sl], (b / kSS) & 1);
-      if (threadIdx.x == 0 && bb == 0) GTT(ti, 7);
+      const int sl = grp * (kSS / npp) + b % (kSS / npp);
+      if (gtid == 0 && bb == 0) GTT(ti, 6);
+      if (ok_wait) ok_wait = mbar_wait(&sfull[sl], (b / (kSS / npp)) & 1, 0x8u);
+      if (gtid == 0 && bb == 0) GTT(ti, 7);
       float* ssm = reinterpret_cast<float*>(sring + (size_t)sl * sp.sring_bytes);
       float* zsm = ssm + sp.sring_bytes / 8;
       const int s_pre = (int)(reinterpret_cast<uintptr_t>(Sg + (size_t)r0 * G) & 15) >> 2;
       const int s_end = s_pre + rows * G;
       const int s_cnt = s_end & ~3;
       if (s_cnt < s_end) {   // the last (< 4) values were not bulk-copied: fetch them
-        const int i = threadIdx.x;
+        const int i = gtid;
         if (i < s_end - s_cnt) {
           const size_t gi0 = (size_t)r0 * G - s_pre + s_cnt + i;
           ssm[s_cnt + i] = __ldg(Sg + gi0);
           if (ASYM) zsm[s_cnt + i] = __ldg(Zg + gi0);
         }
-        named_barrier_sync(1, nthr);
+        named_barrier_sync(bid, nthr);
       }
       // scale / zero addresses of this lane's rows (rows past the block read stale values)
       const uint32_t ss_s = smem_u32(ssm), zs_s = smem_u32(zsm);
@@ -524,14 +608,14 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
         for (int h = 0; h < 2; ++h) so[mt][h] = (uint32_t)(s_pre + min(row0 + mt * 16 + 8 * h, rows - 1) * G) * 4;
 
       for (int kc = 0; kc < nkc; ++kc, ++c) {
-        const int st = c % sp.nst, use = c / sp.nst;
+        const int st = grp * (sp.nst / npp) + c % (sp.nst / npp), use = c / (sp.nst / npp);
         const int k0 = kc * KC;
         const int gc0 = k0 >> lg2gs;
         const int gcn = min(KC, Kt - k0) >> lg2gs;
         const int ga = active ? gc0 + min(gcn, ks * GPS) : 0;
         const int gb = active ? gc0 + min(gcn, (ks + 1) * GPS) : 0;
-        if (ok_wait) ok_wait = mbar_wait(&full[st], use & 1);
-        if (threadIdx.x == 0 && bb == 0 && kc == 0) GTT(ti, 2);
+        if (ok_wait) ok_wait = mbar_wait(&full[st], use & 1, 0x10u);
+        if (gtid == 0 && bb == 0 && kc == 0) GTT(ti, 2);
         // A address of (row0, k = 0) in this stage
         const uint32_t a_s = smem_s + sp.stage_base + (uint32_t)st * sp.stage_bytes +
                              (uint32_t)row0 * RS + t * LB - (uint32_t)(k0 >> 1);
@@ -610,10 +694,10 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
           }
         }
       }
-      named_barrier_sync(1, nthr);
+      named_barrier_sync(bid, nthr);
       __syncwarp();
       if (lane == 0) mbar_arrive(&sempty[sl]);
-      for (int idx = threadIdx.x; idx < rows * T; idx += nthr) {
+      for (int idx = gtid; idx < rows * T; idx += nthr) {
         const int tok = idx / rows, r = idx - tok * rows;
         float a = 0.f;
         for (int k = 0; k < KS; ++k) a += rbuf[(k * T + tok) * R + r];
@@ -621,9 +705,84 @@ __global__ void __launch_bounds__(kImmaMaxThreads, 1) q4_gemv_imma_kernel(const 
         st_y(Yg, (size_t)tok * N + r0 + r, a, ydt);
       }
     }
-    if (tpre)
-      reinterpret_cast<uint4*>(smem + kTaskOff + ((ti + 1) & 1) * kTaskBytes)[threadIdx.x] = tnext;
-    if (threadIdx.x == 0) GTT(ti, 3);
+    if (tpre) reinterpret_cast<uint4*>(tslot + ((own + 1) & 1) * kTaskBytes)[gtid] = tnext;
+    named_barrier_sync(bid, nthr);   // the whole group is done with this task
+    if (gtid == 0) {
+      mbar_arrive(&xempty[grp]);      // its activation buffer may be refilled
+      if (sp.done) {                  // publish completion of task ti by this CTA
+        __threadfence();
+        atomicAdd(sp.done + ti, 1u);
+      }
+    }
+    if (gtid == 0) GTT(ti, 3);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Activation pre-pass for tasks whose X does not depend on earlier tasks: the
+// same fixed-point digit split as the in-kernel staging, written once to a
+// scratch arena ([T][3][K] digit bytes, then [T][G] group scales and [T][G]
+// sums), so that the GEMV kernel only bulk-copies it.  One CTA per task.
+// ---------------------------------------------------------------------------
+template <int T>
+__global__ void __launch_bounds__(256) q4_x_digits_kernel(const ImmaParams* __restrict__ tasks) {
+  const ImmaParams& p = tasks[blockIdx.x];
+  if (!p.xd) return;
+  const int lane = threadIdx.x & 31;
+  const int octs = p.K >> 3, total = T * octs;
+  const int lpg = 1 << (p.lg2gs - 3);
+  float* gsc = reinterpret_cast<float*>(p.xd + (size_t)3 * T * p.K);
+  float* xsm = gsc + T * p.G;
+  for (int ob = (threadIdx.x >> 5) * 32; ob < total; ob += blockDim.x) {
+    const int o = ob + lane;
+    const bool ok = o < total;
+    const int tok = ok ? o / octs : 0;
+    const int oo = ok ? o - tok * octs : 0;
+    float v[8];
+    if (ok) ld_x8(p.X, (size_t)tok * p.K + (size_t)oo * 8, p.xdt, v);
+    else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = 0.f;
+    }
+    float m = 0.f;
+    int bad = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      m = fmaxf(m, fabsf(v[j]));
+      bad |= !(fabsf(v[j]) <= 3.402823466e38f);
+    }
+    for (int off = 1; off < lpg; off <<= 1) {
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+      bad |= __shfl_xor_sync(0xffffffffu, bad, off);
+    }
+    const int be = (int)(__float_as_uint(m) >> 23);
+    const bool zero = bad || be < 22;
+    const float scl = zero ? 0.f : __uint_as_float((uint32_t)(275 - be) << 23);
+    int d[3][8];
+    int s = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int xf = __float2int_rn(v[j] * scl);
+      s += xf;
+      const int d0 = (xf << 24) >> 24;
+      const int r1 = (xf - d0) >> 8;
+      const int d1 = (r1 << 24) >> 24;
+      d[0][j] = d0;
+      d[1][j] = d1;
+      d[2][j] = (r1 - d1) >> 8;
+    }
+    for (int off = 1; off < lpg; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (ok) {
+#pragma unroll
+      for (int dg = 0; dg < 3; ++dg)
+        *reinterpret_cast<uint2*>(p.xd + (size_t)(tok * 3 + dg) * p.K + (size_t)oo * 8) = pack_digits(d[dg]);
+      if ((lane & (lpg - 1)) == 0) {
+        const int gi = (oo * 8) >> p.lg2gs;
+        gsc[tok * p.G + gi] = bad ? __int_as_float(0x7fc00000)
+                                  : (zero ? 0.f : __uint_as_float((uint32_t)(be - 21) << 23));
+        xsm[tok * p.G + gi] = (float)s;
+      }
+    }
   }
 }
 
@@ -700,32 +859,41 @@ bool plan_task(int N, int K, int T, int gs, int ncons, int grid, size_t stage, I
 bool finish_plan(const Need& need, size_t stage, long long nchunks_max, StepPlan& pl) {
   const DeviceInfo& di = device_info();
   StepParams& sp = pl.sp;
-  const size_t red_base = kTaskOff + 2 * kTaskBytes;
-  const size_t xs_base = (red_base + 2 * need.red_half + 15) & ~(size_t)15;
-  const size_t xb_base = (xs_base + need.xs + 127) & ~(size_t)127;
+  const int npp = sp.npp;
+  const size_t red_base = kTaskOff + 4 * kTaskBytes;
+  const size_t tb_base = (red_base + (size_t)npp * 2 * need.red_half + 15) & ~(size_t)15;
+  const size_t xs_half = (need.xs + 15) & ~(size_t)15;
+  const size_t xs_base = (tb_base + (size_t)8 * (sp.ntasks + 1) + 15) & ~(size_t)15;
+  const size_t xb_half = (need.xb + 127) & ~(size_t)127;
+  const size_t xb_base = (xs_base + npp * xs_half + 127) & ~(size_t)127;
   const size_t sring_bytes = (pl.asym ? 2 : 1) * need.sring_half;   // zeros in the upper half
-  const size_t sring_base = (xb_base + need.xb + 127) & ~(size_t)127;
+  const size_t sring_base = (xb_base + npp * xb_half + 127) & ~(size_t)127;
   const size_t stage_base = sring_base + kSS * sring_bytes;
   const size_t budget = (size_t)env_int("SF_GEMV_SMEM_KB", 220) * 1024;
   const size_t cap = budget < (size_t)di.smem_optin ? budget : (size_t)di.smem_optin;
   if (stage_base + (nchunks_max > 1 ? 2 : 1) * stage > cap) return false;
   long long S = (long long)((cap - stage_base) / stage);
-  const int want_st = env_int("SF_GEMV_STAGES", 3);
+  const int want_st = env_int("SF_GEMV_STAGES", 4);
   if (S > want_st) S = want_st;
   if (S > kMaxStages) S = kMaxStages;
   if (S > nchunks_max) S = nchunks_max;
-  if (S < 1) S = 1;
+  S -= S % npp;                        // equal ring slices per consumer group
+  if (S < npp) S = npp;
+  if (stage_base + (size_t)S * stage > cap) return false;
   sp.nst = (int)S;
   sp.stage_bytes = (uint32_t)stage;
   sp.stage_base = (uint32_t)stage_base;
   sp.red_base = (uint32_t)red_base;
   sp.red_half = (uint32_t)(need.red_half / 4);
+  sp.tb_base = (uint32_t)tb_base;
   sp.xs_base = (uint32_t)xs_base;
+  sp.xs_half = (uint32_t)xs_half;
   sp.xb_base = (uint32_t)xb_base;
+  sp.xb_half = (uint32_t)xb_half;
   sp.sring_base = (uint32_t)sring_base;
   sp.sring_bytes = (uint32_t)sring_bytes;
   pl.smem = stage_base + (size_t)S * stage;
-  pl.threads = (sp.ncons + 1) * 32;
+  pl.threads = (sp.ncons + 2) * 32;   // + weight producer + activation producer
   return pl.threads <= kImmaMaxThreads;
 }
 
@@ -804,14 +972,15 @@ bool plan_gemv_imma(int N, int K, int T, int gs, bool asym, StepPlan& pl) {
   pl = StepPlan{};
   pl.T = T; pl.asym = asym; pl.LB = lb_for(gs); pl.grid = grid; pl.coop = false;
   StepParams& sp = pl.sp;
-  sp.ncons = env_int("SF_GEMV_WARPS", 15);
-  if (sp.ncons > kImmaMaxThreads / 32 - 1) sp.ncons = kImmaMaxThreads / 32 - 1;
+  sp.ncons = env_int("SF_GEMV_WARPS", 14);
+  if (sp.ncons > kImmaMaxThreads / 32 - 2) sp.ncons = kImmaMaxThreads / 32 - 2;
   sp.dbg = env_int("SF_GEMV_DBG", 0);
-  sp.ntasks = 1; sp.tasks = nullptr; sp.bar = nullptr;
+  sp.ntasks = 1; sp.tasks = nullptr; sp.done = nullptr; sp.npp = 1;
   const size_t stage = (size_t)env_int("SF_GEMV_STAGE_KB", 64) * 1024;
   Need need;
   if (!plan_task(N, K, T, gs, sp.ncons, grid, stage, sp.single, need)) return false;
   sp.single.wait_before = 0;
+  sp.single.wait_from = 0;
   return finish_plan(need, stage, task_chunks(sp.single, grid), pl);
 }
 
@@ -838,24 +1007,49 @@ cudaError_t launch_gemv_imma(const StepPlan& pl0, cudaStream_t st, bool pdl) {
 using namespace sf;
 
 namespace {
-constexpr size_t kStepHeader = 256;   // grid-barrier counter lives here
+// workspace: [per-task completion counters, 256-aligned][task table]
+size_t step_header(int ntasks) { return ((size_t)4 * (ntasks > 0 ? ntasks : 0) + 255) & ~(size_t)255; }
 struct StepHandle {
   StepPlan plan;
   void* workspace;
   int device;
+  bool prepass;   // some tasks read pre-converted activations
 };
+
+template <int T>
+cudaError_t launch_prepass(const StepHandle* hd, cudaStream_t st) {
+  q4_x_digits_kernel<T><<<hd->plan.sp.ntasks, 256, 0, st>>>(hd->plan.sp.tasks);
+  return cudaGetLastError();
+}
 }  // namespace
 
 extern "C" {
 
 size_t sf_q4_step_workspace_bytes(int ntasks) {
-  return kStepHeader + (size_t)(ntasks > 0 ? ntasks : 0) * sizeof(ImmaParams);
+  return step_header(ntasks) + (size_t)(ntasks > 0 ? ntasks : 0) * sizeof(ImmaParams);
+}
+
+// Bytes of the activation arena (digits + group scales/sums) of a task list.
+static size_t x_arena_bytes(const sf_q4_task* tasks, int ntasks) {
+  size_t n = 0;
+  for (int i = 0; i < ntasks; ++i) {
+    const sf_q4_task& a = tasks[i];
+    const int G = a.group_size > 0 ? a.K / a.group_size : 0;
+    n += (((size_t)3 * a.T * a.K + ((size_t)a.T * G * 8 + 15) / 16 * 16) + 127) & ~(size_t)127;
+  }
+  return n;
+}
+
+size_t sf_q4_step_workspace_bytes2(const sf_q4_task* tasks, int ntasks) {
+  return sf_q4_step_workspace_bytes(ntasks) + x_arena_bytes(tasks, ntasks);
 }
 
 int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size_t workspace_bytes,
                       void** handle_out) {
   if (!tasks || !workspace || !handle_out) return fail(SF_ERR_NULL, "null pointer argument");
   if (ntasks < 1) return fail(SF_ERR_SHAPE, "ntasks must be >= 1");
+  // the activation pre-pass is used when the workspace also has room for its arena
+  const bool use_arena = workspace_bytes >= sf_q4_step_workspace_bytes2(tasks, ntasks);
   if (workspace_bytes < sf_q4_step_workspace_bytes(ntasks))
     return fail(SF_ERR_SHAPE, "workspace too small: need %zu bytes",
                 sf_q4_step_workspace_bytes(ntasks));
@@ -868,10 +1062,16 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
   StepPlan pl{};
   pl.T = T; pl.asym = asym; pl.LB = lb_for(gs0); pl.grid = di.sms;
   StepParams& sp = pl.sp;
-  sp.ncons = env_int("SF_GEMV_WARPS", 15);
-  if (sp.ncons > kImmaMaxThreads / 32 - 1) sp.ncons = kImmaMaxThreads / 32 - 1;
+  sp.npp = ntasks > 1 ? env_int("SF_GEMV_PINGPONG", 2) : 1;
+  if (sp.npp < 1) sp.npp = 1;
+  if (sp.npp > 2) sp.npp = 2;
+  sp.ncons = env_int("SF_GEMV_WARPS", 14);
+  if (sp.ncons > kImmaMaxThreads / 32 - 2) sp.ncons = kImmaMaxThreads / 32 - 2;
+  sp.ncons -= sp.ncons % sp.npp;
+  sp.ntasks = ntasks;
   sp.dbg = env_int("SF_GEMV_DBG", 0);
   std::vector<ImmaParams> h(ntasks);
+  bool any_pre = false;
   // largest stage that fits next to the activations and the scale ring
   bool planned = false;
   for (int stage_kb = env_int("SF_GEMV_STAGE_KB", 64); stage_kb >= 16 && !planned; stage_kb -= 16) {
@@ -879,6 +1079,9 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
   Need need;
   long long nch = 1;
   bool any_wait = false;
+  int last_wait = 0;
+  size_t arena_off = sf_q4_step_workspace_bytes(ntasks);
+  any_pre = false;
   for (int i = 0; i < ntasks; ++i) {
     const sf_q4_task& a = tasks[i];
     if (!a.W || !a.scales || !a.X || !a.Y) return fail(SF_ERR_NULL, "task %d: null pointer", i);
@@ -891,12 +1094,20 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
       return fail(SF_ERR_ALIGN, "task %d: W, scales, zeros and X must be 16-byte aligned", i);
     ImmaParams& q = h[i];
     q = ImmaParams{};
-    if (!plan_task(a.N, a.K, T, a.group_size, sp.ncons, pl.grid, stage, q, need))
+    if (!plan_task(a.N, a.K, T, a.group_size, sp.ncons / sp.npp, pl.grid, stage, q, need))
       return fail(SF_ERR_UNSUPPORTED, "task %d: shape N=%d K=%d gs=%d not supported by the step kernel",
                   i, a.N, a.K, a.group_size);
     q.W = a.W; q.S = a.scales; q.Z = a.zeros; q.bias = a.bias; q.X = a.X; q.Y = a.Y;
     q.xdt = a.x_dtype; q.ydt = a.y_dtype;
     q.wait_before = i > 0 ? (a.wait_before ? 1 : 0) : 0;
+    q.wait_from = last_wait;
+    q.xd = nullptr;
+    if (use_arena && !q.wait_before) {
+      q.xd = static_cast<uint8_t*>(workspace) + arena_off;
+      arena_off += (((size_t)3 * T * q.K + ((size_t)T * q.G * 8 + 15) / 16 * 16) + 127) & ~(size_t)127;
+      any_pre = true;
+    }
+    if (q.wait_before) last_wait = i;
     any_wait |= q.wait_before != 0;
     nch += task_chunks(q, pl.grid);
   }
@@ -904,13 +1115,12 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
   planned = finish_plan(need, stage, nch, pl);
   }
   if (!planned) return fail(SF_ERR_UNSUPPORTED, "step does not fit shared memory");
-  sp.ntasks = ntasks;
-  sp.bar = static_cast<unsigned int*>(workspace);
-  sp.tasks = reinterpret_cast<const ImmaParams*>(static_cast<uint8_t*>(workspace) + kStepHeader);
+  sp.done = static_cast<unsigned int*>(workspace);
+  sp.tasks = reinterpret_cast<const ImmaParams*>(static_cast<uint8_t*>(workspace) + step_header(ntasks));
   cudaError_t e = cudaMemcpy(const_cast<ImmaParams*>(sp.tasks), h.data(), sizeof(ImmaParams) * ntasks,
                              cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return cuda_fail(e, "uploading the task table");
-  StepHandle* hd = new StepHandle{pl, workspace, 0};
+  StepHandle* hd = new StepHandle{pl, workspace, 0, any_pre};
   cudaGetDevice(&hd->device);
   *handle_out = hd;
   return SF_OK;
@@ -920,8 +1130,22 @@ int sf_q4_step_run(void* handle, void* stream) {
   if (!handle) return fail(SF_ERR_NULL, "null handle");
   StepHandle* hd = static_cast<StepHandle*>(handle);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(hd->workspace, 0, kStepHeader, st);
+  cudaError_t e = cudaMemsetAsync(hd->workspace, 0, step_header(hd->plan.sp.ntasks), st);
   if (e != cudaSuccess) return cuda_fail(e, "clearing the barrier counter");
+  if (hd->prepass) {
+    switch (hd->plan.T) {
+      case 1: e = launch_prepass<1>(hd, st); break;
+      case 2: e = launch_prepass<2>(hd, st); break;
+      case 3: e = launch_prepass<3>(hd, st); break;
+      case 4: e = launch_prepass<4>(hd, st); break;
+      case 5: e = launch_prepass<5>(hd, st); break;
+      case 6: e = launch_prepass<6>(hd, st); break;
+      case 7: e = launch_prepass<7>(hd, st); break;
+      default: e = launch_prepass<8>(hd, st); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "activation pre-pass launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+  }
   e = launch_gemv_imma(hd->plan, st, false);
   if (e != cudaSuccess) return cuda_fail(e, "q4 step launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);

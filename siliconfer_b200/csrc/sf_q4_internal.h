@@ -47,7 +47,9 @@ struct alignas(16) ImmaParams {
   int KS, RG, R, KC, GPS;   // K-slices, row groups, rows per block, k per chunk, groups per slice
   int lg2gs;                // log2(group size): group sizes of this kernel are powers of two
   int contiguous;           // 1: a stage holds whole rows (one contiguous region)
-  int wait_before;          // grid barrier before reading X (X depends on earlier tasks)
+  int wait_before;          // read X only after every CTA finished tasks [wait_from, this)
+  int wait_from;
+  uint8_t* xd;              // pre-converted activations (digit columns, then scales/sums) or null
   uint32_t RS, CSB, TS;     // stage row stride, digit column stride, token stride
 };
 
@@ -56,8 +58,10 @@ struct StepParams {
   const ImmaParams* tasks;  // device array, or nullptr: use `single`
   ImmaParams single;
   int ntasks, ncons, nst;
-  unsigned int* bar;        // grid-barrier counter (zeroed before every launch)
+  int npp;                  // consumer groups taking alternate tasks (1 or 2)
+  unsigned int* done;       // per-task completion counters (zeroed before every launch) or null
   uint32_t stage_bytes, stage_base, red_base, red_half, xs_base, xb_base;
+  uint32_t xs_half, xb_half, tb_base;  // per-group activation areas, ring-base table
   uint32_t sring_base, sring_bytes;
   int trace_id;
   int dbg;                  // development switches (SF_GEMV_DBG): 1 no weight copies, 2 no x staging
@@ -165,12 +169,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait: gives up after kWaitCycles, records the failure in the sticky
 // device error word and returns false so that the caller can wind down.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int code = 1u) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (clock64() - t0 > kWaitCycles) {
-      atomicOr(&g_dev_error, 1u);
+      atomicOr(&g_dev_error, code);
       return false;
     }
   }
