@@ -90,15 +90,19 @@ int sf_q4_linear(const uint8_t* W, const float* scales, const float* zeros,
  * (siliconfer/model/layers.py:93-95, 133, 144; q4_linear.py:49-68).  Here a
  * caller describes the whole sequence once and replays it: one cooperative
  * launch streams every task's weights back to back, so HBM stays busy across
- * projection boundaries.  A task with wait_before != 0 reads X only after
- * every earlier task has finished writing (a grid-wide barrier, bounded in
- * time), which is how a dependency such as o_proj <- attention(q, k, v) is
- * expressed; tasks without it may overlap with the previous ones.
+ * projection boundaries.
+ * Ordering: a task with wait_before != 0 starts a new phase.  Every task of a
+ * phase reads its X only after all tasks of the previous phase have written
+ * their Y (bounded device-side waits on per-task completion counters), which
+ * is how o_proj <- attention(q, k, v) is expressed.  Tasks of one phase run
+ * concurrently.  Only the first phase's X must exist before the launch.
  * All tasks must share T (1..8), the layout (zeros NULL or not) and the group
- * class (group_size % 128, % 64 or % 32 == 0).  `workspace` is caller-owned
- * device memory of sf_q4_step_workspace_bytes(ntasks) bytes, 256-byte aligned,
- * kept alive until sf_q4_step_destroy; it holds the task table and the
- * barrier counter, so two handles that run concurrently need two workspaces.
+ * class (group_size % 128, % 64 or % 32 == 0); group_size a power of two in
+ * 32..256, K % 32 == 0, W/scales/zeros/X 16-byte aligned.  `workspace` is
+ * caller-owned device memory of sf_q4_step_workspace_bytes(tasks, ntasks)
+ * bytes, 256-byte aligned, kept alive until sf_q4_step_destroy; it holds the
+ * task table, the completion counters and the activations in integer form, so
+ * two handles that run concurrently need two workspaces.
  * create() uploads the table synchronously; run() is asynchronous. */
 typedef struct {
   const uint8_t* W;
@@ -109,12 +113,7 @@ typedef struct {
   void* Y;              /* [T, N] of y_dtype */
   int N, K, T, group_size, x_dtype, y_dtype, wait_before;
 } sf_q4_task;
-size_t sf_q4_step_workspace_bytes(int ntasks);
-/* Workspace size that also holds the activation pre-pass arena: with this
-   much workspace, tasks whose wait_before is 0 have their activations
-   converted once per run by a small pre-pass kernel and streamed into the
-   GEMV kernel instead of being converted inside it. */
-size_t sf_q4_step_workspace_bytes2(const sf_q4_task* tasks, int ntasks);
+size_t sf_q4_step_workspace_bytes(const sf_q4_task* tasks, int ntasks);
 int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size_t workspace_bytes,
                       void** handle_out);
 int sf_q4_step_run(void* handle, void* stream);

@@ -42,15 +42,13 @@ SIGNATURES = {
     "sf_q4_quantize_pack": [_P, _P, _P, _P, _I, _I, _I, _P],
     "sf_q4_check_device_error": [],
     "sf_q4_launch_count": [],
-    "sf_q4_step_workspace_bytes": [_I],
-    "sf_q4_step_workspace_bytes2": [ctypes.POINTER(Q4Task), _I],
+    "sf_q4_step_workspace_bytes": [ctypes.POINTER(Q4Task), _I],
     "sf_q4_step_create": [ctypes.POINTER(Q4Task), _I, _P, _SZ, ctypes.POINTER(_P)],
     "sf_q4_step_run": [_P, _P],
     "sf_q4_step_destroy": [_P],
 }
 _RESTYPES = {"sf_status_string": ctypes.c_char_p, "sf_last_error": ctypes.c_char_p,
              "sf_q4_launch_count": _LL, "sf_q4_step_workspace_bytes": _SZ,
-             "sf_q4_step_workspace_bytes2": _SZ,
              "sf_q4_step_destroy": None}
 
 _lib = None

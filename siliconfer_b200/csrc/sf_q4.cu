@@ -21,6 +21,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -249,6 +250,17 @@ int run_linear(const uint8_t* W, const float* S, const float* Z, const float* bi
     int rc = run_tc_gemm(W, S, Z, bias, X, xdt, Y, ydt, N, K, T, gs, flags, stream);
     if (rc != SF_ERR_UNSUPPORTED) return rc;
   }
+  if (!force_generic && aligned && !getenv("SF_GEMV_LEGACY")) {
+    // Decode GEMV as independent warp units; T above kMaxGemvT that the GEMM
+    // path declined is cut into chunks of kMaxGemvT tokens (weights re-read).
+    int rc = SF_OK;
+    for (int t0 = 0; t0 < T && rc == SF_OK; t0 += kMaxGemvT) {
+      const int tc = T - t0 < kMaxGemvT ? T - t0 : kMaxGemvT;
+      rc = run_tile_linear(W, S, Z, bias, static_cast<const uint8_t*>(X) + (size_t)t0 * K * xe, xdt,
+                           static_cast<uint8_t*>(Y) + (size_t)t0 * N * ye, ydt, N, K, tc, gs, stream);
+    }
+    if (rc != SF_ERR_UNSUPPORTED) return rc;
+  }
   if (!force_generic && aligned) {
     // Decode GEMV on the tensor cores.  Larger T that the GEMM path declined
     // is split into launches of at most kMaxGemvT tokens (weights re-read).
@@ -384,7 +396,7 @@ int sf_q4_quantize_pack(const float* W, uint8_t* packed, float* scales, float* z
 
 int sf_q4_check_device_error(void) {
   const unsigned int a = take_dev_error_gemv(), b = take_dev_error_tc(),
-                     c = take_dev_error_gemv_tc();
+                     c = take_dev_error_gemv_tc() | take_dev_error_tile();
   if (a == 0xffffffffu || b == 0xffffffffu || c == 0xffffffffu)
     return fail(SF_ERR_CUDA, "reading the device error word failed");
   if (a | b | c) return fail(SF_ERR_TIMEOUT, "a device-side wait expired (code %u)", a | b | c);

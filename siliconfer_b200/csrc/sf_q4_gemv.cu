@@ -1023,6 +1023,7 @@ cudaError_t launch_prepass(const StepHandle* hd, cudaStream_t st) {
 }
 }  // namespace
 
+#ifdef SF_LEGACY_STEP
 extern "C" {
 
 size_t sf_q4_step_workspace_bytes(int ntasks) {
@@ -1155,3 +1156,4 @@ int sf_q4_step_run(void* handle, void* stream) {
 void sf_q4_step_destroy(void* handle) { delete static_cast<StepHandle*>(handle); }
 
 }  // extern "C"
+#endif  // SF_LEGACY_STEP

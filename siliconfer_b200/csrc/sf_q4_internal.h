@@ -100,6 +100,13 @@ static __device__ unsigned int g_dev_error = 0;
 unsigned int take_dev_error_gemv();
 unsigned int take_dev_error_gemv_tc();
 unsigned int take_dev_error_tc();
+unsigned int take_dev_error_tile();
+
+// Decode GEMV (1 <= T <= kMaxGemvT) on the warp-unit kernel; SF_ERR_UNSUPPORTED
+// when the shape is not one it takes.
+int run_tile_linear(const uint8_t* W, const float* S, const float* Z, const float* bias,
+                    const void* X, int xdt, void* Y, int ydt, int N, int K, int T, int gs,
+                    cudaStream_t stream);
 
 // ---------------------------------------------------------------------------
 // Launch helper: optional programmatic dependent launch (PDL).

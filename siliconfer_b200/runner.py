@@ -89,7 +89,7 @@ class Q4StepRunner:
                 self.x.data_ptr() + c.x_off * xs, self.y.data_ptr() + c.y_off * ys,
                 m.out_features, m.in_features, self.tokens, m.group_size, xc, yc,
                 1 if self.waits[i] else 0)
-        nbytes = int(lib.sf_q4_step_workspace_bytes2(arr, n))
+        nbytes = int(lib.sf_q4_step_workspace_bytes(arr, n))
         self._workspace = torch.zeros(nbytes + 256, dtype=torch.uint8, device=self.device)
         base = self._workspace.data_ptr()
         aligned = (base + 255) & ~255

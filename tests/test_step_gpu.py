@@ -69,7 +69,7 @@ def test_step_chain_dependency(cuda):
         arr[i] = _lib.Q4Task(m.packed_d.data_ptr(), m.scales_d.data_ptr(), None, None,
                              bufs[i].data_ptr(), bufs[i + 1].data_ptr(), n, n, 1, 128,
                              _lib.SF_F32, _lib.SF_F32, 1)
-    nb = int(lib.sf_q4_step_workspace_bytes(len(layers)))
+    nb = int(lib.sf_q4_step_workspace_bytes(arr, len(layers)))
     ws = torch.zeros(nb, dtype=torch.uint8, device="cuda")
     h = ctypes.c_void_p()
     _lib.check(lib.sf_q4_step_create(arr, len(layers), ws.data_ptr(), nb, ctypes.byref(h)))
@@ -101,7 +101,7 @@ def test_step_rejects_mixed_tasks(cuda):
                          y.data_ptr(), 256, 512, 1, 128, 0, 0, 0)
     arr[1] = _lib.Q4Task(b.packed_d.data_ptr(), b.scales_d.data_ptr(), b.zeros_d.data_ptr(), None,
                          x.data_ptr(), y[1:].data_ptr(), 256, 512, 1, 128, 0, 0, 0)
-    nb = int(lib.sf_q4_step_workspace_bytes(2))
+    nb = int(lib.sf_q4_step_workspace_bytes(arr, 2))
     ws = torch.zeros(nb, dtype=torch.uint8, device="cuda")
     h = ctypes.c_void_p()
     assert lib.sf_q4_step_create(arr, 2, ws.data_ptr(), nb, ctypes.byref(h)) == 6
