@@ -6,33 +6,41 @@
 //   sym : y += s[i,g] * sum_k sext(q[i,k]) * x[k]
 //   asym: y += s[i,g] * (sum_k q[i,k] * x[k] - z[i,g] * sum_k x[k])
 //
-// Arithmetic (unchanged from the reference's algebra, exact where it can be):
+// Arithmetic (the reference's algebra, exact where it can be):
 //  * weights are UNSIGNED int8 A operands; symmetric nibbles are flipped
 //    (u ^ 8 = q + 8) by the LOP3 that masks them, so both layouts become
 //    s * (sum u*x - zeff * sum x) with zeff = 8 (sym) or z (asym);
 //  * activations: per (token, group) x_fix = rint(x * 2^(22-E)), E the binary
 //    exponent of the group's max |x|, split into three signed int8 digits
-//    (x_fix = d0 + 256 d1 + 65536 d2) by a pre-pass (or, for a task that
-//    depends on earlier ones, by the first warp that reaches it);
+//    (x_fix = d0 + 256 d1 + 65536 d2);
 //  * mma.sync m16n8k32 u8 x s8 -> s32 sums u*d exactly; one fp32 epilogue per
 //    (row, group, token) recombines the digits, removes zeff * sum(x_fix) and
 //    applies s * 2^(E-22).
 //
-// Work decomposition (the B200 part):
+// Work decomposition:
 //  * A launch owns a list of tasks (GEMVs).  Each task is cut into units of
 //    32 rows x one k-range; all units of all tasks form one global sequence.
 //  * Every warp is independent: warp w takes units w, w + W, w + 2W, ...
-//    (W = warps in the grid).  There is no block-level synchronisation at all:
-//    a unit's operands (packed weights, activation digits, scales, zeros) are
-//    streamed by the warp's own cp.async ring of D stages, each lane copying
-//    exactly the bytes it feeds to its own MMA fragments, so a lane only waits
-//    for its own copies.  Units of consecutive tasks run concurrently on
-//    different warps, which hides every per-task latency.
+//    (W = warps in the grid); there is no block-level synchronisation.  A warp
+//    streams its unit through its own ring of shared-memory stages, each
+//    guarded by its own mbarrier: lane 0 issues one TMA tile copy of the
+//    weights (32 rows x one k-segment, straight from the reference's row-major
+//    [N, K/2] bytes) and one bulk copy of the segment's activation block.
+//  * Activations are converted once per task into that block layout (digits
+//    in MMA B-fragment order, then the group scales 2^(E-22) and sums), by a
+//    pre-pass kernel for tasks whose input exists at launch, and otherwise in
+//    parallel by the warps that reach the task, in 32-octet chunks.
+//  * A unit that covers part of K writes fp32 partial sums; the last unit of
+//    a 32-row tile to finish (per-tile arrival counter) adds the partials in
+//    k order -- deterministic -- and writes Y.
 //  * Dependencies (a task that reads what earlier tasks wrote) are per-task
-//    completion counters: a warp starting a unit of such a task waits until
-//    every unit of the tasks it depends on has been published.  All warps are
-//    resident (cooperative launch, grid <= SMs) and take units in increasing
+//    completion counters: a warp starting a unit of such a task first pulls
+//    the unit's weights towards L2 (they do not depend on anything), then
+//    waits until every tile of the tasks it depends on has been written.  All
+//    warps are resident (cooperative launch) and take units in increasing
 //    order, so a wait never blocks a unit it depends on.  Waits are bounded.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -55,41 +63,167 @@ SF_DEFINE_ERROR_READER(take_dev_error_tile)
 
 namespace {
 
-constexpr int kD = 4;                  // cp.async ring depth per warp (segments)
+constexpr int kD = 4;                  // stages per warp ring
 constexpr int kTileMaxThreads = 512;
+constexpr int kUnitRows = 32;          // rows per unit (two m16 tiles)
 // More than 4 tokens doubles the accumulators; those launches hold at most 8
 // warps (their stages are larger) and get 255 registers per thread instead.
 __host__ __device__ constexpr int tile_max_threads(int T) { return T > 4 ? 256 : kTileMaxThreads; }
-constexpr int kUnitRows = 32;          // rows per unit (two m16 tiles)
 
-// One GEMV of a launch.  16-byte aligned: copied and indexed in device memory.
-struct alignas(16) TileTask {
+// Bytes of one segment's activation block: [T][3 digits][4 lanes][2*LB] digit
+// bytes, then [T] x (group scale 2^(E-22), sum of x_fix) as two fp32.
+__host__ __device__ constexpr int xblock_bytes(int T, int LB) { return (T * (24 * LB + 8) + 15) & ~15; }
+
+// Shared-memory layout of one warp's region.
+template <int T, bool ASYM, int LB>
+struct WarpLayout {
+  static constexpr int BAR = 0;                       // kD mbarriers
+  static constexpr int ZERO = 64;                     // 64 zero bytes (B fragment of absent columns)
+  static constexpr int SRING = 128;                   // 2 x [32 rows][4 groups] fp32 scales
+  static constexpr int ZRING = SRING + 1024;          // same for zeros (asym)
+  static constexpr int STAGES = ZRING + (ASYM ? 1024 : 0);
+  static constexpr int ABYTES = 32 * 4 * LB;          // [32 rows][SEGK/2 bytes]
+  static constexpr int XB = xblock_bytes(T, LB);
+  static constexpr int STAGE = (ABYTES + XB + 127) & ~127;
+  static constexpr int BYTES = STAGES + kD * STAGE;
+};
+
+// One GEMV of a launch.  The tensor maps come first (64-byte aligned).
+struct alignas(64) TileTask {
+  CUtensorMap tmW;    // packed weights [N][K/2] u8, box {SEGK/2, 32}
+  CUtensorMap tmS;    // scales [N][G] f32, box {4, 32} (when stma)
+  CUtensorMap tmZ;    // zeros, same
   const uint8_t* W;
   const float* S;
   const float* Z;
   const float* bias;
   const void* X;
   void* Y;
-  uint8_t* xd;        // activation digits [T][3][K], then gsc [T][G], xsum [T][G]
-  float* part;        // k-split partial sums [ksplit][T][N] (ksplit > 1) or null
+  uint8_t* xd;        // activation blocks, one per k-segment
+  float* part;        // k-split partial sums [ksplit][T][N] (ksplit > 1)
+  unsigned int* tcnt; // per-tile arrival counters (ksplit > 1)
   long long ubase;    // index of the task's first unit in the launch
   int N, K, G, lg2gs, xdt, ydt;
   int ntile, ksplit, kper;   // 32-row tiles, k-splits, k per split (whole groups)
-  int xpre;                  // digits were written by the pre-pass
+  int xpre;                  // activation blocks were written by the pre-pass
   int wait_from, wait_to;    // tasks [wait_from, wait_to) finish before this one reads X
+  int stma;                  // scales (and zeros) by TMA; else per-lane copies
+  int nchunk;                // 32-octet conversion chunks
 };
 
 struct TileLaunch {
-  const TileTask* tasks;  // device table, or null: use `single`
-  TileTask single;
-  int ntasks;
+  TileTask single;        // used when `tasks` is null
+  const TileTask* tasks;  // device table
+  unsigned int* ctr;      // per task: [units done, chunks claimed, chunks done, -] or null
   long long total;        // units in the launch
-  unsigned int* done;     // per task: units finished (zeroed before each launch) or null
-  unsigned int* xflag;    // per task: 0 digits missing, 1 being written, 2 ready
+  int ntasks;
+  int prefetch;           // pull a waiting unit's weights into L2 before the wait
+  int dbg;                // development: 2 = copies only, 3 = arithmetic only (wrong results)
 };
 
-__device__ __forceinline__ const TileTask& tile_task(const TileLaunch& L, int i) {
-  return L.tasks ? L.tasks[i] : L.single;
+__device__ __forceinline__ const TileTask* tile_task(const TileLaunch& L, int i) {
+  return L.tasks ? L.tasks + i : &L.single;
+}
+
+// ---- PTX wrappers -----------------------------------------------------------
+__device__ __forceinline__ void bar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void bar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// Arrives on `bar` once every cp.async this thread issued so far has landed.
+__device__ __forceinline__ void bar_arrive_cpasync(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool bar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, unsigned int code) {
+  if (bar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!bar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) {
+      atomicOr(&g_dev_error, code);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void cpa4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+template <int NB>   // NB bytes from shared memory into NB/4 words
+__device__ __forceinline__ void lds_n(uint32_t a, uint32_t* w) {
+  if constexpr (NB == 32) {
+    const uint4 u = lds128(a), v = lds128(a + 16);
+    w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w; w[4] = v.x; w[5] = v.y; w[6] = v.z; w[7] = v.w;
+  } else if constexpr (NB == 16) {
+    const uint4 u = lds128(a);
+    w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
+  } else if constexpr (NB == 8) {
+    const uint2 u = lds64(a);
+    w[0] = u.x; w[1] = u.y;
+  } else {
+    w[0] = lds32(a);
+  }
+}
+
+__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded spin on a global counter (one thread).  false on timeout.
+__device__ __forceinline__ bool spin_geq(const unsigned int* p, unsigned int target, unsigned int code) {
+  if (ld_acquire(p) >= target) return true;
+  const long long t0 = clock64();
+  while (ld_acquire(p) < target) {
+    if (clock64() - t0 > kWaitCycles) {
+      atomicOr(&g_dev_error, code);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
 }
 
 __device__ __forceinline__ void ld_x8(const void* x, size_t idx, int dt, float* v) {
@@ -118,13 +252,21 @@ __device__ __forceinline__ void st_y(void* y, size_t idx, float v, int dt) {
   else reinterpret_cast<__nv_bfloat16*>(y)[idx] = __float2bfloat16_rn(v);
 }
 
-// D += A(u8, 16x32) * B(s8, 32x8), s32 accumulate (no side effects: not volatile).
+// D (+)= A(u8, 16x32) * B(s8, 32x8), s32.  Not volatile: no side effects, so
+// the compiler may interleave independent chains.
 __device__ __forceinline__ void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                      uint32_t a3, uint32_t b0, uint32_t b1) {
   asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void imma0(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                      uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
 
 template <bool ASYM>
@@ -147,9 +289,8 @@ __device__ __forceinline__ uint2 pack_digits(const int* d) {
   return r;
 }
 
-// Fixed-point digit split of 8 activations of one lane.  Lanes [lpg-aligned
-// blocks] form one quantization group.  Writes the three digit words and
-// returns (through gsc_out / sum_out) the group scale and sum.
+// Fixed-point digit split of 8 activations of one lane; lanes in aligned
+// blocks of `lpg` form one quantization group.
 __device__ __forceinline__ void digits8(const float* v, int lpg, uint2* dig, float& gsc_out,
                                         int& sum_out) {
   float m = 0.f;
@@ -163,7 +304,7 @@ __device__ __forceinline__ void digits8(const float* v, int lpg, uint2* dig, flo
     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
     bad |= __shfl_xor_sync(0xffffffffu, bad, off);
   }
-  // binary exponent field of the group max; groups below 2^-105 are zero
+  // biased binary exponent of the group max; groups below 2^-105 are zero
   const int be = (int)(__float_as_uint(m) >> 23);
   const bool zero = bad || be < 22;
   const float scl = zero ? 0.f : __uint_as_float((uint32_t)(275 - be) << 23);   // 2^(22-E)
@@ -189,235 +330,189 @@ __device__ __forceinline__ void digits8(const float* v, int lpg, uint2* dig, flo
   sum_out = s;
 }
 
-// Activation digits of one task, written by the threads [tid0, tid0 + nthr)
-// (a whole CTA in the pre-pass, one warp inside the GEMV kernel).
-template <int T>
-__device__ __forceinline__ void write_digits(const TileTask& p, int tid, int nthr) {
-  const int lane = tid & 31;
-  const int octs = p.K >> 3, total = T * octs;
-  const int lpg = 1 << (p.lg2gs - 3);
-  float* gsc = reinterpret_cast<float*>(p.xd + (size_t)3 * T * p.K);
-  float* xsm = gsc + T * p.G;
-  for (int ob = tid - lane; ob < total; ob += nthr) {
-    const int o = ob + lane;
-    const bool ok = o < total;
-    const int tok = ok ? o / octs : 0;
-    const int oo = ok ? o - tok * octs : 0;
-    float v[8];
-    if (ok) ld_x8(p.X, (size_t)tok * p.K + (size_t)oo * 8, p.xdt, v);
-    else {
+// Converts chunk `c` (32 consecutive octets of the [T][K] input) of a task
+// into its activation blocks.  Called by a whole warp.
+template <int T, int LB>
+__device__ __forceinline__ void convert_chunk(const TileTask* p, int c, int lane) {
+  constexpr int SEGK = 8 * LB, XB = xblock_bytes(T, LB);
+  const int K = p->K, lg2gs = p->lg2gs;
+  const int octs = K >> 3, total = T * octs;
+  const int lpg = 1 << (lg2gs - 3);
+  const int o = c * 32 + lane;
+  const bool ok = o < total;
+  const int tok = ok ? o / octs : 0;
+  const int oo = ok ? o - tok * octs : 0;
+  float v[8];
+  if (ok) ld_x8(p->X, (size_t)tok * K + (size_t)oo * 8, p->xdt, v);
+  else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = 0.f;
-    }
-    uint2 dig[3];
-    float gs_;
-    int s;
-    digits8(v, lpg, dig, gs_, s);
-    if (ok) {
+    for (int j = 0; j < 8; ++j) v[j] = 0.f;
+  }
+  uint2 dig[3];
+  float gsc;
+  int s;
+  digits8(v, lpg, dig, gsc, s);
+  if (!ok) return;
+  const int k0 = oo * 8;
+  const int seg = k0 / SEGK, within = k0 - seg * SEGK;
+  const int tt = within / (2 * LB), j = (within - tt * 2 * LB) >> 3;
+  uint8_t* blk = p->xd + (size_t)seg * XB;
 #pragma unroll
-      for (int dg = 0; dg < 3; ++dg)
-        *reinterpret_cast<uint2*>(p.xd + (size_t)(tok * 3 + dg) * p.K + (size_t)oo * 8) = dig[dg];
-      if ((lane & (lpg - 1)) == 0) {
-        const int gi = (oo * 8) >> p.lg2gs;
-        gsc[tok * p.G + gi] = gs_;
-        xsm[tok * p.G + gi] = (float)s;
-      }
-    }
-  }
-}
-
-// ---- cp.async helpers (each lane copies only what it later reads itself) ----
-template <int BYTES>
-__device__ __forceinline__ void cpa(uint32_t dst, const void* src) {
-  if constexpr (BYTES == 16)
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-  else
-    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(dst), "l"(src), "n"(BYTES)
-                 : "memory");
-}
-__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cpa_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-__device__ __forceinline__ uint4 lds128(uint32_t a) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ uint2 lds64(uint32_t a) {
-  uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ uint32_t lds32(uint32_t a) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-  return v;
-}
-
-template <int NB>   // NB bytes from shared memory into NB/4 words
-__device__ __forceinline__ void lds_n(uint32_t a, uint32_t* w) {
-  if constexpr (NB == 32) {
-    const uint4 u = lds128(a), v = lds128(a + 16);
-    w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w; w[4] = v.x; w[5] = v.y; w[6] = v.z; w[7] = v.w;
-  } else if constexpr (NB == 16) {
-    const uint4 u = lds128(a);
-    w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
-  } else if constexpr (NB == 8) {
-    const uint2 u = lds64(a);
-    w[0] = u.x; w[1] = u.y;
-  } else {
-    w[0] = lds32(a);
-  }
-}
-
-// Bounded spin on a global counter (one thread).  false on timeout.
-__device__ __forceinline__ bool spin_geq(const unsigned int* p, unsigned int target, unsigned int code) {
-  const long long t0 = clock64();
-  while (true) {
-    unsigned int v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    if (v >= target) return true;
-    if (clock64() - t0 > kWaitCycles) {
-      atomicOr(&g_dev_error, code);
-      return false;
-    }
-    __nanosleep(128);
+  for (int dg = 0; dg < 3; ++dg)
+    *reinterpret_cast<uint2*>(blk + ((tok * 3 + dg) * 4 + tt) * 2 * LB + j * 8) = dig[dg];
+  if ((lane & (lpg - 1)) == 0) {
+    // every segment of the group carries the group's scale and sum
+    const int gs = 1 << lg2gs;
+    const int s0 = ((k0 >> lg2gs) << lg2gs) / SEGK;
+    const float2 gv = make_float2(gsc, (float)s);
+    for (int sg = s0; sg < s0 + gs / SEGK; ++sg)
+      *reinterpret_cast<float2*>(p->xd + (size_t)sg * XB + T * 24 * LB + tok * 8) = gv;
   }
 }
 
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// Per-warp shared-memory stage (bytes), lane-major inside each operand:
-//   A  [4 row slots][32 lanes][LB]        rows g, g+8 of tiles 0 and 1
-//   B  [NT tiles][32 lanes][2*LB]         the lane's digit column
-//   S  [4 row slots][32 lanes][4]         scales (Z: zeros, asym only)
-//   X  [NTG][32 lanes][8]                 group scale 2^(E-22) and sum(x_fix)
+// The GEMV kernel
 // ---------------------------------------------------------------------------
-template <int T, bool ASYM, int LB>
-struct TileStage {
-  static constexpr int NTG = (T + 3) / 4;
-  static constexpr int NT = 2 * NTG;
-  static constexpr int A = 0;
-  static constexpr int B = A + 4 * 32 * LB;
-  static constexpr int S = B + NT * 32 * 2 * LB;
-  static constexpr int Z = S + 4 * 32 * 4;
-  static constexpr int X = Z + (ASYM ? 4 * 32 * 4 : 0);
-  static constexpr int BYTES = X + NTG * 32 * 8;
-};
-
 template <int T, bool ASYM, int LB>
 __global__ void __launch_bounds__(tile_max_threads(T), 1)
     q4_tile_kernel(const __grid_constant__ TileLaunch L) {
-  using St = TileStage<T, ASYM, LB>;
-  constexpr int NTG = St::NTG, NT = St::NT, WPL = LB / 4, SEGK = 8 * LB;
+  using Ly = WarpLayout<T, ASYM, LB>;
+  constexpr int NTG = (T + 3) / 4, NT = 2 * NTG, WPL = LB / 4, SEGK = 8 * LB, ROWB = 4 * LB;
+  constexpr int XOFF = Ly::ABYTES;               // activation block inside a stage
+  constexpr int GOFF = XOFF + T * 24 * LB;       // group scales / sums inside the block
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int wpc = blockDim.x >> 5;
-  const uint32_t ring = (uint32_t)__cvta_generic_to_shared(smem) + (uint32_t)warp * kD * St::BYTES;
-  const long long W_all = (long long)gridDim.x * wpc;
+  const uint32_t wb = (uint32_t)__cvta_generic_to_shared(smem) + (uint32_t)warp * Ly::BYTES;
+  const uint32_t bar0 = wb + Ly::BAR, zblk = wb + Ly::ZERO, sring = wb + Ly::SRING,
+                 zring = wb + Ly::ZRING, stage0 = wb + Ly::STAGES;
+
+  if (lane < kD) bar_init(bar0 + lane * 8, 33);   // lane 0's expect_tx + 32 cp.async arrivals
+  if (lane < 16) asm volatile("st.shared.u32 [%0], %1;" ::"r"(zblk + lane * 4), "r"(0u) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+
+  // B fragment sources: column g of tile nt is (token, digit) or absent.
+  int bslot[NT];
+  bool bval[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int tok = (nt >> 1) * 4 + (g >> 1);
+    const int dg = (nt & 1) ? ((g & 1) ? -1 : 2) : (g & 1);
+    bval[nt] = tok < T && dg >= 0;
+    bslot[nt] = bval[nt] ? ((tok * 3 + dg) * 4 + t) * 2 * LB : 0;
+  }
+  // rows of this lane inside a unit: slot i -> tile (i>>1), row g (+8 when i odd)
+  int rloc[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) rloc[i] = (i >> 1) * 16 + g + 8 * (i & 1);
+
+  const long long W_all = (long long)gridDim.x * (blockDim.x >> 5);
+  uint32_t gseg = 0;   // segments this warp has consumed (ring position and phase)
   int ti = 0;
   bool ok = true;
 
   for (long long u = (long long)warp * gridDim.x + blockIdx.x; u < L.total && ok; u += W_all) {
-    while (ti + 1 < L.ntasks && u >= tile_task(L, ti + 1).ubase) ++ti;
-    const TileTask& p = tile_task(L, ti);
-    const int N = p.N, K = p.K, G = p.G, lg2gs = p.lg2gs, ntile = p.ntile;
-    const int lu = (int)(u - p.ubase);
+    while (ti + 1 < L.ntasks && u >= tile_task(L, ti + 1)->ubase) ++ti;
+    const TileTask* p = tile_task(L, ti);
+    const int N = p->N, K = p->K, G = p->G, lg2gs = p->lg2gs, ntile = p->ntile;
+    const int ksplit = p->ksplit, kper = p->kper, stma = p->stma;
+    const int lu = (int)(u - p->ubase);
     const int tile = lu % ntile, ks = lu / ntile;
+    const int r0 = tile * kUnitRows;
+    const int kb = ks * kper;
+    const int ke = min(K, kb + kper);
+    const int nseg = (ke - kb) / SEGK;
+    const int g0 = kb >> lg2gs, gend = ke >> lg2gs;
+    const int lg2spg = lg2gs - (31 - __clz(SEGK));   // segments per group = 1 << lg2spg
+    const int spg_mask = (1 << lg2spg) - 1;
 
-    // ---- dependencies and activation digits ------------------------------
-    if (p.wait_to > p.wait_from) {
+    // ---- dependencies and activation blocks --------------------------------
+    if (p->wait_to > p->wait_from) {
+      if (L.prefetch) {
+        // The weights do not depend on earlier tasks: start them towards L2
+        // now, so that the wait overlaps with HBM traffic.
+        const int rows = min(kUnitRows, N - r0);
+        if (ksplit == 1) {
+          if (lane == 0) prefetch_l2(p->W + (size_t)r0 * (K >> 1), (uint32_t)rows * (K >> 1));
+        } else if (lane < rows) {
+          prefetch_l2(p->W + (size_t)(r0 + lane) * (K >> 1) + (kb >> 1), (uint32_t)(ke - kb) >> 1);
+        }
+      }
       int okw = 1;
       if (lane == 0)
-        for (int i = p.wait_from; i < p.wait_to && okw; ++i) {
-          const TileTask& q = tile_task(L, i);
-          okw = spin_geq(L.done + i, (unsigned)(q.ntile * q.ksplit), 0x200u);
-        }
+        for (int i = p->wait_from; i < p->wait_to && okw; ++i)
+          okw = spin_geq(L.ctr + 4 * i, (unsigned)tile_task(L, i)->ntile, 0x200u);
       ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
       if (!ok) break;
     }
-    if (!p.xpre) {   // the first warp to reach the task writes its digits
-      int state = 0;
-      if (lane == 0) state = (int)atomicCAS(L.xflag + ti, 0u, 1u);
-      state = __shfl_sync(0xffffffffu, state, 0);
-      if (state == 0) {
-        write_digits<T>(p, lane, 32);
+    if (!p->xpre) {
+      // convert whatever chunks no other warp has claimed, then wait for all
+      unsigned int* xc = L.ctr + 4 * ti;
+      const int nch = p->nchunk;
+      while (true) {
+        int c = 0;
+        if (lane == 0) c = (int)atomicAdd(xc + 1, 1u);
+        c = __shfl_sync(0xffffffffu, c, 0);
+        if (c >= nch) break;
+        convert_chunk<T, LB>(p, c, lane);
+        asm volatile("fence.proxy.async.global;" ::: "memory");
         __threadfence();
         __syncwarp();
-        if (lane == 0) atomicExch(L.xflag + ti, 2u);
-      } else {
-        int okx = 1;
-        if (lane == 0) okx = spin_geq(L.xflag + ti, 2u, 0x400u);
-        ok = __shfl_sync(0xffffffffu, okx, 0) != 0;
-        if (!ok) break;
+        if (lane == 0) atomicAdd(xc + 2, 1u);
       }
+      int okx = 1;
+      if (lane == 0) {
+        okx = spin_geq(xc + 2, (unsigned)nch, 0x400u);
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+      }
+      ok = __shfl_sync(0xffffffffu, okx, 0) != 0;
+      if (!ok) break;
     }
 
-    // ---- operand sources of this lane --------------------------------------
-    const int r0 = tile * kUnitRows;
-    const int kb = ks * p.kper;
-    const int ke = min(K, kb + p.kper);
-    const int nseg = (ke - kb) / SEGK;
-    const uint8_t* asrc[4];
-    const float* ssrc[4];
-    const float* zsrc[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int row = min(r0 + (i >> 1) * 16 + g + 8 * (i & 1), N - 1);
-      asrc[i] = p.W + (size_t)row * (K >> 1) + (kb >> 1) + t * LB;
-      ssrc[i] = p.S + (size_t)row * G;
-      zsrc[i] = ASYM ? p.Z + (size_t)row * G : nullptr;
-    }
-    const uint8_t* bsrc[NT];
-    bool bval[NT];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int tok = (nt >> 1) * 4 + (g >> 1);
-      const int dg = (nt & 1) ? ((g & 1) ? -1 : 2) : (g & 1);
-      bval[nt] = tok < T && dg >= 0;
-      bsrc[nt] = p.xd + (size_t)(bval[nt] ? tok * 3 + dg : 0) * K + kb + t * 2 * LB;
-    }
-    const float* xgsc = reinterpret_cast<const float*>(p.xd + (size_t)3 * T * K);
-    const float* xsum = xgsc + T * G;
-
-    auto issue = [&](int seg) {
-      const uint32_t st = ring + (uint32_t)(seg % kD) * St::BYTES;
-      const int gi = (kb + seg * SEGK) >> lg2gs;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        cpa<LB>(st + St::A + (i * 32 + lane) * LB, asrc[i] + seg * (SEGK >> 1));
-        cpa<4>(st + St::S + (i * 32 + lane) * 4, ssrc[i] + gi);
-        if (ASYM) cpa<4>(st + St::Z + (i * 32 + lane) * 4, zsrc[i] + gi);
+    // ---- operand streaming ---------------------------------------------------
+    const uint8_t* xsrc = p->xd + (size_t)(kb / SEGK) * Ly::XB;
+    const float* Sb = p->S;
+    const float* Zb = p->Z;
+    auto issue = [&](int s) {
+      if (L.dbg == 3) return;
+      const uint32_t slot = (gseg + s) % kD;
+      const uint32_t st = stage0 + slot * Ly::STAGE, bar = bar0 + slot * 8;
+      const int gl = s >> lg2spg;                                  // group inside the unit
+      const bool sblk = (s & spg_mask) == 0 && (gl & 3) == 0;      // first segment of a 4-group block
+      const uint32_t soff = (uint32_t)((gl >> 2) & 1) * 512;
+      if (lane == 0) {
+        const uint32_t sbytes = (sblk && stma) ? (ASYM ? 1024u : 512u) : 0u;
+        bar_expect_tx(bar, (uint32_t)Ly::ABYTES + Ly::XB + sbytes);
+        tma_2d(st, &p->tmW, (kb >> 1) + s * ROWB, r0, bar);
+        bulk_copy(st + XOFF, xsrc + (size_t)s * Ly::XB, Ly::XB, bar);
+        if (sblk && stma) {
+          tma_2d(sring + soff, &p->tmS, g0 + gl, r0, bar);
+          if (ASYM) tma_2d(zring + soff, &p->tmZ, g0 + gl, r0, bar);
+        }
       }
+      if (sblk && !stma) {
+        const int grp = g0 + gl + t;
+        if (grp < gend) {
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        if (bval[nt]) {
-          const uint32_t d = st + St::B + (nt * 32 + lane) * 2 * LB;
-          const uint8_t* sp = bsrc[nt] + seg * SEGK;
-          if constexpr (LB == 16) {
-            cpa<16>(d, sp);
-            cpa<16>(d + 16, sp + 16);
-          } else {
-            cpa<2 * LB>(d, sp);
+          for (int i = 0; i < 4; ++i) {
+            const int row = min(r0 + rloc[i], N - 1);
+            cpa4(sring + soff + rloc[i] * 16 + t * 4, Sb + (size_t)row * G + grp);
+            if (ASYM) cpa4(zring + soff + rloc[i] * 16 + t * 4, Zb + (size_t)row * G + grp);
           }
         }
       }
-#pragma unroll
-      for (int tg = 0; tg < NTG; ++tg) {
-        const int tok = min(tg * 4 + t, T - 1);
-        cpa<4>(st + St::X + (tg * 32 + lane) * 8, xgsc + tok * G + gi);
-        cpa<4>(st + St::X + (tg * 32 + lane) * 8 + 4, xsum + tok * G + gi);
-      }
+      bar_arrive_cpasync(bar);
     };
 
+    __syncwarp();
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 #pragma unroll
-    for (int s = 0; s < kD - 1; ++s) {
+    for (int s = 0; s < kD - 1; ++s)
       if (s < nseg) issue(s);
-      cpa_commit();
-    }
 
     float acc[2][NTG][2];
 #pragma unroll
@@ -425,115 +520,136 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
 #pragma unroll
       for (int tg = 0; tg < NTG; ++tg) acc[mt][tg][0] = acc[mt][tg][1] = 0.f;
     int C[2][NT][4];
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) C[mt][nt][0] = C[mt][nt][1] = C[mt][nt][2] = C[mt][nt][3] = 0;
-    const int segs_per_group = (1 << lg2gs) / SEGK;
 
-    for (int seg = 0; seg < nseg; ++seg) {
-      cpa_wait<kD - 2>();   // this lane's copies of segment `seg` have landed
-      const uint32_t st = ring + (uint32_t)(seg % kD) * St::BYTES;
-      uint32_t w[4][WPL];
+    for (int s = 0; s < nseg; ++s) {
+      const uint32_t slot = (gseg + s) % kD;
+      const uint32_t st = stage0 + slot * Ly::STAGE;
+      if (L.dbg != 3 && !bar_wait(bar0 + slot * 8, ((gseg + s) / kD) & 1, 0x10u)) {
+        ok = false;
+        break;
+      }
+      if (L.dbg != 2) {
+        uint32_t w[4][WPL];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) lds_n<LB>(st + St::A + (i * 32 + lane) * LB, w[i]);
-      uint32_t bq[NT][2 * WPL];
+        for (int i = 0; i < 4; ++i) lds_n<LB>(st + rloc[i] * ROWB + t * LB, w[i]);
+        uint32_t bq[NT][2 * WPL];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        lds_n<2 * LB>(st + St::B + (nt * 32 + lane) * 2 * LB, bq[nt]);
-        if (!bval[nt]) {
+        for (int nt = 0; nt < NT; ++nt) lds_n<2 * LB>(bval[nt] ? st + XOFF + bslot[nt] : zblk, bq[nt]);
+        const bool first = (s & spg_mask) == 0;
 #pragma unroll
-          for (int j = 0; j < 2 * WPL; ++j) bq[nt][j] = 0u;
+        for (int q = 0; q < WPL; ++q)
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) {
+            const uint32_t a0 = nib_lo<ASYM>(w[2 * mt][q]), a2 = nib_hi<ASYM>(w[2 * mt][q]);
+            const uint32_t a1 = nib_lo<ASYM>(w[2 * mt + 1][q]), a3 = nib_hi<ASYM>(w[2 * mt + 1][q]);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              if (q == 0 && first) imma0(C[mt][nt], a0, a1, a2, a3, bq[nt][0], bq[nt][1]);
+              else imma(C[mt][nt], a0, a1, a2, a3, bq[nt][2 * q], bq[nt][2 * q + 1]);
+            }
+          }
+        if ((s & spg_mask) == spg_mask) {
+          // epilogue of this group: recombine digits, remove zeff * sum(x), scale.
+          // Lanes whose token does not exist compute on token T-1 and never store.
+          const int gl = s >> lg2spg;
+          const uint32_t soff = (uint32_t)((gl >> 2) & 1) * 512 + (gl & 3) * 4;
+#pragma unroll
+          for (int tg = 0; tg < NTG; ++tg) {
+            const uint2 xv = lds64(st + GOFF + min(tg * 4 + t, T - 1) * 8);
+            const float gsc = __uint_as_float(xv.x), xs = __uint_as_float(xv.y);
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int r = rloc[2 * mt + h];
+                const float sc = __uint_as_float(lds32(sring + soff + r * 16));
+                const float zp = ASYM ? __uint_as_float(lds32(zring + soff + r * 16)) : 8.f;
+                const int i01 = C[mt][2 * tg][2 * h] + 256 * C[mt][2 * tg][2 * h + 1];
+                float f = fmaf(65536.f, (float)C[mt][2 * tg + 1][2 * h], (float)i01);
+                f = fmaf(-zp, xs, f);
+                acc[mt][tg][h] = fmaf(f, sc * gsc, acc[mt][tg][h]);
+              }
+          }
         }
       }
+      __syncwarp();
+      if (s + kD - 1 < nseg) issue(s + kD - 1);
+    }
+    if (!ok) break;
+    gseg += (uint32_t)nseg;
+
+    // ---- results ---------------------------------------------------------------
+    if (ksplit == 1) {
 #pragma unroll
-      for (int q = 0; q < WPL; ++q)
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          const uint32_t a0 = nib_lo<ASYM>(w[2 * mt][q]), a2 = nib_hi<ASYM>(w[2 * mt][q]);
-          const uint32_t a1 = nib_lo<ASYM>(w[2 * mt + 1][q]), a3 = nib_hi<ASYM>(w[2 * mt + 1][q]);
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-            imma(C[mt][nt], a0, a1, a2, a3, bq[nt][2 * q], bq[nt][2 * q + 1]);
-        }
-      if ((seg + 1) % segs_per_group == 0 || seg + 1 == nseg) {
-        // epilogue of this group: recombine digits, remove zeff * sum(x), scale.
-        // Lanes whose token does not exist compute on token T-1 and never store.
-#pragma unroll
-        for (int tg = 0; tg < NTG; ++tg) {
-          const uint2 xv = lds64(st + St::X + (tg * 32 + lane) * 8);
-          const float gsc = __uint_as_float(xv.x), xs = __uint_as_float(xv.y);
+      for (int tg = 0; tg < NTG; ++tg) {
+        const int tok = tg * 4 + t;
+        if (tok < T) {
 #pragma unroll
           for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const float sc = __uint_as_float(lds32(st + St::S + ((2 * mt + h) * 32 + lane) * 4));
-              const float zp = ASYM ? __uint_as_float(lds32(st + St::Z + ((2 * mt + h) * 32 + lane) * 4))
-                                    : 8.f;
-              const int i01 = C[mt][2 * tg][2 * h] + 256 * C[mt][2 * tg][2 * h + 1];
-              float f = fmaf(65536.f, (float)C[mt][2 * tg + 1][2 * h], (float)i01);
-              f = fmaf(-zp, xs, f);
-              acc[mt][tg][h] = fmaf(f, sc * gsc, acc[mt][tg][h]);
-            }
-        }
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) C[mt][nt][0] = C[mt][nt][1] = C[mt][nt][2] = C[mt][nt][3] = 0;
-      }
-      if (seg + kD - 1 < nseg) issue(seg + kD - 1);
-      cpa_commit();
-    }
-    cpa_wait<0>();
-
-    // ---- results -----------------------------------------------------------
-#pragma unroll
-    for (int tg = 0; tg < NTG; ++tg) {
-      const int tok = tg * 4 + t;
-      if (tok < T) {
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int row = r0 + mt * 16 + g + 8 * h;
-            if (row < N) {
-              const float a = acc[mt][tg][h];
-              if (p.ksplit == 1) {
-                st_y(p.Y, (size_t)tok * N + row, p.bias ? a + __ldg(p.bias + row) : a, p.ydt);
-              } else {
-                p.part[((size_t)ks * T + tok) * N + row] = a;
+              const int row = r0 + rloc[2 * mt + h];
+              if (row < N) {
+                const float a = acc[mt][tg][h];
+                st_y(p->Y, (size_t)tok * N + row, p->bias ? a + __ldg(p->bias + row) : a, p->ydt);
               }
             }
-          }
+        }
       }
-    }
-    if (L.done) {   // publish this unit
+      if (L.ctr) {
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(L.ctr + 4 * ti, 1u);
+      }
+    } else {
+#pragma unroll
+      for (int tg = 0; tg < NTG; ++tg) {
+        const int tok = tg * 4 + t;
+        if (tok < T) {
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int row = r0 + rloc[2 * mt + h];
+              if (row < N) __stcg(p->part + ((size_t)ks * T + tok) * N + row, acc[mt][tg][h]);
+            }
+        }
+      }
       __threadfence();
       __syncwarp();
-      if (lane == 0) atomicAdd(L.done + ti, 1u);
+      unsigned int old = 0;
+      if (lane == 0) old = atomicAdd(p->tcnt + tile, 1u);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old == (unsigned)ksplit - 1) {
+        // last unit of this tile: add the partial sums in k order
+        __threadfence();
+        if (lane == 0) p->tcnt[tile] = 0;   // ready for the next launch
+        const int row = r0 + lane;
+        if (row < N) {
+          const float bv = p->bias ? __ldg(p->bias + row) : 0.f;
+          for (int tok = 0; tok < T; ++tok) {
+            float a = 0.f;
+            for (int k2 = 0; k2 < ksplit; ++k2) a += __ldcg(p->part + ((size_t)k2 * T + tok) * N + row);
+            st_y(p->Y, (size_t)tok * N + row, a + bv, p->ydt);
+          }
+        }
+        if (L.ctr) {
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) atomicAdd(L.ctr + 4 * ti, 1u);
+        }
+      }
     }
   }
-  cpa_wait<0>();
 }
 
-// Activation digits of the pre-converted tasks: one CTA per task.
-template <int T>
-__global__ void __launch_bounds__(256) q4_digits_kernel(const __grid_constant__ TileLaunch L) {
-  const TileTask& p = tile_task(L, blockIdx.x);
-  if (!p.xpre) return;
-  write_digits<T>(p, threadIdx.x, blockDim.x);
-}
-
-// y[t, n] = sum_k part[k][t][n] (+ bias), for k-split tasks.
-__global__ void q4_splitk_reduce_kernel(const float* __restrict__ part, const float* __restrict__ bias,
-                                        void* Y, int ydt, int N, int T, int ksplit) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= N * T) return;
-  const int n = i % N;
-  float a = 0.f;
-  for (int k = 0; k < ksplit; ++k) a += part[(size_t)k * N * T + i];
-  if (bias) a += __ldg(bias + n);
-  st_y(Y, i, a, ydt);
+// Activation blocks of the tasks whose input exists at launch: one CTA per task.
+template <int T, int LB>
+__global__ void __launch_bounds__(256) q4_xblocks_kernel(const __grid_constant__ TileLaunch L) {
+  const TileTask* p = tile_task(L, blockIdx.x);
+  if (!p->xpre) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c = warp; c < p->nchunk; c += blockDim.x >> 5) convert_chunk<T, LB>(p, c, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -548,13 +664,15 @@ int env_int(const char* name, int dflt) {
 
 int lb_for(int gs) { return (gs % 128 == 0) ? 16 : (gs % 64 == 0 ? 8 : 4); }
 
-int stage_bytes(int T, bool asym, int LB) {
-  const int ntg = (T + 3) / 4, nt = 2 * ntg;
-  return 4 * 32 * LB + nt * 32 * 2 * LB + 4 * 32 * 4 + (asym ? 4 * 32 * 4 : 0) + ntg * 32 * 8;
+int warp_bytes(int T, bool asym, int LB) {
+  const int xb = xblock_bytes(T, LB);
+  const int stage = (32 * 4 * LB + xb + 127) & ~127;
+  return 128 + 1024 + (asym ? 1024 : 0) + kD * stage;
 }
 
-size_t digit_bytes(int T, int K, int G) {
-  return (((size_t)3 * T * K + (size_t)8 * T * G) + 127) & ~(size_t)127;
+size_t xblocks_bytes(int T, int K, int gs) {
+  const int LB = lb_for(gs);
+  return (((size_t)K / (8 * LB)) * xblock_bytes(T, LB) + 127) & ~(size_t)127;
 }
 
 struct TileConfig {
@@ -570,10 +688,9 @@ bool shape_ok(int N, int K, int gs) {
 bool make_config(int T, bool asym, int gs, TileConfig& c) {
   const DeviceInfo& di = device_info();
   c.T = T; c.asym = asym; c.LB = lb_for(gs);
-  const size_t per_warp = (size_t)kD * stage_bytes(T, asym, c.LB);
-  const size_t cap = (size_t)env_int("SF_TILE_SMEM_KB", 224) * 1024 < (size_t)di.smem_optin
-                         ? (size_t)env_int("SF_TILE_SMEM_KB", 224) * 1024
-                         : (size_t)di.smem_optin;
+  const size_t per_warp = (size_t)warp_bytes(T, asym, c.LB);
+  size_t cap = (size_t)env_int("SF_TILE_SMEM_KB", 227) * 1024;
+  if (cap > (size_t)di.smem_optin) cap = (size_t)di.smem_optin;
   int wpc = (int)(cap / per_warp);
   const int want = env_int("SF_TILE_WARPS", 16);
   if (wpc > want) wpc = want;
@@ -585,15 +702,66 @@ bool make_config(int T, bool asym, int gs, TileConfig& c) {
   return true;
 }
 
-void fill_task(TileTask& q, int N, int K, int gs, int ksplit) {
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
+              uint64_t stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {stride_bytes};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Groups per unit for a wanted number of k-ranges: whole groups, at least 4
+// (a few segments per unit), in blocks of 4 when the scales come by TMA.
+int groups_per_unit(int G, long long want, bool stma) {
+  if (want < 1) want = 1;
+  int gper = (int)((G + want - 1) / want);
+  if (gper < 4) gper = 4;
+  if (stma) gper = (gper + 3) & ~3;
+  if (gper > G) gper = G;
+  return gper;
+}
+
+// Fills the shape fields and the tensor maps of a task (W, S, Z set).
+int fill_task(TileTask& q, int N, int K, int gs, int T, long long ksplit_want) {
+  const int LB = lb_for(gs);
   q.N = N; q.K = K; q.G = K / gs; q.lg2gs = __builtin_ctz((unsigned)gs);
   q.ntile = (N + kUnitRows - 1) / kUnitRows;
-  const int G = K / gs;
-  if (ksplit < 1) ksplit = 1;
-  if (ksplit > G) ksplit = G;
-  const int gper = (G + ksplit - 1) / ksplit;
+  const int G = q.G;
+  q.stma = (G % 4 == 0) && ((reinterpret_cast<uintptr_t>(q.S) | reinterpret_cast<uintptr_t>(q.Z)) & 15) == 0;
+  const int gper = groups_per_unit(G, ksplit_want, q.stma != 0);
   q.kper = gper * gs;
   q.ksplit = (G + gper - 1) / gper;
+  q.nchunk = (T * (K / 8) + 31) / 32;
+  if (!make_map(&q.tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, q.W, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                (uint32_t)(4 * LB), kUnitRows))
+    return fail(SF_ERR_CUDA, "cuTensorMapEncodeTiled failed for the weights (N=%d K=%d)", N, K);
+  if (q.stma) {
+    if (!make_map(&q.tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, q.S, (uint64_t)G, (uint64_t)N, (uint64_t)G * 4, 4,
+                  kUnitRows))
+      return fail(SF_ERR_CUDA, "cuTensorMapEncodeTiled failed for the scales");
+    if (q.Z && !make_map(&q.tmZ, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, q.Z, (uint64_t)G, (uint64_t)N,
+                         (uint64_t)G * 4, 4, kUnitRows))
+      return fail(SF_ERR_CUDA, "cuTensorMapEncodeTiled failed for the zeros");
+  }
+  return SF_OK;
 }
 
 template <int T, bool ASYM, int LB>
@@ -645,58 +813,88 @@ cudaError_t launch_tile(const TileConfig& c, const TileLaunch& L, bool coop, cud
   return launch_tile_lb<false, 4>(c, L, coop, st);
 }
 
-cudaError_t launch_digits(int T, int ntasks, const TileLaunch& L, cudaStream_t st) {
+template <int LB>
+cudaError_t launch_xblocks_lb(int T, int ntasks, const TileLaunch& L, cudaStream_t st) {
   switch (T) {
-    case 1: q4_digits_kernel<1><<<ntasks, 256, 0, st>>>(L); break;
-    case 2: q4_digits_kernel<2><<<ntasks, 256, 0, st>>>(L); break;
-    case 3: q4_digits_kernel<3><<<ntasks, 256, 0, st>>>(L); break;
-    case 4: q4_digits_kernel<4><<<ntasks, 256, 0, st>>>(L); break;
-    case 5: q4_digits_kernel<5><<<ntasks, 256, 0, st>>>(L); break;
-    case 6: q4_digits_kernel<6><<<ntasks, 256, 0, st>>>(L); break;
-    case 7: q4_digits_kernel<7><<<ntasks, 256, 0, st>>>(L); break;
-    default: q4_digits_kernel<8><<<ntasks, 256, 0, st>>>(L); break;
+    case 1: q4_xblocks_kernel<1, LB><<<ntasks, 256, 0, st>>>(L); break;
+    case 2: q4_xblocks_kernel<2, LB><<<ntasks, 256, 0, st>>>(L); break;
+    case 3: q4_xblocks_kernel<3, LB><<<ntasks, 256, 0, st>>>(L); break;
+    case 4: q4_xblocks_kernel<4, LB><<<ntasks, 256, 0, st>>>(L); break;
+    case 5: q4_xblocks_kernel<5, LB><<<ntasks, 256, 0, st>>>(L); break;
+    case 6: q4_xblocks_kernel<6, LB><<<ntasks, 256, 0, st>>>(L); break;
+    case 7: q4_xblocks_kernel<7, LB><<<ntasks, 256, 0, st>>>(L); break;
+    default: q4_xblocks_kernel<8, LB><<<ntasks, 256, 0, st>>>(L); break;
   }
   return cudaGetLastError();
 }
 
-// Library-owned scratch of the single-GEMV entry (activation digits and k-split
-// partial sums), one buffer per (device, stream) so that concurrent streams do
-// not share it.  Grows on demand; never shrinks.
+cudaError_t launch_xblocks(int T, int LB, int ntasks, const TileLaunch& L, cudaStream_t st) {
+  if (LB == 16) return launch_xblocks_lb<16>(T, ntasks, L, st);
+  if (LB == 8) return launch_xblocks_lb<8>(T, ntasks, L, st);
+  return launch_xblocks_lb<4>(T, ntasks, L, st);
+}
+
+// Library-owned scratch of the single-GEMV entry, one pair of buffers per
+// (device, stream) so that concurrent streams never share one:
+//  * per-tile arrival counters, zeroed when allocated and left at zero by the
+//    kernel (the last unit of a tile resets its counter), so they must never
+//    be reused for anything else;
+//  * k-split partial sums and activation blocks.
+// Both grow on demand and never shrink.
 struct Scratch {
-  void* ptr = nullptr;
-  size_t bytes = 0;
+  void* ctr = nullptr;
+  size_t ctr_bytes = 0;
+  void* data = nullptr;
+  size_t data_bytes = 0;
 };
 std::mutex g_scratch_mu;
 std::map<std::pair<int, cudaStream_t>, Scratch> g_scratch;
 
-int get_scratch(cudaStream_t st, size_t bytes, void** out) {
+int grow(cudaStream_t st, void** buf, size_t* have, size_t need, bool zero) {
+  if (*have >= need) return SF_OK;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(st, &cs);
+  if (cs != cudaStreamCaptureStatusNone)
+    return fail(SF_ERR_UNSUPPORTED,
+                "GEMV scratch must grow during stream capture: run the same shape once before capturing");
+  if (*buf) {
+    cudaStreamSynchronize(st);
+    cudaFree(*buf);
+  }
+  *buf = nullptr;
+  *have = 0;
+  const size_t nb = (need + ((size_t)1 << 16) - 1) & ~(((size_t)1 << 16) - 1);
+  cudaError_t e = cudaMalloc(buf, nb);
+  if (e != cudaSuccess) return cuda_fail(e, "allocating GEMV scratch");
+  if (zero) {
+    e = cudaMemset(*buf, 0, nb);
+    if (e != cudaSuccess) return cuda_fail(e, "clearing GEMV scratch");
+  }
+  *have = nb;
+  return SF_OK;
+}
+
+int get_scratch(cudaStream_t st, size_t ctr_bytes, size_t data_bytes, void** ctr, void** data) {
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(g_scratch_mu);
   Scratch& s = g_scratch[{dev, st}];
-  if (s.bytes < bytes) {
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    cudaStreamIsCapturing(st, &cs);
-    if (cs != cudaStreamCaptureStatusNone)
-      return fail(SF_ERR_UNSUPPORTED,
-                  "scratch must grow during stream capture: run the same shape once before capturing");
-    if (s.ptr) cudaFree(s.ptr);
-    s.ptr = nullptr;
-    s.bytes = 0;
-    const size_t nb = (bytes + ((size_t)1 << 20) - 1) & ~(((size_t)1 << 20) - 1);
-    cudaError_t e = cudaMalloc(&s.ptr, nb);
-    if (e != cudaSuccess) return cuda_fail(e, "allocating GEMV scratch");
-    s.bytes = nb;
-  }
-  *out = s.ptr;
+  int rc = grow(st, &s.ctr, &s.ctr_bytes, ctr_bytes, true);
+  if (rc != SF_OK) return rc;
+  rc = grow(st, &s.data, &s.data_bytes, data_bytes, false);
+  if (rc != SF_OK) return rc;
+  *ctr = s.ctr;
+  *data = s.data;
   return SF_OK;
 }
 
+size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
+
 }  // namespace
 
-// One GEMV (T <= 8): digits pre-pass, tile kernel with a k-split sized to fill
-// the GPU, then a reduce when the k-split is > 1.  SF_ERR_UNSUPPORTED when the
-// shape is not one this kernel takes.
+// One GEMV (T <= 8): activation-block pre-pass, then the tile kernel with a
+// k-split sized to give every warp of the GPU about one unit.
+// SF_ERR_UNSUPPORTED when the shape is not one this kernel takes.
 int run_tile_linear(const uint8_t* W, const float* S, const float* Z, const float* bias,
                     const void* X, int xdt, void* Y, int ydt, int N, int K, int T, int gs,
                     cudaStream_t stream) {
@@ -708,32 +906,33 @@ int run_tile_linear(const uint8_t* W, const float* S, const float* Z, const floa
   q.W = W; q.S = S; q.Z = Z; q.bias = bias; q.X = X; q.Y = Y; q.xdt = xdt; q.ydt = ydt;
   const int ntile = (N + kUnitRows - 1) / kUnitRows;
   const int warps = c.grid * c.wpc;
-  fill_task(q, N, K, gs, (warps + ntile - 1) / ntile);
-  const size_t dbytes = digit_bytes(T, K, K / gs);
-  const size_t pbytes = q.ksplit > 1 ? (size_t)q.ksplit * T * N * 4 : 0;
-  void* scr = nullptr;
-  int rc = get_scratch(stream, dbytes + pbytes, &scr);
+  int rc = fill_task(q, N, K, gs, T, (warps + ntile - 1) / ntile);
   if (rc != SF_OK) return rc;
-  q.xd = static_cast<uint8_t*>(scr);
-  q.part = pbytes ? reinterpret_cast<float*>(static_cast<uint8_t*>(scr) + dbytes) : nullptr;
+  const size_t cbytes = align256((size_t)q.ntile * 4);
+  const size_t pbytes = q.ksplit > 1 ? align256((size_t)q.ksplit * T * N * 4) : 0;
+  const size_t xbytes = xblocks_bytes(T, K, gs);
+  void* cscr = nullptr;
+  void* dscr = nullptr;
+  rc = get_scratch(stream, cbytes, pbytes + xbytes, &cscr, &dscr);
+  if (rc != SF_OK) return rc;
+  uint8_t* base = static_cast<uint8_t*>(dscr);
+  q.tcnt = static_cast<unsigned int*>(cscr);
+  q.part = pbytes ? reinterpret_cast<float*>(base) : nullptr;
+  q.xd = base + pbytes;
   q.xpre = 1;
   q.ubase = 0;
+  q.wait_from = q.wait_to = 0;
   L.tasks = nullptr; L.ntasks = 1; L.total = (long long)q.ntile * q.ksplit;
-  L.done = nullptr; L.xflag = nullptr;
+  L.ctr = nullptr;
+  L.prefetch = 0;
+  L.dbg = 0;
   const int need = (int)((L.total + c.wpc - 1) / c.wpc);
   if (c.grid > need) c.grid = need;
-  cudaError_t e = launch_digits(T, 1, L, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "activation digits launch");
+  cudaError_t e = launch_xblocks(T, c.LB, 1, L, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "activation pre-pass launch");
   e = launch_tile(c, L, false, stream);
   if (e != cudaSuccess) return cuda_fail(e, "q4_tile_kernel launch");
   g_launches.fetch_add(2, std::memory_order_relaxed);
-  if (q.ksplit > 1) {
-    const int n = N * T;
-    q4_splitk_reduce_kernel<<<(n + 255) / 256, 256, 0, stream>>>(q.part, bias, Y, ydt, N, T, q.ksplit);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "k-split reduce launch");
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-  }
   return SF_OK;
 }
 
@@ -745,55 +944,95 @@ int run_tile_linear(const uint8_t* W, const float* S, const float* Z, const floa
 using namespace sf;
 
 namespace {
-// workspace: [done counters | ready flags] (256-aligned) [task table] [digit arena]
-size_t step_header(int n) { return ((size_t)8 * (n > 0 ? n : 0) + 255) & ~(size_t)255; }
-size_t step_table(int n) { return (size_t)(n > 0 ? n : 0) * sizeof(TileTask); }
+// Workspace: [per-task counters: 4 x u32 | per-tile arrival counters] (both
+// cleared before every run) [task table] [k-split partials] [activation blocks].
+struct StepSizes {
+  size_t ctr, tiles, table, part, xblk;
+  size_t total() const { return ctr + tiles + table + part + xblk; }
+};
+
+// k-splits of a task list: each phase (a run of tasks that need not wait for
+// one another) is cut into about `units_per_warp` units per warp of the grid.
+std::vector<int> plan_ksplit(const sf_q4_task* tasks, int n, int warps) {
+  std::vector<int> ks(n, 1);
+  const int upw = env_int("SF_TILE_UNITS_PER_WARP", 1);
+  int i = 0;
+  while (i < n) {
+    int j = i + 1;
+    while (j < n && !tasks[j].wait_before) ++j;
+    long long tiles = 0;
+    for (int k = i; k < j; ++k) tiles += (tasks[k].N + kUnitRows - 1) / kUnitRows;
+    const long long want = tiles > 0 ? ((long long)warps * upw + tiles - 1) / tiles : 1;
+    for (int k = i; k < j; ++k) {
+      const int G = tasks[k].K / tasks[k].group_size;
+      const bool stma = G % 4 == 0 &&
+                        ((reinterpret_cast<uintptr_t>(tasks[k].scales) |
+                          reinterpret_cast<uintptr_t>(tasks[k].zeros)) & 15) == 0;
+      const int gper = groups_per_unit(G, want, stma);
+      ks[k] = (G + gper - 1) / gper;
+    }
+    i = j;
+  }
+  return ks;
+}
+
+StepSizes step_sizes(const sf_q4_task* tasks, int n, const std::vector<int>& ksplit) {
+  StepSizes z{};
+  z.ctr = align256((size_t)16 * n);
+  size_t tiles = 0, part = 0, xb = 0;
+  for (int i = 0; i < n; ++i) {
+    const sf_q4_task& a = tasks[i];
+    const int ntile = (a.N + kUnitRows - 1) / kUnitRows;
+    tiles += (size_t)ntile * 4;
+    if (ksplit[i] > 1) part += align256((size_t)ksplit[i] * a.T * a.N * 4);
+    xb += xblocks_bytes(a.T, a.K, a.group_size);
+  }
+  z.tiles = align256(tiles);
+  z.table = align256((size_t)n * sizeof(TileTask));
+  z.part = part;
+  z.xblk = xb;
+  return z;
+}
 
 struct StepHandle {
   TileConfig cfg;
   TileLaunch L;
   void* workspace;
+  size_t clear_bytes;
   bool coop, prepass;
 };
+
+bool step_config(const sf_q4_task* tasks, TileConfig& c) {
+  return make_config(tasks[0].T, tasks[0].zeros != nullptr, tasks[0].group_size, c);
+}
 }  // namespace
 
 extern "C" {
 
 size_t sf_q4_step_workspace_bytes(const sf_q4_task* tasks, int ntasks) {
   if (!tasks || ntasks < 1) return 0;
-  size_t n = step_header(ntasks) + ((step_table(ntasks) + 127) & ~(size_t)127);
-  for (int i = 0; i < ntasks; ++i) {
-    const sf_q4_task& a = tasks[i];
-    const int G = a.group_size > 0 ? a.K / a.group_size : 0;
-    n += digit_bytes(a.T, a.K, G);
-  }
-  return n;
+  for (int i = 0; i < ntasks; ++i)
+    if (tasks[i].T < 1 || tasks[i].T > kMaxGemvT || !shape_ok(tasks[i].N, tasks[i].K, tasks[i].group_size))
+      return 0;
+  TileConfig c;
+  if (!step_config(tasks, c)) return 0;
+  return step_sizes(tasks, ntasks, plan_ksplit(tasks, ntasks, c.grid * c.wpc)).total();
 }
 
 int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size_t workspace_bytes,
                       void** handle_out) {
   if (!tasks || !workspace || !handle_out) return fail(SF_ERR_NULL, "null pointer argument");
   if (ntasks < 1) return fail(SF_ERR_SHAPE, "ntasks must be >= 1");
-  const size_t need = sf_q4_step_workspace_bytes(tasks, ntasks);
-  if (workspace_bytes < need) return fail(SF_ERR_SHAPE, "workspace too small: need %zu bytes", need);
   if (reinterpret_cast<uintptr_t>(workspace) & 255)
     return fail(SF_ERR_ALIGN, "workspace must be 256-byte aligned");
   const int T = tasks[0].T;
   const bool asym = tasks[0].zeros != nullptr;
   if (T < 1 || T > kMaxGemvT) return fail(SF_ERR_UNSUPPORTED, "step tasks need 1 <= T <= %d", kMaxGemvT);
-  TileConfig c;
-  if (!make_config(T, asym, tasks[0].group_size, c))
-    return fail(SF_ERR_UNSUPPORTED, "no launch configuration for T=%d", T);
-  std::vector<TileTask> h(ntasks);
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  size_t arena = step_header(ntasks) + ((step_table(ntasks) + 127) & ~(size_t)127);
-  long long ub = 0;
-  int phase = 0, prev_phase = 0;   // first task of the current / previous phase
-  bool any_wait = false, any_pre = false;
   for (int i = 0; i < ntasks; ++i) {
     const sf_q4_task& a = tasks[i];
     if (!a.W || !a.scales || !a.X || !a.Y) return fail(SF_ERR_NULL, "task %d: null pointer", i);
-    if (a.T != T || (a.zeros != nullptr) != asym || lb_for(a.group_size) != c.LB)
+    if (a.T != T || (a.zeros != nullptr) != asym || a.group_size <= 0 ||
+        lb_for(a.group_size) != lb_for(tasks[0].group_size))
       return fail(SF_ERR_UNSUPPORTED, "task %d: all tasks need the same T, layout and group class", i);
     if (!shape_ok(a.N, a.K, a.group_size))
       return fail(SF_ERR_UNSUPPORTED, "task %d: shape N=%d K=%d gs=%d not supported by the step kernel",
@@ -803,14 +1042,40 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
     if ((reinterpret_cast<uintptr_t>(a.W) | reinterpret_cast<uintptr_t>(a.scales) |
          reinterpret_cast<uintptr_t>(a.zeros) | reinterpret_cast<uintptr_t>(a.X)) & 15)
       return fail(SF_ERR_ALIGN, "task %d: W, scales, zeros and X must be 16-byte aligned", i);
+  }
+  TileConfig c;
+  if (!step_config(tasks, c)) return fail(SF_ERR_UNSUPPORTED, "no launch configuration for T=%d", T);
+  const std::vector<int> want = plan_ksplit(tasks, ntasks, c.grid * c.wpc);
+  const StepSizes z = step_sizes(tasks, ntasks, want);
+  if (workspace_bytes < z.total())
+    return fail(SF_ERR_SHAPE, "workspace too small: need %zu bytes", z.total());
+
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint8_t* tiles = ws + z.ctr;
+  uint8_t* table = tiles + z.tiles;
+  uint8_t* part = table + z.table;
+  uint8_t* xblk = part + z.part;
+  std::vector<TileTask> h(ntasks);
+  long long ub = 0;
+  int phase = 0, prev_phase = 0;   // first task of the current / previous phase
+  bool any_wait = false, any_pre = false;
+  for (int i = 0; i < ntasks; ++i) {
+    const sf_q4_task& a = tasks[i];
     TileTask& q = h[i];
     q = TileTask{};
     q.W = a.W; q.S = a.scales; q.Z = a.zeros; q.bias = a.bias; q.X = a.X; q.Y = a.Y;
     q.xdt = a.x_dtype; q.ydt = a.y_dtype;
-    fill_task(q, a.N, a.K, a.group_size, 1);
+    int rc = fill_task(q, a.N, a.K, a.group_size, T, want[i]);
+    if (rc != SF_OK) return rc;
+    q.tcnt = reinterpret_cast<unsigned int*>(tiles);
+    tiles += (size_t)q.ntile * 4;
     q.part = nullptr;
-    q.xd = ws + arena;
-    arena += digit_bytes(T, q.K, q.G);
+    if (q.ksplit > 1) {
+      q.part = reinterpret_cast<float*>(part);
+      part += align256((size_t)q.ksplit * T * a.N * 4);
+    }
+    q.xd = xblk;
+    xblk += xblocks_bytes(T, a.K, a.group_size);
     // A task with wait_before opens a phase; every task of a phase reads X only
     // after the whole previous phase has finished (and, transitively, all
     // earlier ones).  Only phase-0 inputs exist before the launch.
@@ -829,16 +1094,17 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
   StepHandle* hd = new StepHandle{};
   hd->cfg = c;
   hd->workspace = workspace;
+  hd->clear_bytes = z.ctr + z.tiles;
   hd->coop = any_wait;
   hd->prepass = any_pre;
   TileLaunch& L = hd->L;
-  L.tasks = reinterpret_cast<const TileTask*>(ws + step_header(ntasks));
+  L.tasks = reinterpret_cast<const TileTask*>(table);
   L.ntasks = ntasks;
   L.total = ub;
-  L.done = reinterpret_cast<unsigned int*>(ws);
-  L.xflag = L.done + ntasks;
-  cudaError_t e = cudaMemcpy(const_cast<TileTask*>(L.tasks), h.data(), step_table(ntasks),
-                             cudaMemcpyHostToDevice);
+  L.ctr = reinterpret_cast<unsigned int*>(ws);
+  L.prefetch = env_int("SF_TILE_PREFETCH", 1);
+  L.dbg = env_int("SF_TILE_DBG", 0);
+  cudaError_t e = cudaMemcpy(table, h.data(), (size_t)ntasks * sizeof(TileTask), cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
     delete hd;
     return cuda_fail(e, "uploading the task table");
@@ -851,11 +1117,11 @@ int sf_q4_step_run(void* handle, void* stream) {
   if (!handle) return fail(SF_ERR_NULL, "null handle");
   StepHandle* hd = static_cast<StepHandle*>(handle);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(hd->workspace, 0, step_header(hd->L.ntasks), st);
-  if (e != cudaSuccess) return cuda_fail(e, "clearing the completion counters");
+  cudaError_t e = cudaMemsetAsync(hd->workspace, 0, hd->clear_bytes, st);
+  if (e != cudaSuccess) return cuda_fail(e, "clearing the step counters");
   if (hd->prepass) {
-    e = launch_digits(hd->cfg.T, hd->L.ntasks, hd->L, st);
-    if (e != cudaSuccess) return cuda_fail(e, "activation digits launch");
+    e = launch_xblocks(hd->cfg.T, hd->cfg.LB, hd->L.ntasks, hd->L, st);
+    if (e != cudaSuccess) return cuda_fail(e, "activation pre-pass launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);
   }
   e = launch_tile(hd->cfg, hd->L, hd->coop, st);
