@@ -11,8 +11,8 @@
 //    (u ^ 8 = q + 8) by the LOP3 that masks them, so both layouts become
 //    s * (sum u*x - zeff * sum x) with zeff = 8 (sym) or z (asym);
 //  * activations: per (token, group) x_fix = rint(x * 2^(22-E)), E the binary
-//    exponent of the group's max |x|, split into three signed int8 digits
-//    (x_fix = d0 + 256 d1 + 65536 d2);
+//    exponent of the group's max |x| (the grid step is 2^-22 of the group
+//    max), split into three signed int8 digits (x_fix = d0 + 256 d1 + 65536 d2);
 //  * mma.sync m16n8k32 u8 x s8 -> s32 sums u*d exactly; one fp32 epilogue per
 //    (row, group, token) recombines the digits, removes zeff * sum(x_fix) and
 //    applies s * 2^(E-22).
@@ -63,30 +63,44 @@ SF_DEFINE_ERROR_READER(take_dev_error_tile)
 
 namespace {
 
-constexpr int kD = 4;                  // stages per warp ring
-constexpr int kTileMaxThreads = 512;
+constexpr int kD = 3;                  // stages per warp ring
 constexpr int kUnitRows = 32;          // rows per unit (two m16 tiles)
-// More than 4 tokens doubles the accumulators; those launches hold at most 8
-// warps (their stages are larger) and get 255 registers per thread instead.
-__host__ __device__ constexpr int tile_max_threads(int T) { return T > 4 ? 256 : kTileMaxThreads; }
+// At most 12 warps per CTA (168 registers per thread); more than 4 tokens
+// doubles the accumulators, and those launches hold at most 8 warps (their
+// stages are larger) with 255 registers per thread.
+__host__ __device__ constexpr int tile_max_threads(int T) { return T > 4 ? 256 : 384; }
 
 // Bytes of one segment's activation block: [T][3 digits][4 lanes][2*LB] digit
 // bytes, then [T] x (group scale 2^(E-22), sum of x_fix) as two fp32.
 __host__ __device__ constexpr int xblock_bytes(int T, int LB) { return (T * (24 * LB + 8) + 15) & ~15; }
 
-// Shared-memory layout of one warp's region.
+// Shared memory of a CTA: first the weight stages of every warp (1024-byte
+// aligned, as the 128-byte TMA swizzle needs), then each warp's other areas.
+// One stage = 32 rows x 128 bytes of W (256 k) = SPS k-segments of 8*LB k.
 template <int T, bool ASYM, int LB>
-struct WarpLayout {
-  static constexpr int BAR = 0;                       // kD mbarriers
-  static constexpr int ZERO = 64;                     // 64 zero bytes (B fragment of absent columns)
-  static constexpr int SRING = 128;                   // 2 x [32 rows][4 groups] fp32 scales
-  static constexpr int ZRING = SRING + 1024;          // same for zeros (asym)
-  static constexpr int STAGES = ZRING + (ASYM ? 1024 : 0);
-  static constexpr int ABYTES = 32 * 4 * LB;          // [32 rows][SEGK/2 bytes]
-  static constexpr int XB = xblock_bytes(T, LB);
-  static constexpr int STAGE = (ABYTES + XB + 127) & ~127;
-  static constexpr int BYTES = STAGES + kD * STAGE;
+struct TileLayout {
+  static constexpr int SPS = 128 / (4 * LB);            // k-segments per stage
+  static constexpr int XB = xblock_bytes(T, LB);         // activation block of one segment
+  static constexpr int ASTAGE = 32 * 128;                // weight tile of one stage
+  static constexpr int SBW = LB == 4 ? 8 : 4;            // groups in one stage's scale box
+  static constexpr int SBYTES = 32 * SBW * 4;            // [32 rows][SBW] fp32
+  static constexpr int XSTAGE = (SPS * XB + 127) & ~127;
+  // per-warp area: [mbarriers 64 B][zeros 64 B][kD x activations][kD x scales][kD x zeros]
+  static constexpr int XOFF = 128;
+  static constexpr int SOFF = XOFF + kD * XSTAGE;
+  static constexpr int ZOFF = SOFF + kD * SBYTES;
+  static constexpr int MISC = ZOFF + (ASYM ? kD * SBYTES : 0);
+  static constexpr int WARP = kD * ASTAGE + MISC;        // shared bytes per warp
 };
+
+// Rows of a 32-row unit held by lane group g (slot i: tile i>>1, +8 when i is
+// odd).  With 128-byte swizzled rows (16-byte chunk c of row r stored at
+// c ^ (r & 7)), the rows that one shared-memory phase of fragment loads reads
+// must land on different banks: for LB=16 the two rows of a phase differ in
+// bit 2, for LB=8 the four rows differ in bits 1-2, for LB=4 any order works.
+__device__ __forceinline__ int lane_row(int g, int LB) {
+  return LB == 16 ? ((g >> 1) | ((g & 1) << 2)) : (LB == 8 ? (((g & 3) << 1) | (g >> 2)) : g);
+}
 
 // One GEMV of a launch.  The tensor maps come first (64-byte aligned).
 struct alignas(64) TileTask {
@@ -106,19 +120,24 @@ struct alignas(64) TileTask {
   int N, K, G, lg2gs, xdt, ydt;
   int ntile, ksplit, kper;   // 32-row tiles, k-splits, k per split (whole groups)
   int xpre;                  // activation blocks were written by the pre-pass
-  int wait_from, wait_to;    // tasks [wait_from, wait_to) finish before this one reads X
   int stma;                  // scales (and zeros) by TMA; else per-lane copies
   int nchunk;                // 32-octet conversion chunks
+  // Phase of this task: a run of tasks that read X only after the previous
+  // phase has written all its tiles.  Phase 0 reads inputs that exist at launch.
+  int phase, ph_first, ph_tiles, ph_chunks, ph_last;
+  long long ph_ubase, ph_units;
 };
 
 struct TileLaunch {
   TileTask single;        // used when `tasks` is null
   const TileTask* tasks;  // device table
-  unsigned int* ctr;      // per task: [units done, chunks claimed, chunks done, -] or null
+  unsigned int* phctr;    // per phase: [tiles written, chunks converted, -, -] or null
+  unsigned int* flags;    // per CTA, one 128-byte line: [phases written, phases converted]
   long long total;        // units in the launch
   int ntasks;
   int prefetch;           // pull a waiting unit's weights into L2 before the wait
   int dbg;                // development: 2 = copies only, 3 = arithmetic only (wrong results)
+  unsigned long long* trace;   // development: per unit [start, dependency met, inputs ready, end] ns
 };
 
 __device__ __forceinline__ const TileTask* tile_task(const TileLaunch& L, int i) {
@@ -304,10 +323,12 @@ __device__ __forceinline__ void digits8(const float* v, int lpg, uint2* dig, flo
     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
     bad |= __shfl_xor_sync(0xffffffffu, bad, off);
   }
-  // biased binary exponent of the group max; groups below 2^-105 are zero
+  // biased binary exponent `be` of the group max m: m < 2^(be-126), so
+  // x * 2^(148-be) stays within +-2^22 and splits into three int8 digits.
+  // Groups whose max is below 2^-105 are zero.
   const int be = (int)(__float_as_uint(m) >> 23);
   const bool zero = bad || be < 22;
-  const float scl = zero ? 0.f : __uint_as_float((uint32_t)(275 - be) << 23);   // 2^(22-E)
+  const float scl = zero ? 0.f : __uint_as_float((uint32_t)(275 - be) << 23);   // 2^(148-be)
   int d[3][8];
   int s = 0;
 #pragma unroll
@@ -326,7 +347,7 @@ __device__ __forceinline__ void digits8(const float* v, int lpg, uint2* dig, flo
   dig[1] = pack_digits(d[1]);
   dig[2] = pack_digits(d[2]);
   gsc_out = bad ? __int_as_float(0x7fc00000)
-                : (zero ? 0.f : __uint_as_float((uint32_t)(be - 21) << 23));   // 2^(E-22)
+                : (zero ? 0.f : __uint_as_float((uint32_t)(be - 21) << 23));   // 2^(be-148)
   sum_out = s;
 }
 
@@ -370,6 +391,25 @@ __device__ __forceinline__ void convert_chunk(const TileTask* p, int c, int lane
   }
 }
 
+// Writes `val` into word `word` of every CTA's flag line (whole warp).
+__device__ __forceinline__ void publish(unsigned int* flags, int word, unsigned int val, int lane) {
+  __threadfence();
+  for (int c = lane; c < (int)gridDim.x; c += 32)
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(flags + c * 32 + word), "r"(val) : "memory");
+}
+
+// A 32-row tile of task p has been written (whole warp): count it towards its
+// phase; the tile that completes the phase tells every CTA.
+__device__ __forceinline__ void tile_written(const TileLaunch& L, const TileTask* p, int lane) {
+  if (!L.phctr || p->ph_last) return;
+  __threadfence();
+  __syncwarp();
+  unsigned int old = 0;
+  if (lane == 0) old = atomicAdd(L.phctr + 4 * p->phase, 1u);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  if (old + 1 == (unsigned)p->ph_tiles) publish(L.flags, 0, (unsigned)p->phase + 1, lane);
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -378,16 +418,25 @@ __device__ __forceinline__ void convert_chunk(const TileTask* p, int c, int lane
 template <int T, bool ASYM, int LB>
 __global__ void __launch_bounds__(tile_max_threads(T), 1)
     q4_tile_kernel(const __grid_constant__ TileLaunch L) {
-  using Ly = WarpLayout<T, ASYM, LB>;
-  constexpr int NTG = (T + 3) / 4, NT = 2 * NTG, WPL = LB / 4, SEGK = 8 * LB, ROWB = 4 * LB;
-  constexpr int XOFF = Ly::ABYTES;               // activation block inside a stage
-  constexpr int GOFF = XOFF + T * 24 * LB;       // group scales / sums inside the block
-  extern __shared__ __align__(128) uint8_t smem[];
+  using Ly = TileLayout<T, ASYM, LB>;
+  // n tiles: T <= 2 packs all 3T digit columns into one tile; otherwise tile
+  // pair (2 tg, 2 tg + 1) holds digits (0, 1) and digit 2 of tokens 4 tg .. 4 tg + 3
+  constexpr bool CMP = T <= 2;
+  constexpr int NTG = (T + 3) / 4, NT = CMP ? 1 : 2 * NTG, WPL = LB / 4, SEGK = 8 * LB, SPS = Ly::SPS;
+  constexpr int GOFF = T * 24 * LB;              // group scales / sums inside a segment's block
+  extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const uint32_t wb = (uint32_t)__cvta_generic_to_shared(smem) + (uint32_t)warp * Ly::BYTES;
-  const uint32_t bar0 = wb + Ly::BAR, zblk = wb + Ly::ZERO, sring = wb + Ly::SRING,
-                 zring = wb + Ly::ZRING, stage0 = wb + Ly::STAGES;
+  const int wpc = blockDim.x >> 5;
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem);
+  if (sbase & 1023) {   // the swizzled TMA tiles need 1024-byte alignment
+    if (threadIdx.x == 0) atomicOr(&g_dev_error, 0x800u);
+    return;
+  }
+  const uint32_t astage0 = sbase + (uint32_t)warp * kD * Ly::ASTAGE;
+  const uint32_t wb = sbase + (uint32_t)wpc * kD * Ly::ASTAGE + (uint32_t)warp * Ly::MISC;
+  const uint32_t bar0 = wb, zblk = wb + 64, xstage0 = wb + Ly::XOFF, sstage0 = wb + Ly::SOFF,
+                 zstage0 = wb + Ly::ZOFF;
 
   if (lane < kD) bar_init(bar0 + lane * 8, 33);   // lane 0's expect_tx + 32 cp.async arrivals
   if (lane < 16) asm volatile("st.shared.u32 [%0], %1;" ::"r"(zblk + lane * 4), "r"(0u) : "memory");
@@ -396,19 +445,37 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
   __syncwarp();
 
   // B fragment sources: column g of tile nt is (token, digit) or absent.
+  // Accumulator columns 2t, 2t+1 of a lane are then digits 0 and 1 of token
+  // t (of its group of four); digit 2 sits in the odd tile at column 2t or,
+  // in the packed layout (T <= 2), at column 2T + t of another lane.
   int bslot[NT];
   bool bval[NT];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    const int tok = (nt >> 1) * 4 + (g >> 1);
-    const int dg = (nt & 1) ? ((g & 1) ? -1 : 2) : (g & 1);
-    bval[nt] = tok < T && dg >= 0;
+    int tok, dg;
+    if (CMP) {
+      tok = g < 2 * T ? (g >> 1) : g - 2 * T;
+      dg = g < 2 * T ? (g & 1) : 2;
+      bval[nt] = g < 3 * T;
+    } else {
+      tok = (nt >> 1) * 4 + (g >> 1);
+      dg = (nt & 1) ? ((g & 1) ? -1 : 2) : (g & 1);
+      bval[nt] = tok < T && dg >= 0;
+    }
     bslot[nt] = bval[nt] ? ((tok * 3 + dg) * 4 + t) * 2 * LB : 0;
   }
-  // rows of this lane inside a unit: slot i -> tile (i>>1), row g (+8 when i odd)
+  // rows of this lane inside a unit and their byte offsets in a swizzled stage
   int rloc[4];
+  uint32_t aoff[4][SPS];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) rloc[i] = (i >> 1) * 16 + g + 8 * (i & 1);
+  for (int i = 0; i < 4; ++i) {
+    rloc[i] = (i >> 1) * 16 + lane_row(g, LB) + 8 * (i & 1);
+#pragma unroll
+    for (int sub = 0; sub < SPS; ++sub) {
+      const int b = sub * 4 * LB + t * LB;   // byte of the row this lane reads for segment `sub`
+      aoff[i][sub] = (uint32_t)(rloc[i] * 128 + ((((b >> 4) ^ (rloc[i] & 7)) << 4) | (b & 15)));
+    }
+  }
 
   const long long W_all = (long long)gridDim.x * (blockDim.x >> 5);
   uint32_t gseg = 0;   // segments this warp has consumed (ring position and phase)
@@ -430,8 +497,11 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     const int lg2spg = lg2gs - (31 - __clz(SEGK));   // segments per group = 1 << lg2spg
     const int spg_mask = (1 << lg2spg) - 1;
 
+    unsigned long long* tr = L.trace ? L.trace + 4 * u : nullptr;
+    if (tr && lane == 0) tr[0] = globaltimer_ns();
     // ---- dependencies and activation blocks --------------------------------
-    if (p->wait_to > p->wait_from) {
+    if (p->phase > 0) {
+      const int ph = p->phase;
       if (L.prefetch) {
         // The weights do not depend on earlier tasks: start them towards L2
         // now, so that the wait overlaps with HBM traffic.
@@ -442,66 +512,82 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
           prefetch_l2(p->W + (size_t)(r0 + lane) * (K >> 1) + (kb >> 1), (uint32_t)(ke - kb) >> 1);
         }
       }
+      const unsigned int* fl = L.flags + blockIdx.x * 32;
       int okw = 1;
-      if (lane == 0)
-        for (int i = p->wait_from; i < p->wait_to && okw; ++i)
-          okw = spin_geq(L.ctr + 4 * i, (unsigned)tile_task(L, i)->ntile, 0x200u);
+      if (lane == 0) okw = spin_geq(fl, (unsigned)ph, 0x200u);   // previous phase written
       ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
       if (!ok) break;
-    }
-    if (!p->xpre) {
-      // convert whatever chunks no other warp has claimed, then wait for all
-      unsigned int* xc = L.ctr + 4 * ti;
-      const int nch = p->nchunk;
-      while (true) {
-        int c = 0;
-        if (lane == 0) c = (int)atomicAdd(xc + 1, 1u);
-        c = __shfl_sync(0xffffffffu, c, 0);
-        if (c >= nch) break;
-        convert_chunk<T, LB>(p, c, lane);
+      if (tr && lane == 0) tr[1] = globaltimer_ns();
+      // The first units of the phase convert its inputs: unit i takes chunks
+      // i, i + CS, ... over all tasks of the phase.  Every warp has at most
+      // one such unit per phase and reaches it before any other unit of the
+      // phase, so no converting warp waits on its own conversion.
+      const long long CS = min(W_all, p->ph_units);
+      const long long i = u - p->ph_ubase;
+      if (i < CS && i < p->ph_chunks) {
+        int n = 0, tj = p->ph_first, cbase = 0;
+        for (long long c = i; c < p->ph_chunks; c += CS) {
+          while (c - cbase >= tile_task(L, tj)->nchunk) cbase += tile_task(L, tj++)->nchunk;
+          convert_chunk<T, LB>(tile_task(L, tj), (int)(c - cbase), lane);
+          ++n;
+        }
         asm volatile("fence.proxy.async.global;" ::: "memory");
         __threadfence();
         __syncwarp();
-        if (lane == 0) atomicAdd(xc + 2, 1u);
+        unsigned int old = 0;
+        if (lane == 0) old = atomicAdd(L.phctr + 4 * ph + 1, (unsigned)n);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old + n == (unsigned)p->ph_chunks) publish(L.flags, 1, (unsigned)ph + 1, lane);
       }
       int okx = 1;
       if (lane == 0) {
-        okx = spin_geq(xc + 2, (unsigned)nch, 0x400u);
+        okx = spin_geq(fl + 1, (unsigned)ph + 1, 0x400u);            // this phase's inputs converted
         asm volatile("fence.proxy.async.global;" ::: "memory");
       }
       ok = __shfl_sync(0xffffffffu, okx, 0) != 0;
       if (!ok) break;
     }
 
+    if (tr && lane == 0) tr[2] = globaltimer_ns();
     // ---- operand streaming ---------------------------------------------------
+    // Stage j holds k [kb + 256 j, kb + 256 j + 256): the weight tile, the
+    // activation blocks of its segments and the scale box of its groups.
+    const int nstage = (nseg + SPS - 1) / SPS;
     const uint8_t* xsrc = p->xd + (size_t)(kb / SEGK) * Ly::XB;
     const float* Sb = p->S;
     const float* Zb = p->Z;
-    auto issue = [&](int s) {
+    auto issue = [&](int j) {
       if (L.dbg == 3) return;
-      const uint32_t slot = (gseg + s) % kD;
-      const uint32_t st = stage0 + slot * Ly::STAGE, bar = bar0 + slot * 8;
-      const int gl = s >> lg2spg;                                  // group inside the unit
-      const bool sblk = (s & spg_mask) == 0 && (gl & 3) == 0;      // first segment of a 4-group block
-      const uint32_t soff = (uint32_t)((gl >> 2) & 1) * 512;
+      const uint32_t slot = (gseg + j) % kD;
+      const uint32_t bar = bar0 + slot * 8;
+      const int nsub = min(SPS, nseg - j * SPS);
+      const int fg = (kb + j * 256) >> lg2gs;                   // first group of the stage
+      // scale box origin: TMA boxes start on SBW-group boundaries (units are
+      // cut in whole boxes, so the stage's groups stay inside); per-lane
+      // copies start at the stage's first group
+      const int sx = stma ? (fg & ~(Ly::SBW - 1)) : fg;
       if (lane == 0) {
-        const uint32_t sbytes = (sblk && stma) ? (ASYM ? 1024u : 512u) : 0u;
-        bar_expect_tx(bar, (uint32_t)Ly::ABYTES + Ly::XB + sbytes);
-        tma_2d(st, &p->tmW, (kb >> 1) + s * ROWB, r0, bar);
-        bulk_copy(st + XOFF, xsrc + (size_t)s * Ly::XB, Ly::XB, bar);
-        if (sblk && stma) {
-          tma_2d(sring + soff, &p->tmS, g0 + gl, r0, bar);
-          if (ASYM) tma_2d(zring + soff, &p->tmZ, g0 + gl, r0, bar);
+        const uint32_t sbytes = stma ? (uint32_t)Ly::SBYTES * (ASYM ? 2 : 1) : 0u;
+        bar_expect_tx(bar, (uint32_t)Ly::ASTAGE + nsub * Ly::XB + sbytes);
+        tma_2d(astage0 + slot * Ly::ASTAGE, &p->tmW, (kb >> 1) + j * 128, r0, bar);
+        bulk_copy(xstage0 + slot * Ly::XSTAGE, xsrc + (size_t)j * SPS * Ly::XB, nsub * Ly::XB, bar);
+        if (stma) {
+          tma_2d(sstage0 + slot * Ly::SBYTES, &p->tmS, sx, r0, bar);
+          if (ASYM) tma_2d(zstage0 + slot * Ly::SBYTES, &p->tmZ, sx, r0, bar);
         }
       }
-      if (sblk && !stma) {
-        const int grp = g0 + gl + t;
-        if (grp < gend) {
+      if (!stma) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int row = min(r0 + rloc[i], N - 1);
-            cpa4(sring + soff + rloc[i] * 16 + t * 4, Sb + (size_t)row * G + grp);
-            if (ASYM) cpa4(zring + soff + rloc[i] * 16 + t * 4, Zb + (size_t)row * G + grp);
+        for (int c = t; c < Ly::SBW; c += 4) {
+          const int grp = sx + c;
+          if (grp >= g0 && grp < gend) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int row = min(r0 + rloc[i], N - 1);
+              const uint32_t o = (uint32_t)(rloc[i] * Ly::SBW + c) * 4;
+              cpa4(sstage0 + slot * Ly::SBYTES + o, Sb + (size_t)row * G + grp);
+              if (ASYM) cpa4(zstage0 + slot * Ly::SBYTES + o, Zb + (size_t)row * G + grp);
+            }
           }
         }
       }
@@ -511,72 +597,122 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     __syncwarp();
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 #pragma unroll
-    for (int s = 0; s < kD - 1; ++s)
-      if (s < nseg) issue(s);
+    for (int j = 0; j < kD - 1; ++j)
+      if (j < nstage) issue(j);
 
     float acc[2][NTG][2];
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
       for (int tg = 0; tg < NTG; ++tg) acc[mt][tg][0] = acc[mt][tg][1] = 0.f;
-    int C[2][NT][4];
+    int C[2][2][NT][4];   // [segment of the pair][m tile][n tile][fragment]
 
-    for (int s = 0; s < nseg; ++s) {
-      const uint32_t slot = (gseg + s) % kD;
-      const uint32_t st = stage0 + slot * Ly::STAGE;
-      if (L.dbg != 3 && !bar_wait(bar0 + slot * 8, ((gseg + s) / kD) & 1, 0x10u)) {
+    // epilogue of the group that ends with segment s: recombine the digits,
+    // remove zeff * sum(x), scale.  Lanes whose token does not exist compute
+    // on token T-1 and never store.
+    auto epilogue = [&](const int (&Cs)[2][NT][4], int s, uint32_t xs0, uint32_t sst, uint32_t zst, int sx) {
+      int sc_i = ((kb + s * SEGK) >> lg2gs) - sx;
+      if ((unsigned)sc_i >= (unsigned)Ly::SBW) {   // cannot happen; never read outside the box
+        atomicOr(&g_dev_error, 0x1000u);
+        sc_i = 0;
+      }
+      const uint32_t soff = (uint32_t)sc_i * 4;
+#pragma unroll
+      for (int tg = 0; tg < NTG; ++tg) {
+        const uint2 xv = lds64(xs0 + GOFF + min(tg * 4 + t, T - 1) * 8);
+        const float gsc = __uint_as_float(xv.x), xsum = __uint_as_float(xv.y);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int r = rloc[2 * mt + h];
+            const float sc = __uint_as_float(lds32(sst + r * (Ly::SBW * 4) + soff));
+            const float zp = ASYM ? __uint_as_float(lds32(zst + r * (Ly::SBW * 4) + soff)) : 8.f;
+            const int i01 = Cs[mt][CMP ? 0 : 2 * tg][2 * h] + 256 * Cs[mt][CMP ? 0 : 2 * tg][2 * h + 1];
+            int c2;
+            if (CMP) {
+              // digit 2 of token t is column 2T + t: lane T of the quad, element t
+              const int va = __shfl_sync(0xffffffffu, Cs[mt][0][2 * h], (lane & ~3) | T);
+              const int vb = T == 2 ? __shfl_sync(0xffffffffu, Cs[mt][0][2 * h + 1], (lane & ~3) | T) : va;
+              c2 = t == 1 ? vb : va;
+            } else {
+              c2 = Cs[mt][2 * tg + 1][2 * h];
+            }
+            float f = fmaf(65536.f, (float)c2, (float)i01);
+            f = fmaf(-zp, xsum, f);
+            acc[mt][tg][h] = fmaf(f, sc * gsc, acc[mt][tg][h]);
+          }
+      }
+    };
+
+    for (int j = 0; j < nstage; ++j) {
+      const uint32_t slot = (gseg + j) % kD;
+      const uint32_t ast = astage0 + slot * Ly::ASTAGE, xst = xstage0 + slot * Ly::XSTAGE;
+      const uint32_t sst = sstage0 + slot * Ly::SBYTES, zst = zstage0 + slot * Ly::SBYTES;
+      if (L.dbg != 3 && !bar_wait(bar0 + slot * 8, ((gseg + j) / kD) & 1, 0x10u)) {
         ok = false;
         break;
       }
-      if (L.dbg != 2) {
-        uint32_t w[4][WPL];
+      const int fgj = (kb + j * 256) >> lg2gs;
+      const int sx = stma ? (fgj & ~(Ly::SBW - 1)) : fgj;
+      // The stage's segments are taken in pairs with one accumulator set each,
+      // so that the two halves' loads, nibble splits and MMAs interleave.
 #pragma unroll
-        for (int i = 0; i < 4; ++i) lds_n<LB>(st + rloc[i] * ROWB + t * LB, w[i]);
-        uint32_t bq[NT][2 * WPL];
+      for (int pr = 0; pr < SPS; pr += 2) {
+        const int s0 = j * SPS + pr;
+        if (L.dbg == 2 || s0 >= nseg) break;
+        const bool has1 = s0 + 1 < nseg;
+        uint32_t w[2][4][WPL];
+        uint32_t bq[2][NT][2 * WPL];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) lds_n<2 * LB>(bval[nt] ? st + XOFF + bslot[nt] : zblk, bq[nt]);
-        const bool first = (s & spg_mask) == 0;
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const uint32_t xs0 = xst + (pr + h2) * Ly::XB;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) lds_n<LB>(ast + aoff[i][pr + h2], w[h2][i]);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) lds_n<2 * LB>(bval[nt] ? xs0 + bslot[nt] : zblk, bq[h2][nt]);
+        }
+        // a set starts afresh at its first segment of a group: with one
+        // segment per group both sets always do; with more, each set carries
+        // its half of the group and the two are added at the group's end
+        const bool first0 = (s0 & spg_mask) == 0;
+        const bool first1 = spg_mask == 0 || (s0 & spg_mask) == 0;
 #pragma unroll
         for (int q = 0; q < WPL; ++q)
 #pragma unroll
-          for (int mt = 0; mt < 2; ++mt) {
-            const uint32_t a0 = nib_lo<ASYM>(w[2 * mt][q]), a2 = nib_hi<ASYM>(w[2 * mt][q]);
-            const uint32_t a1 = nib_lo<ASYM>(w[2 * mt + 1][q]), a3 = nib_hi<ASYM>(w[2 * mt + 1][q]);
+          for (int h2 = 0; h2 < 2; ++h2)
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              if (q == 0 && first) imma0(C[mt][nt], a0, a1, a2, a3, bq[nt][0], bq[nt][1]);
-              else imma(C[mt][nt], a0, a1, a2, a3, bq[nt][2 * q], bq[nt][2 * q + 1]);
-            }
-          }
-        if ((s & spg_mask) == spg_mask) {
-          // epilogue of this group: recombine digits, remove zeff * sum(x), scale.
-          // Lanes whose token does not exist compute on token T-1 and never store.
-          const int gl = s >> lg2spg;
-          const uint32_t soff = (uint32_t)((gl >> 2) & 1) * 512 + (gl & 3) * 4;
+            for (int mt = 0; mt < 2; ++mt) {
+              const uint32_t a0 = nib_lo<ASYM>(w[h2][2 * mt][q]), a2 = nib_hi<ASYM>(w[h2][2 * mt][q]);
+              const uint32_t a1 = nib_lo<ASYM>(w[h2][2 * mt + 1][q]), a3 = nib_hi<ASYM>(w[h2][2 * mt + 1][q]);
+              const bool fst = h2 == 0 ? first0 : first1;
 #pragma unroll
-          for (int tg = 0; tg < NTG; ++tg) {
-            const uint2 xv = lds64(st + GOFF + min(tg * 4 + t, T - 1) * 8);
-            const float gsc = __uint_as_float(xv.x), xs = __uint_as_float(xv.y);
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int r = rloc[2 * mt + h];
-                const float sc = __uint_as_float(lds32(sring + soff + r * 16));
-                const float zp = ASYM ? __uint_as_float(lds32(zring + soff + r * 16)) : 8.f;
-                const int i01 = C[mt][2 * tg][2 * h] + 256 * C[mt][2 * tg][2 * h + 1];
-                float f = fmaf(65536.f, (float)C[mt][2 * tg + 1][2 * h], (float)i01);
-                f = fmaf(-zp, xs, f);
-                acc[mt][tg][h] = fmaf(f, sc * gsc, acc[mt][tg][h]);
+              for (int nt = 0; nt < NT; ++nt) {
+                if (q == 0 && fst) imma0(C[h2][mt][nt], a0, a1, a2, a3, bq[h2][nt][0], bq[h2][nt][1]);
+                else imma(C[h2][mt][nt], a0, a1, a2, a3, bq[h2][nt][2 * q], bq[h2][nt][2 * q + 1]);
               }
-          }
+            }
+        // group ends inside the pair: one per segment when a group is one
+        // segment long, else at most one (the odd segment) with the sets summed
+        if (spg_mask == 0) {
+          epilogue(C[0], s0, xst + pr * Ly::XB, sst, zst, sx);
+          if (has1) epilogue(C[1], s0 + 1, xst + (pr + 1) * Ly::XB, sst, zst, sx);
+        } else if (((s0 + 1) & spg_mask) == spg_mask) {
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) C[0][mt][nt][e] += C[1][mt][nt][e];
+          epilogue(C[0], s0 + 1, xst + (pr + 1) * Ly::XB, sst, zst, sx);
         }
       }
       __syncwarp();
-      if (s + kD - 1 < nseg) issue(s + kD - 1);
+      if (j + kD - 1 < nstage) issue(j + kD - 1);
     }
     if (!ok) break;
-    gseg += (uint32_t)nseg;
+    gseg += (uint32_t)nstage;
+    if (tr && lane == 0) tr[3] = globaltimer_ns();
 
     // ---- results ---------------------------------------------------------------
     if (ksplit == 1) {
@@ -596,11 +732,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
             }
         }
       }
-      if (L.ctr) {
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) atomicAdd(L.ctr + 4 * ti, 1u);
-      }
+      tile_written(L, p, lane);
     } else {
 #pragma unroll
       for (int tg = 0; tg < NTG; ++tg) {
@@ -628,16 +760,21 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
         if (row < N) {
           const float bv = p->bias ? __ldg(p->bias + row) : 0.f;
           for (int tok = 0; tok < T; ++tok) {
+            // loads first (eight in flight), then the sum in k order
+            const float* src = p->part + (size_t)tok * N + row;
+            const size_t kstride = (size_t)T * N;
             float a = 0.f;
-            for (int k2 = 0; k2 < ksplit; ++k2) a += __ldcg(p->part + ((size_t)k2 * T + tok) * N + row);
+            for (int kc = 0; kc < ksplit; kc += 8) {
+              float v[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[j] = kc + j < ksplit ? __ldcg(src + (size_t)(kc + j) * kstride) : 0.f;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) a += v[j];
+            }
             st_y(p->Y, (size_t)tok * N + row, a + bv, p->ydt);
           }
         }
-        if (L.ctr) {
-          __threadfence();
-          __syncwarp();
-          if (lane == 0) atomicAdd(L.ctr + 4 * ti, 1u);
-        }
+        tile_written(L, p, lane);
       }
     }
   }
@@ -664,10 +801,11 @@ int env_int(const char* name, int dflt) {
 
 int lb_for(int gs) { return (gs % 128 == 0) ? 16 : (gs % 64 == 0 ? 8 : 4); }
 
+// Shared bytes per warp: TileLayout<T, ASYM, LB>::WARP.
 int warp_bytes(int T, bool asym, int LB) {
-  const int xb = xblock_bytes(T, LB);
-  const int stage = (32 * 4 * LB + xb + 127) & ~127;
-  return 128 + 1024 + (asym ? 1024 : 0) + kD * stage;
+  const int sps = 128 / (4 * LB), sbw = LB == 4 ? 8 : 4;
+  const int xstage = (sps * xblock_bytes(T, LB) + 127) & ~127;
+  return kD * 32 * 128 + 128 + kD * xstage + kD * 32 * sbw * 4 * (asym ? 2 : 1);
 }
 
 size_t xblocks_bytes(int T, int K, int gs) {
@@ -692,9 +830,12 @@ bool make_config(int T, bool asym, int gs, TileConfig& c) {
   size_t cap = (size_t)env_int("SF_TILE_SMEM_KB", 227) * 1024;
   if (cap > (size_t)di.smem_optin) cap = (size_t)di.smem_optin;
   int wpc = (int)(cap / per_warp);
-  const int want = env_int("SF_TILE_WARPS", 16);
+  const int want = env_int("SF_TILE_WARPS", 12);
   if (wpc > want) wpc = want;
   if (wpc > tile_max_threads(T) / 32) wpc = tile_max_threads(T) / 32;
+  // whole multiples of the 4 schedulers: an odd warp would carry a 3-warp
+  // scheduler and, since every warp gets the same share of units, slow all
+  if (wpc > 4) wpc &= ~3;
   if (wpc < 1) return false;
   c.wpc = wpc;
   c.smem = per_warp * wpc;
@@ -716,7 +857,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
-              uint64_t stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+              uint64_t stride_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
   auto fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {inner, rows};
@@ -724,17 +865,19 @@ bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t
   const cuuint32_t box[2] = {box_inner, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // Groups per unit for a wanted number of k-ranges: whole groups, at least 4
-// (a few segments per unit), in blocks of 4 when the scales come by TMA.
-int groups_per_unit(int G, long long want, bool stma) {
+// (a few segments per unit), in whole scale boxes (4 groups, 8 at group size
+// 32) when the scales come by TMA, so that every stage's box is aligned.
+int groups_per_unit(int G, long long want, bool stma, int gs) {
   if (want < 1) want = 1;
+  const int sbw = gs == 32 ? 8 : 4;
   int gper = (int)((G + want - 1) / want);
   if (gper < 4) gper = 4;
-  if (stma) gper = (gper + 3) & ~3;
+  if (stma) gper = (gper + sbw - 1) / sbw * sbw;
   if (gper > G) gper = G;
   return gper;
 }
@@ -746,19 +889,21 @@ int fill_task(TileTask& q, int N, int K, int gs, int T, long long ksplit_want) {
   q.ntile = (N + kUnitRows - 1) / kUnitRows;
   const int G = q.G;
   q.stma = (G % 4 == 0) && ((reinterpret_cast<uintptr_t>(q.S) | reinterpret_cast<uintptr_t>(q.Z)) & 15) == 0;
-  const int gper = groups_per_unit(G, ksplit_want, q.stma != 0);
+  const int gper = groups_per_unit(G, ksplit_want, q.stma != 0, gs);
   q.kper = gper * gs;
   q.ksplit = (G + gper - 1) / gper;
   q.nchunk = (T * (K / 8) + 31) / 32;
+  (void)LB;
   if (!make_map(&q.tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, q.W, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
-                (uint32_t)(4 * LB), kUnitRows))
+                128, kUnitRows, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(SF_ERR_CUDA, "cuTensorMapEncodeTiled failed for the weights (N=%d K=%d)", N, K);
   if (q.stma) {
-    if (!make_map(&q.tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, q.S, (uint64_t)G, (uint64_t)N, (uint64_t)G * 4, 4,
-                  kUnitRows))
+    const uint32_t sbw = gs == 32 ? 8 : 4;
+    if (!make_map(&q.tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, q.S, (uint64_t)G, (uint64_t)N, (uint64_t)G * 4, sbw,
+                  kUnitRows, CU_TENSOR_MAP_SWIZZLE_NONE))
       return fail(SF_ERR_CUDA, "cuTensorMapEncodeTiled failed for the scales");
     if (q.Z && !make_map(&q.tmZ, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, q.Z, (uint64_t)G, (uint64_t)N,
-                         (uint64_t)G * 4, 4, kUnitRows))
+                         (uint64_t)G * 4, sbw, kUnitRows, CU_TENSOR_MAP_SWIZZLE_NONE))
       return fail(SF_ERR_CUDA, "cuTensorMapEncodeTiled failed for the zeros");
   }
   return SF_OK;
@@ -767,6 +912,7 @@ int fill_task(TileTask& q, int N, int K, int gs, int T, long long ksplit_want) {
 template <int T, bool ASYM, int LB>
 cudaError_t launch_tile_t(const TileConfig& c, const TileLaunch& L, bool coop, cudaStream_t st) {
   auto* fn = q4_tile_kernel<T, ASYM, LB>;
+  if (warp_bytes(T, ASYM, LB) != TileLayout<T, ASYM, LB>::WARP) return cudaErrorInvalidConfiguration;
   static int configured[kMaxDevices] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -921,9 +1067,11 @@ int run_tile_linear(const uint8_t* W, const float* S, const float* Z, const floa
   q.xd = base + pbytes;
   q.xpre = 1;
   q.ubase = 0;
-  q.wait_from = q.wait_to = 0;
+  q.phase = 0;
+  q.ph_last = 1;
   L.tasks = nullptr; L.ntasks = 1; L.total = (long long)q.ntile * q.ksplit;
-  L.ctr = nullptr;
+  L.phctr = nullptr;
+  L.flags = nullptr;
   L.prefetch = 0;
   L.dbg = 0;
   const int need = (int)((L.total + c.wpc - 1) / c.wpc);
@@ -944,8 +1092,9 @@ int run_tile_linear(const uint8_t* W, const float* S, const float* Z, const floa
 using namespace sf;
 
 namespace {
-// Workspace: [per-task counters: 4 x u32 | per-tile arrival counters] (both
-// cleared before every run) [task table] [k-split partials] [activation blocks].
+// Workspace: [per-CTA flag lines | per-phase counters | per-tile arrival
+// counters] (cleared before every run) [task table] [k-split partials]
+// [activation blocks].
 struct StepSizes {
   size_t ctr, tiles, table, part, xblk;
   size_t total() const { return ctr + tiles + table + part + xblk; }
@@ -968,7 +1117,7 @@ std::vector<int> plan_ksplit(const sf_q4_task* tasks, int n, int warps) {
       const bool stma = G % 4 == 0 &&
                         ((reinterpret_cast<uintptr_t>(tasks[k].scales) |
                           reinterpret_cast<uintptr_t>(tasks[k].zeros)) & 15) == 0;
-      const int gper = groups_per_unit(G, want, stma);
+      const int gper = groups_per_unit(G, want, stma, tasks[k].group_size);
       ks[k] = (G + gper - 1) / gper;
     }
     i = j;
@@ -976,9 +1125,9 @@ std::vector<int> plan_ksplit(const sf_q4_task* tasks, int n, int warps) {
   return ks;
 }
 
-StepSizes step_sizes(const sf_q4_task* tasks, int n, const std::vector<int>& ksplit) {
+StepSizes step_sizes(const sf_q4_task* tasks, int n, const std::vector<int>& ksplit, int grid) {
   StepSizes z{};
-  z.ctr = align256((size_t)16 * n);
+  z.ctr = align256((size_t)128 * grid) + align256((size_t)16 * n);
   size_t tiles = 0, part = 0, xb = 0;
   for (int i = 0; i < n; ++i) {
     const sf_q4_task& a = tasks[i];
@@ -1016,7 +1165,7 @@ size_t sf_q4_step_workspace_bytes(const sf_q4_task* tasks, int ntasks) {
       return 0;
   TileConfig c;
   if (!step_config(tasks, c)) return 0;
-  return step_sizes(tasks, ntasks, plan_ksplit(tasks, ntasks, c.grid * c.wpc)).total();
+  return step_sizes(tasks, ntasks, plan_ksplit(tasks, ntasks, c.grid * c.wpc), c.grid).total();
 }
 
 int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size_t workspace_bytes,
@@ -1046,7 +1195,7 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
   TileConfig c;
   if (!step_config(tasks, c)) return fail(SF_ERR_UNSUPPORTED, "no launch configuration for T=%d", T);
   const std::vector<int> want = plan_ksplit(tasks, ntasks, c.grid * c.wpc);
-  const StepSizes z = step_sizes(tasks, ntasks, want);
+  const StepSizes z = step_sizes(tasks, ntasks, want, c.grid);
   if (workspace_bytes < z.total())
     return fail(SF_ERR_SHAPE, "workspace too small: need %zu bytes", z.total());
 
@@ -1057,8 +1206,7 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
   uint8_t* xblk = part + z.part;
   std::vector<TileTask> h(ntasks);
   long long ub = 0;
-  int phase = 0, prev_phase = 0;   // first task of the current / previous phase
-  bool any_wait = false, any_pre = false;
+  int nph = 0;
   for (int i = 0; i < ntasks; ++i) {
     const sf_q4_task& a = tasks[i];
     TileTask& q = h[i];
@@ -1077,31 +1225,45 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
     q.xd = xblk;
     xblk += xblocks_bytes(T, a.K, a.group_size);
     // A task with wait_before opens a phase; every task of a phase reads X only
-    // after the whole previous phase has finished (and, transitively, all
+    // after the whole previous phase has written Y (and, transitively, all
     // earlier ones).  Only phase-0 inputs exist before the launch.
-    if (i > 0 && a.wait_before) {
-      prev_phase = phase;
-      phase = i;
-    }
-    q.wait_from = prev_phase;
-    q.wait_to = phase;
-    q.xpre = phase == 0 ? 1 : 0;
-    any_wait |= phase > 0;
-    any_pre |= q.xpre != 0;
+    if (i == 0 || a.wait_before) ++nph;
+    q.phase = nph - 1;
+    q.xpre = q.phase == 0 ? 1 : 0;
     q.ubase = ub;
     ub += (long long)q.ntile * q.ksplit;
+  }
+  for (int i = 0; i < ntasks;) {
+    int j = i;
+    long long tiles_ph = 0, chunks = 0, units = 0;
+    while (j < ntasks && h[j].phase == h[i].phase) {
+      tiles_ph += h[j].ntile;
+      chunks += h[j].nchunk;
+      units += (long long)h[j].ntile * h[j].ksplit;
+      ++j;
+    }
+    for (int k = i; k < j; ++k) {
+      h[k].ph_first = i;
+      h[k].ph_tiles = (int)tiles_ph;
+      h[k].ph_chunks = (int)chunks;
+      h[k].ph_units = units;
+      h[k].ph_ubase = h[i].ubase;
+      h[k].ph_last = h[k].phase == nph - 1 ? 1 : 0;
+    }
+    i = j;
   }
   StepHandle* hd = new StepHandle{};
   hd->cfg = c;
   hd->workspace = workspace;
   hd->clear_bytes = z.ctr + z.tiles;
-  hd->coop = any_wait;
-  hd->prepass = any_pre;
+  hd->coop = nph > 1;
+  hd->prepass = true;
   TileLaunch& L = hd->L;
   L.tasks = reinterpret_cast<const TileTask*>(table);
   L.ntasks = ntasks;
   L.total = ub;
-  L.ctr = reinterpret_cast<unsigned int*>(ws);
+  L.flags = reinterpret_cast<unsigned int*>(ws);
+  L.phctr = reinterpret_cast<unsigned int*>(ws + align256((size_t)128 * c.grid));
   L.prefetch = env_int("SF_TILE_PREFETCH", 1);
   L.dbg = env_int("SF_TILE_DBG", 0);
   cudaError_t e = cudaMemcpy(table, h.data(), (size_t)ntasks * sizeof(TileTask), cudaMemcpyHostToDevice);
@@ -1131,5 +1293,28 @@ int sf_q4_step_run(void* handle, void* stream) {
 }
 
 void sf_q4_step_destroy(void* handle) { delete static_cast<StepHandle*>(handle); }
+
+// Development aid, not part of the public header: record per-unit timestamps
+// of every later run of `handle` into `buf` (4 x u64 per unit; null stops).
+int sf_q4_step_set_trace(void* handle, unsigned long long* buf) {
+  if (!handle) return fail(SF_ERR_NULL, "null handle");
+  static_cast<StepHandle*>(handle)->L.trace = buf;
+  return SF_OK;
+}
+
+// Development aid: first unit and phase of task i (host copy of the table).
+int sf_q4_step_task_info(void* handle, int i, long long* ubase, int* phase) {
+  StepHandle* hd = static_cast<StepHandle*>(handle);
+  if (!hd || i < 0 || i >= hd->L.ntasks) return SF_ERR_SHAPE;
+  TileTask q;
+  cudaMemcpy(&q, hd->L.tasks + i, sizeof(q), cudaMemcpyDeviceToHost);
+  *ubase = q.ubase;
+  *phase = q.phase;
+  return SF_OK;
+}
+
+long long sf_q4_step_units(void* handle) {
+  return handle ? static_cast<StepHandle*>(handle)->L.total : 0;
+}
 
 }  // extern "C"
