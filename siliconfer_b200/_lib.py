@@ -45,6 +45,7 @@ SIGNATURES = {
     "sf_q4_step_workspace_bytes": [ctypes.POINTER(Q4Task), _I],
     "sf_q4_step_create": [ctypes.POINTER(Q4Task), _I, _P, _SZ, ctypes.POINTER(_P)],
     "sf_q4_step_run": [_P, _P],
+    "sf_q4_step_launch": [_P, _P, _I],
     "sf_q4_step_destroy": [_P],
 }
 _RESTYPES = {"sf_status_string": ctypes.c_char_p, "sf_last_error": ctypes.c_char_p,

@@ -1275,22 +1275,31 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
   return SF_OK;
 }
 
-int sf_q4_step_run(void* handle, void* stream) {
+int sf_q4_step_launch(void* handle, void* stream, int part) {
   if (!handle) return fail(SF_ERR_NULL, "null handle");
+  if (part < 0 || part > 2) return fail(SF_ERR_SHAPE, "part must be 0, 1 or 2");
   StepHandle* hd = static_cast<StepHandle*>(handle);
+  if (part == 2 && hd->coop)
+    return fail(SF_ERR_UNSUPPORTED, "the GEMV kernel alone needs a single-phase step (no wait_before)");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(hd->workspace, 0, hd->clear_bytes, st);
-  if (e != cudaSuccess) return cuda_fail(e, "clearing the step counters");
-  if (hd->prepass) {
+  cudaError_t e = cudaSuccess;
+  if (part != 2) {
+    e = cudaMemsetAsync(hd->workspace, 0, hd->clear_bytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, "clearing the step counters");
+  }
+  if (part != 2 && hd->prepass) {
     e = launch_xblocks(hd->cfg.T, hd->cfg.LB, hd->L.ntasks, hd->L, st);
     if (e != cudaSuccess) return cuda_fail(e, "activation pre-pass launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);
   }
+  if (part == 1) return SF_OK;
   e = launch_tile(hd->cfg, hd->L, hd->coop, st);
   if (e != cudaSuccess) return cuda_fail(e, "q4 step launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return SF_OK;
 }
+
+int sf_q4_step_run(void* handle, void* stream) { return sf_q4_step_launch(handle, stream, 0); }
 
 void sf_q4_step_destroy(void* handle) { delete static_cast<StepHandle*>(handle); }
 
