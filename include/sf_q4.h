@@ -126,6 +126,28 @@ int sf_q4_step_run(void* handle, void* stream);
 int sf_q4_step_launch(void* handle, void* stream, int part);
 void sf_q4_step_destroy(void* handle);
 
+/* sf_q4_linear for T <= 8 that allocates nothing.  No counterpart in the
+ * reference (its kernels need no device scratch).  sf_q4_linear keeps a
+ * library-owned scratch buffer per stream and grows it with cudaMalloc the
+ * first time it sees a shape; this entry point is for callers that cannot let
+ * a library allocate (a process that reserves the whole GPU for its own pool,
+ * code where an allocation would stall or be refused).  It uses a fixed 4 MiB
+ * buffer compiled into the library's device image instead:
+ *   - limits: N <= 524288 rows, and the activation blocks (about
+ *     3*T*K + 8*T*K/group_size bytes) must fit in 4032 KiB, e.g. T = 8 up to
+ *     K = 160000 at group 128; larger requests fail with SF_ERR_SHAPE and a
+ *     message naming the limit.  When the k-split partial sums would not fit,
+ *     fewer k-splits are used.
+ *   - the first call on each device looks the buffer up
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - there is ONE buffer per device: calls that overlap in time on the same
+ *     device (other streams, other host threads) race on it.  Order them,
+ *     e.g. issue them all on one stream.
+ * Same arguments, layouts and results as sf_q4_linear otherwise (no flags). */
+int sf_q4_linear_static_scratch(const uint8_t* W, const float* scales, const float* zeros,
+                                const float* bias, const void* X, int x_dtype, void* Y,
+                                int y_dtype, int N, int K, int T, int group_size, void* stream);
+
 /* Device dequant to fp32/fp16/bf16 [N, K].  fp32 output is bit-exact with
    dequantize_sym / dequantize_asym (siliconfer/quant/primitives.py:54-75,
    117-140); fp16/bf16 are that value rounded to nearest even. */

@@ -38,6 +38,7 @@ SIGNATURES = {
     "sf_q4_gemm_sym": [_P, _P, _P, _P, _I, _I, _I, _I, _P],
     "sf_q4_gemm_asym": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "sf_q4_linear": [_P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _P],
+    "sf_q4_linear_static_scratch": [_P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P],
     "sf_q4_dequant": [_P, _P, _P, _P, _I, _I, _I, _I, _P],
     "sf_q4_quantize_pack": [_P, _P, _P, _P, _I, _I, _I, _P],
     "sf_q4_check_device_error": [],

@@ -1327,3 +1327,117 @@ long long sf_q4_step_units(void* handle) {
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// Decode GEMV without any allocation: the single-GEMV launch above, with its
+// scratch (arrival counters, k-split partial sums, activation blocks) taken
+// from a fixed buffer that lives in this library's own device image.
+//
+// Why: sf_q4_linear grows a library-owned scratch buffer with cudaMalloc the
+// first time it meets a shape.  Some callers cannot let a library allocate at
+// all -- a serving process that hands every byte of the GPU to its own pool
+// up front, code that runs where an allocation would synchronise the device
+// or be refused.  For them this entry point uses only memory that exists from
+// the moment the library is loaded.
+// ===========================================================================
+namespace {
+constexpr size_t kStaticCounterBytes = (size_t)64 << 10;               // 16384 tiles: N <= 524288
+constexpr size_t kStaticScratchBytes = (size_t)4 << 20;                // 4 MiB in total
+constexpr size_t kStaticDataBytes = kStaticScratchBytes - kStaticCounterBytes;
+
+// Part of the module image: created with the library, never allocated or freed.
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+std::mutex g_static_mu;
+void* g_static_ptr[kMaxDevices] = {nullptr};
+
+// Device address of the buffer on the current device; looked up once per
+// device on the first call.
+int static_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(SF_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress of the static GEMV scratch");
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return SF_OK;
+}
+}  // namespace
+
+extern "C" int sf_q4_linear_static_scratch(const uint8_t* W, const float* scales, const float* zeros,
+                                           const float* bias, const void* X, int x_dtype, void* Y,
+                                           int y_dtype, int N, int K, int T, int group_size, void* stream) {
+  if (!W || !scales || !X || !Y) return fail(SF_ERR_NULL, "null pointer argument");
+  if (x_dtype < 0 || x_dtype > 2 || y_dtype < 0 || y_dtype > 2) return fail(SF_ERR_DTYPE, "unknown dtype code");
+  if (N < 0 || K <= 0 || T < 0) return fail(SF_ERR_SHAPE, "invalid N/K/T");
+  if (group_size <= 0 || group_size % 2) return fail(SF_ERR_SHAPE, "group_size must be a positive even number");
+  if (K % group_size) return fail(SF_ERR_SHAPE, "in_features must be divisible by group_size");
+  if (T > kMaxGemvT || !shape_ok(N > 0 ? N : 1, K, group_size))
+    return fail(SF_ERR_UNSUPPORTED,
+                "static-scratch GEMV takes T <= %d, K %% 32 == 0 and a power-of-two group_size in 32..256",
+                kMaxGemvT);
+  if ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(zeros) |
+       reinterpret_cast<uintptr_t>(X)) & 15)
+    return fail(SF_ERR_ALIGN, "W, scales, zeros and X must be 16-byte aligned");
+  const int ntile = (N + kUnitRows - 1) / kUnitRows;
+  const size_t cbytes = align256((size_t)ntile * 4);
+  const size_t xbytes = xblocks_bytes(T, K, group_size);
+  if (cbytes > kStaticCounterBytes || xbytes > kStaticDataBytes)
+    return fail(SF_ERR_SHAPE,
+                "N=%d K=%d T=%d needs more than the static GEMV scratch holds (%zu KiB of tile counters for "
+                "N <= %zu, %zu KiB of activation blocks); use sf_q4_linear",
+                N, K, T, kStaticCounterBytes >> 10, (kStaticCounterBytes / 4) * kUnitRows, kStaticDataBytes >> 10);
+  if (N == 0 || T == 0) return SF_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* base = nullptr;
+  int rc = static_scratch(&base);
+  if (rc != SF_OK) return rc;
+
+  TileConfig c;
+  if (!make_config(T, zeros != nullptr, group_size, c)) return fail(SF_ERR_UNSUPPORTED, "no launch configuration");
+  TileLaunch L{};
+  TileTask& q = L.single;
+  q.W = W; q.S = scales; q.Z = zeros; q.bias = bias; q.X = X; q.Y = Y; q.xdt = x_dtype; q.ydt = y_dtype;
+  // k-split as the allocating entry would choose it, reduced until the
+  // partial sums fit next to the activation blocks
+  long long want = (c.grid * c.wpc + ntile - 1) / ntile;
+  size_t pbytes = 0;
+  for (;;) {
+    rc = fill_task(q, N, K, group_size, T, want);
+    if (rc != SF_OK) return rc;
+    pbytes = q.ksplit > 1 ? align256((size_t)q.ksplit * T * N * 4) : 0;
+    if (pbytes + xbytes <= kStaticDataBytes || q.ksplit == 1) break;
+    want = q.ksplit - 1;
+  }
+  if (pbytes + xbytes > kStaticDataBytes) return fail(SF_ERR_SHAPE, "static GEMV scratch too small");
+  uint8_t* b = static_cast<uint8_t*>(base);
+  // The counters must start at zero; a run cut short could have left some set.
+  cudaError_t e = cudaMemsetAsync(b, 0, cbytes, st);
+  if (e != cudaSuccess) return cuda_fail(e, "clearing the static scratch counters");
+  q.tcnt = reinterpret_cast<unsigned int*>(b);
+  q.part = pbytes ? reinterpret_cast<float*>(b + kStaticCounterBytes) : nullptr;
+  q.xd = b + kStaticCounterBytes + pbytes;
+  q.xpre = 1;
+  q.ubase = 0;
+  q.phase = 0;
+  q.ph_last = 1;
+  L.tasks = nullptr; L.ntasks = 1; L.total = (long long)q.ntile * q.ksplit;
+  L.phctr = nullptr;
+  L.flags = nullptr;
+  L.prefetch = 0;
+  L.dbg = 0;
+  const int need = (int)((L.total + c.wpc - 1) / c.wpc);
+  if (c.grid > need) c.grid = need;
+  e = launch_xblocks(T, c.LB, 1, L, st);
+  if (e != cudaSuccess) return cuda_fail(e, "activation pre-pass launch");
+  e = launch_tile(c, L, false, st);
+  if (e != cudaSuccess) return cuda_fail(e, "q4_tile_kernel launch");
+  g_launches.fetch_add(2, std::memory_order_relaxed);
+  return SF_OK;
+}
