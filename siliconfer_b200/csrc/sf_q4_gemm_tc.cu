@@ -44,6 +44,10 @@
 #include "sf_q4.h"
 #include "sf_q4_internal.h"
 
+#ifndef SF_TC_DQ_LANES
+#define SF_TC_DQ_LANES 4
+#endif
+
 namespace sf {
 SF_DEFINE_ERROR_READER(take_dev_error_tc)
 extern std::atomic<long long> g_launches;
@@ -52,7 +56,9 @@ namespace {
 
 constexpr int kBK = 64;                 // k per stage: 64 bf16 = one 128-byte swizzle row
 constexpr int kSliceBytes = 128 * 128;  // one 128-token slice of X per stage
-constexpr int kEpiWarps = 4, kProdWarp = 4, kMmaWarp = 5, kDqWarp0 = 6, kDqWarps = 8;
+constexpr int kEpiWarps = 4, kProdWarp = 4, kMmaWarp = 5, kDqWarp0 = 6;
+constexpr int kDqLanes = SF_TC_DQ_LANES;   // dequant warps per TMEM lane quarter, one per in-flight k-block
+constexpr int kDqWarps = 4 * kDqLanes;
 constexpr int kThreads = 32 * (kDqWarp0 + kDqWarps);
 constexpr int kSmemLimit = 232448;      // 227 KB opt-in per block
 constexpr int kTcMinT = 48;             // below this the GEMV kernel (weights re-read per 8 tokens) wins
@@ -66,7 +72,7 @@ struct TcParams {
   const float* Z;
   const float* bias;
   void* Y;
-  int T, N, K, G, gs, ydt;
+  int T, N, K, G, gs, lg2gs, ydt;
   int mtiles, ntiles, kblocks, stages;
 };
 
@@ -191,64 +197,113 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return d;
 }
 
-// Eight nibbles of one packed word (k order: lo nibble of byte 0 first) to
-// eight bf16 weights RNE((q - z) * s), as four bf16x2 words.
-//  * u: the nibbles as unsigned 0..15 (symmetric nibbles already flipped
-//    with ^8, so that u - 8 is the two's-complement value);
-//  * 2^23 + u is built exactly as a float from the byte (prmt);
-//  * zint: the zero point is an integer, so 2^23 + z is exact and one
-//    subtraction gives u - z exactly; otherwise u and u - z are formed in two
-//    steps, rounding exactly as the reference's fp32 (q - z).
-template <bool ZINT>
-__device__ __forceinline__ uint4 dequant8(uint32_t w, bool sym, float zc, float z, float s) {
-  uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
-  if (sym) { lo ^= 0x08080808u; hi ^= 0x08080808u; }
-  float f[8];
-#pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    f[2 * b] = __uint_as_float(prmt(lo, 0x4B000000u, 0x7440u + b));
-    f[2 * b + 1] = __uint_as_float(prmt(hi, 0x4B000000u, 0x7440u + b));
-  }
-  uint32_t o[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float a, c;
-    if (ZINT) {
-      a = __fmul_rn(__fsub_rn(f[2 * j], zc), s);
-      c = __fmul_rn(__fsub_rn(f[2 * j + 1], zc), s);
-    } else {
-      a = __fmul_rn(__fsub_rn(__fsub_rn(f[2 * j], 8388608.f), z), s);
-      c = __fmul_rn(__fsub_rn(__fsub_rn(f[2 * j + 1], 8388608.f), z), s);
-    }
-    o[j] = pack_bf16(a, c);
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
+// Two fp32 lanes per instruction (sm_100 packed f32x2 arithmetic).
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
+  return v;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return pack_bf16(lo, hi);
 }
 
-template <int MT, int BN>
+// Eight nibbles of one packed word (k order: lo nibble of byte 0 first) to
+// eight bf16 weights RNE((q - z) * s), as four bf16x2 words (k pairs).
+//  * u: the nibbles as unsigned 0..15 (symmetric nibbles flipped with ^8, so
+//    that u - 8 is the two's-complement value and sym is the case z = 8);
+//  * 2^23 + u is built exactly as a float from the byte (prmt);
+//  * ZINT (integer zero point): negzc = -(2^23 + z) is exact, so one addition
+//    gives u - z exactly, then one multiply rounds (u - z) * s once, as the
+//    reference's fp32 arithmetic does;
+//  * otherwise u is recovered exactly, then u - z and (u - z) * s each round
+//    once, again as in the reference.
+template <bool ZINT>
+__device__ __forceinline__ void dequant8(uint32_t w, bool sym, uint64_t negzc2, uint64_t negz2, uint64_t s2,
+                                         uint32_t (&o)[4]) {
+  uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+  if (sym) { lo ^= 0x08080808u; hi ^= 0x08080808u; }
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    uint64_t v = f2(__uint_as_float(prmt(lo, 0x4B000000u, 0x7440u + b)),
+                    __uint_as_float(prmt(hi, 0x4B000000u, 0x7440u + b)));
+    if (ZINT) {
+      v = add2(v, negzc2);
+    } else {
+      v = add2(add2(v, f2(-8388608.f, -8388608.f)), negz2);
+    }
+    o[b] = pack_bf16x2(mul2(v, s2));
+  }
+}
+
+// 32 consecutive 32-bit TMEM columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T: A (128 x 16 bf16) in TMEM, one row per
+// lane, two k per 32-bit column.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Shared-memory and TMEM plan of a BT-token tile:
+//  * stage s: X tile [BT tokens x 64 k] bf16 in the 128-byte swizzle, then
+//    the packed weight tile [128 rows x 32 bytes] in the 32-byte swizzle
+//    (rows r and r+4 land in different banks for the dequant reads);
+//  * TMEM: the fp32 accumulators (BT columns, two buffers when BT <= 128),
+//    then one 32-column slot of dequantized weights per stage.
+template <int BT>
 struct TcLayout {
-  static constexpr uint32_t X = MT * kSliceBytes;
-  static constexpr uint32_t WQ = BN * 128;     // dequantized bf16 tile
-  static constexpr uint32_t P = BN * 32;       // packed bytes
-  static constexpr uint32_t STAGE = X + WQ + P;  // multiple of 1024
-  static constexpr int ACC_COLS = MT * BN;
-  static constexpr int NBUF = ACC_COLS <= 256 ? 2 : 1;
-  static constexpr uint32_t TMEM_COLS = ACC_COLS * NBUF <= 256 ? 256 : 512;
+  static constexpr uint32_t X = BT * 128;
+  static constexpr uint32_t P = 128 * 32;
+  static constexpr uint32_t STAGE = X + P;
+  static constexpr int S = (kSmemLimit - 1024 - 512) / STAGE > 6 ? 6 : (kSmemLimit - 1024 - 512) / STAGE;
+  static constexpr int NBUF = BT <= 128 ? 2 : 1;
+  static constexpr uint32_t A_COL = NBUF * BT;  // first weight slot column
+  static constexpr uint32_t TMEM_COLS = 512;
   static_assert(STAGE % 1024 == 0, "stage must keep 1024-byte alignment");
+  static_assert(A_COL + 32 * S <= TMEM_COLS, "TMEM plan exceeds 512 columns");
+  static constexpr size_t SMEM = 1024 + (size_t)S * STAGE + 512;
 };
 
 // ---------------------------------------------------------------------------
-// The kernel
+// The kernel: one CTA computes Y[t0 : t0+BT, n0 : n0+128] tiles in turn.
 // ---------------------------------------------------------------------------
-template <int MT, int BN, bool ASYM>
+template <int BT, bool ASYM>
 __global__ void __launch_bounds__(kThreads, 1)
     q4_gemm_tc_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_constant__ CUtensorMap mapW,
                       const TcParams p) {
-  using L = TcLayout<MT, BN>;
+  using L = TcLayout<BT>;
+  constexpr int S = L::S;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
-  const int S = p.stages;
   // control block after the stages: barriers, TMEM address, abort flag
   const uint32_t ctl = base + (uint32_t)S * L::STAGE;
   const uint32_t full0 = ctl, dq0 = ctl + 8 * 8, empty0 = ctl + 16 * 8;
@@ -261,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       bar_init(full0 + 8 * s, 1);
-      bar_init(dq0 + 8 * s, kDqWarps);
+      bar_init(dq0 + 8 * s, 4);  // one warp per lane quarter
       bar_init(empty0 + 8 * s, 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -297,15 +352,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles_total && ok; tile += gridDim.x) {
-        const int m0 = (tile % p.mtiles) * (128 * MT), n0 = (tile / p.mtiles) * BN;
+        const int m0 = (tile % p.mtiles) * BT, n0 = (tile / p.mtiles) * 128;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1;
           if (!bar_wait(empty0 + 8 * s, ph ^ 1, kErrProd, abort_flag)) { ok = false; break; }
           const uint32_t st = base + s * L::STAGE;
           bar_expect_tx(full0 + 8 * s, L::X + L::P);
-#pragma unroll
-          for (int m = 0; m < MT; ++m) tma_2d(st + m * kSliceBytes, &mapX, kb * kBK, m0 + m * 128, full0 + 8 * s);
-          tma_2d(st + L::X + L::WQ, &mapW, kb * (kBK / 2), n0, full0 + 8 * s);
+          tma_2d(st, &mapX, kb * kBK, m0, full0 + 8 * s);
+          tma_2d(st + L::X, &mapW, kb * (kBK / 2), n0, full0 + 8 * s);
         }
       }
       // Drain: every issued copy must have landed before the block exits.
@@ -322,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16(128, BN);
+      const uint32_t idesc = idesc_bf16(128, BT);
       uint32_t it = 0, issued = 0;
       int local = 0;
       bool ok = true;
@@ -331,21 +385,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t use = L::NBUF == 2 ? (uint32_t)(local >> 1) : (uint32_t)local;
         if (!bar_wait(acce0 + 8 * b, (use & 1) ^ 1, kErrMma, abort_flag)) break;
         tc_fence_after();
-        const uint32_t dcol = tmem + (uint32_t)(b * L::ACC_COLS);
+        const uint32_t dcol = tmem + (uint32_t)(b * BT);
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1;
           if (!bar_wait(full0 + 8 * s, ph, kErrMma, abort_flag) ||
               !bar_wait(dq0 + 8 * s, ph, kErrMma, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint32_t st = base + s * L::STAGE;
+          const uint32_t acol = tmem + L::A_COL + 32 * s;
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t bdesc = sw128_desc(st + L::X + kk * 32);
-#pragma unroll
-            for (int m = 0; m < MT; ++m)
-              mma_bf16(dcol + m * BN, sw128_desc(st + m * kSliceBytes + kk * 32), bdesc, idesc,
-                       (kb | kk) != 0);
-          }
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_bf16_ts(dcol, acol + 8 * kk, sw128_desc(st + kk * 32), idesc, (kb | kk) != 0);
           issued = 1;
           mma_commit(empty0 + 8 * s);
         }
@@ -362,128 +412,100 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp >= kDqWarp0) {
-    // ---------------- dequant: packed bytes -> bf16 swizzled tile ----------------
-    const int dt = threadIdx.x - 32 * kDqWarp0;  // 0..255
-    constexpr int kUnits = BN * 2;               // (row, 32-k half) pairs per stage
-    constexpr int kPer = kUnits / (32 * kDqWarps);
-    static_assert(kUnits % (32 * kDqWarps) == 0, "units must divide evenly");
-    uint32_t it = 0;
+    // ------- dequant: packed bytes -> bf16 weights in this stage's TMEM slot -------
+    // Warp w serves TMEM lanes 32*(w%4)... (weight rows r = one per thread)
+    // and every kDqLanes-th stage (stage lane j): all 64 weights of its row
+    // for that k-block.  kDqLanes k-blocks are dequantized concurrently per
+    // lane quarter, which hides the latency of each one.
+    const int q = warp & 3, j = (warp - kDqWarp0) >> 2;
+    const int r = 32 * q + lane;
+    uint32_t it0 = 0;  // global stage index of the current tile's k-block 0
     bool ok = true;
-    for (int tile = blockIdx.x; tile < ntiles_total && ok; tile += gridDim.x) {
-      const int n0 = (tile / p.mtiles) * BN;
-      for (int kb = 0; kb < KB; ++kb, ++it) {
+    for (int tile = blockIdx.x; tile < ntiles_total && ok; tile += gridDim.x, it0 += KB) {
+      const int n = (tile / p.mtiles) * 128 + r;
+      const bool in = n < p.N;
+      const float* srow = p.S + (size_t)(in ? n : 0) * p.G;
+      const float* zrow = ASYM ? p.Z + (size_t)(in ? n : 0) * p.G : nullptr;
+      // first k-block of this tile that belongs to stage lane j
+      const int kb0 = (int)(((uint32_t)j + kDqLanes - it0 % kDqLanes) % kDqLanes);
+      // scales / zero points of both 32-k halves, loaded one own k-block ahead
+      auto ld2 = [&](const float* row, int kb, float (&v)[2]) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+          v[hh] = (in && kb < KB) ? __ldg(row + ((kb * kBK + 32 * hh) >> p.lg2gs)) : 0.f;
+      };
+      float sn[2], zn[2] = {8.f, 8.f};
+      ld2(srow, kb0, sn);
+      if (ASYM) ld2(zrow, kb0, zn);
+      for (int kb = kb0; kb < KB; kb += kDqLanes) {
+        const uint32_t it = it0 + kb;
         const uint32_t s = it % S, ph = (it / S) & 1;
-        // the unit's scale and zero point, fetched before the wait
-        float sc[kPer], zz[kPer];
-#pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-          const int u = dt + j * 32 * kDqWarps, r = u >> 1, h = u & 1;
-          const int n = n0 + r, g = (kb * kBK + h * 32) / p.gs;
-          const bool in = n < p.N;
-          sc[j] = in ? __ldg(p.S + (size_t)n * p.G + g) : 0.f;
-          zz[j] = (ASYM && in) ? __ldg(p.Z + (size_t)n * p.G + g) : 0.f;
-        }
+        const float sc[2] = {sn[0], sn[1]}, zc[2] = {zn[0], zn[1]};
+        ld2(srow, kb + kDqLanes, sn);
+        if (ASYM) ld2(zrow, kb + kDqLanes, zn);
         if (!bar_wait(full0 + 8 * s, ph, kErrDq, abort_flag)) { ok = false; break; }
+        tc_fence_after();
         const uint32_t st = base + s * L::STAGE;
+        // packed row r: 32 bytes in the 32-byte swizzle (16-byte chunk c at c ^ ((r >> 2) & 1))
+        uint32_t w8[8];
+        const uint32_t prow = st + L::X + r * 32, sw = (uint32_t)((r >> 2) & 1) << 4;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(w8[0]), "=r"(w8[1]), "=r"(w8[2]), "=r"(w8[3]) : "r"(prow + sw));
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(w8[4]), "=r"(w8[5]), "=r"(w8[6]), "=r"(w8[7]) : "r"(prow + (sw ^ 16)));
+        uint32_t o[32];
 #pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-          const int u = dt + j * 32 * kDqWarps, r = u >> 1, h = u & 1;
-          uint4 wq;
-          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                       : "=r"(wq.x), "=r"(wq.y), "=r"(wq.z), "=r"(wq.w)
-                       : "r"(st + L::X + L::WQ + r * 32 + h * 16));
-          const float z = ASYM ? zz[j] : 8.f;
+        for (int hh = 0; hh < 2; ++hh) {
+          const float z = ASYM ? zc[hh] : 8.f;
           const bool zint = !ASYM || (z == rintf(z) && fabsf(z) < 4194304.f);
-          const float zc = 8388608.f + z;
-          const uint32_t w4[4] = {wq.x, wq.y, wq.z, wq.w};
-          const uint32_t row = st + L::X + r * 128;
+          const uint64_t s2 = f2(sc[hh], sc[hh]), negzc2 = f2(-(8388608.f + z), -(8388608.f + z)),
+                         negz2 = f2(-z, -z);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            const uint4 o = zint ? dequant8<true>(w4[c], !ASYM, zc, z, sc[j])
-                                 : dequant8<false>(w4[c], !ASYM, zc, z, sc[j]);
-            const uint32_t chunk = (uint32_t)(h * 4 + c) ^ (uint32_t)(r & 7);
-            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(row + chunk * 16), "r"(o.x), "r"(o.y),
-                         "r"(o.z), "r"(o.w)
-                         : "memory");
+            uint32_t oc[4];
+            if (zint) dequant8<true>(w8[4 * hh + c], !ASYM, negzc2, negz2, s2, oc);
+            else dequant8<false>(w8[4 * hh + c], !ASYM, negzc2, negz2, s2, oc);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[16 * hh + 4 * c + e] = oc[e];
           }
         }
-        fence_async_smem();
+        tmem_st32(tmem + ((uint32_t)(32 * q) << 16) + L::A_COL + 32 * s, o);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) bar_arrive(dq0 + 8 * s);
       }
     }
   } else {
     // ---------------- epilogue: TMEM -> Y ----------------
-    const int q = warp;  // TMEM lanes 32q..32q+31
+    // Warp q reads TMEM lanes 32q.. = weight rows; each register column is a
+    // token, so every store of the warp writes 32 consecutive outputs of one
+    // token row of Y.
+    const int q = warp;
     int local = 0;
-    const size_t ye = p.ydt == SF_F32 ? 4 : 2;
     for (int tile = blockIdx.x; tile < ntiles_total; tile += gridDim.x, ++local) {
-      const int m0 = (tile % p.mtiles) * (128 * MT), n0 = (tile / p.mtiles) * BN;
+      const int m0 = (tile % p.mtiles) * BT, n = (tile / p.mtiles) * 128 + 32 * q + lane;
       const int b = L::NBUF == 2 ? (local & 1) : 0;
       const uint32_t use = L::NBUF == 2 ? (uint32_t)(local >> 1) : (uint32_t)local;
       if (!bar_wait(accf0 + 8 * b, use & 1, kErrEpi, abort_flag)) break;
       tc_fence_after();
+      const bool nin = n < p.N;
+      const float bv = (p.bias && nin) ? __ldg(p.bias + n) : 0.f;
 #pragma unroll 1
-      for (int m = 0; m < MT; ++m) {
-        const int t = m0 + m * 128 + q * 32 + lane;
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-          float v[32];
-          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * L::ACC_COLS + m * BN + c0), v);
-          const int nb = n0 + c0;
-          if (t < p.T && nb < p.N) {  // rows past T and columns past N store nothing
-          const int nv = p.N - nb < 32 ? p.N - nb : 32;
-          if (p.bias) {
+      for (int c0 = 0; c0 < BT; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * BT + c0), v);
+        if (nin) {
+          const int t0 = m0 + c0;
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (i < nv) v[i] += __ldg(p.bias + nb + i);
-          }
-          uint8_t* yrow = static_cast<uint8_t*>(p.Y) + ((size_t)t * p.N + nb) * ye;
-          const bool vec = nv == 32 && ((reinterpret_cast<uintptr_t>(yrow) & 15) == 0);
-          if (p.ydt == SF_F32) {
-            float* y = reinterpret_cast<float*>(yrow);
-            if (vec) {
-#pragma unroll
-              for (int i = 0; i < 32; i += 4)
-                *reinterpret_cast<float4*>(y + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (i < nv) y[i] = v[i];
+          for (int j = 0; j < 32; ++j) {
+            if (t0 + j < p.T) {
+              const size_t o = (size_t)(t0 + j) * p.N + n;
+              const float y = v[j] + bv;
+              if (p.ydt == SF_F32) static_cast<float*>(p.Y)[o] = y;
+              else if (p.ydt == SF_BF16) static_cast<__nv_bfloat16*>(p.Y)[o] = __float2bfloat16_rn(y);
+              else static_cast<__half*>(p.Y)[o] = __float2half_rn(y);
             }
-          } else if (p.ydt == SF_BF16) {
-            __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(yrow);
-            if (vec) {
-#pragma unroll
-              for (int i = 0; i < 32; i += 8) {
-                uint4 o;
-                o.x = pack_bf16(v[i], v[i + 1]); o.y = pack_bf16(v[i + 2], v[i + 3]);
-                o.z = pack_bf16(v[i + 4], v[i + 5]); o.w = pack_bf16(v[i + 6], v[i + 7]);
-                *reinterpret_cast<uint4*>(y + i) = o;
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (i < nv) y[i] = __float2bfloat16_rn(v[i]);
-            }
-          } else {
-            __half* y = reinterpret_cast<__half*>(yrow);
-            if (vec) {
-#pragma unroll
-              for (int i = 0; i < 32; i += 8) {
-                __half2 h0 = __floats2half2_rn(v[i], v[i + 1]), h1 = __floats2half2_rn(v[i + 2], v[i + 3]),
-                        h2 = __floats2half2_rn(v[i + 4], v[i + 5]), h3 = __floats2half2_rn(v[i + 6], v[i + 7]);
-                uint4 o;
-                o.x = *reinterpret_cast<uint32_t*>(&h0); o.y = *reinterpret_cast<uint32_t*>(&h1);
-                o.z = *reinterpret_cast<uint32_t*>(&h2); o.w = *reinterpret_cast<uint32_t*>(&h3);
-                *reinterpret_cast<uint4*>(y + i) = o;
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (i < nv) y[i] = __float2half_rn(v[i]);
-            }
-          }
           }
         }
       }
@@ -579,43 +601,28 @@ int xbuf_get(cudaStream_t st, size_t bytes, void** out) {
   return SF_OK;
 }
 
-struct TcChoice {
-  int MT, BN;
-};
-
-// Tile shape: fewest tile-rounds per SM, weighing a 128-token tile (MT = 1)
-// by the extra dequant work per MAC and a 128-column tile by its extra
-// shared-memory operand traffic.
-TcChoice choose_tile(int T, int N, int sms) {
-  const int cand[4][2] = {{2, 256}, {2, 128}, {1, 256}, {1, 128}};
-  TcChoice best{2, 128};
-  double best_cost = 1e300;
-  for (auto& c : cand) {
-    if (c[0] == 2 && T <= 128) continue;  // a second 128-token slice would hold no tokens
-    const long long mt = (T + 128 * c[0] - 1) / (128 * c[0]), nt = (N + c[1] - 1) / c[1];
-    const long long rounds = (mt * nt + sms - 1) / sms;
-    double cost = (double)rounds * 128.0 * c[0] * c[1];
-    if (c[0] == 1) cost *= 1.25;
-    if (c[1] == 128) cost *= 1.1;
-    if (cost < best_cost) { best_cost = cost; best = {c[0], c[1]}; }
-  }
-  return best;
+// Token-tile width: fewest tile rounds per SM, weighing a 128-token tile by
+// its double dequant work per MAC (each weight tile is dequantized once per
+// token tile) and a 256-token tile by its epilogue, which does not overlap
+// the next tile's main loop (one accumulator buffer).
+int choose_bt(int T, int N, int sms) {
+  const long long nt = (N + 127) / 128;
+  const long long r128 = ((T + 127) / 128 * nt + sms - 1) / sms;
+  const long long r256 = ((T + 255) / 256 * nt + sms - 1) / sms;
+  const double c128 = (double)r128 * 128 * 1.3, c256 = (double)r256 * 256 * 1.05;
+  return (T > 128 && c256 <= c128) ? 256 : 128;
 }
 
-template <int MT, int BN, bool ASYM>
+template <int BT, bool ASYM>
 int launch_tc(const CUtensorMap& mx, const CUtensorMap& mw, TcParams& p, int sms, cudaStream_t st) {
-  using L = TcLayout<MT, BN>;
-  int S = (int)((kSmemLimit - 1024 - 512) / L::STAGE);
-  if (S > 6) S = 6;
-  if (S < 2) return SF_ERR_UNSUPPORTED;
-  p.stages = S;
-  const size_t smem = 1024 + (size_t)S * L::STAGE + 512;
-  auto* fn = q4_gemm_tc_kernel<MT, BN, ASYM>;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  using L = TcLayout<BT>;
+  p.stages = L::S;
+  auto* fn = q4_gemm_tc_kernel<BT, ASYM>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::SMEM);
   if (e != cudaSuccess) return cuda_fail(e, "q4_gemm_tc_kernel smem attribute");
   const int tiles = p.mtiles * p.ntiles;
   const int grid = tiles < sms ? tiles : sms;
-  fn<<<grid, kThreads, smem, st>>>(mx, mw, p);
+  fn<<<grid, kThreads, L::SMEM, st>>>(mx, mw, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "q4_gemm_tc_kernel launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -631,7 +638,7 @@ int run_tc_gemm(const uint8_t* W, const float* S, const float* Z, const float* b
   if (T < kTcMinT && !getenv("SF_TC_FORCE")) return SF_ERR_UNSUPPORTED;
   // Shapes this kernel takes: whole 64-k blocks, a group size that keeps each
   // 32-k half inside one group, 16-byte aligned weights and activations.
-  if (K % kBK || gs % 32 || ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(X)) & 15))
+  if (K % kBK || gs % 32 || (gs & (gs - 1)) || ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(X)) & 15))
     return SF_ERR_UNSUPPORTED;
   DeviceInfo& di = device_info();
   if (di.smem_optin < kSmemLimit) return SF_ERR_UNSUPPORTED;
@@ -651,32 +658,25 @@ int run_tc_gemm(const uint8_t* W, const float* S, const float* Z, const float* b
     xb = buf;
   }
 
-  const TcChoice c = choose_tile(T, N, di.sms);
+  const int BT = choose_bt(T, N, di.sms);
   CUtensorMap mx, mw;
-  if (!make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xb, (uint64_t)K, (uint64_t)T, (uint64_t)K * 2, kBK, 128,
-                CU_TENSOR_MAP_SWIZZLE_128B))
+  if (!make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xb, (uint64_t)K, (uint64_t)T, (uint64_t)K * 2, kBK,
+                (uint32_t)BT, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(SF_ERR_CUDA, "cuTensorMapEncodeTiled failed for the prefill activations (T=%d K=%d)", T, K);
   if (!make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, kBK / 2,
-                (uint32_t)c.BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+                128, CU_TENSOR_MAP_SWIZZLE_32B))
     return fail(SF_ERR_CUDA, "cuTensorMapEncodeTiled failed for the prefill weights (N=%d K=%d)", N, K);
 
   TcParams p{};
   p.S = S; p.Z = Z; p.bias = bias; p.Y = Y;
-  p.T = T; p.N = N; p.K = K; p.G = K / gs; p.gs = gs; p.ydt = ydt;
-  p.mtiles = (T + 128 * c.MT - 1) / (128 * c.MT);
-  p.ntiles = (N + c.BN - 1) / c.BN;
+  p.T = T; p.N = N; p.K = K; p.G = K / gs; p.gs = gs; p.lg2gs = __builtin_ctz((unsigned)gs); p.ydt = ydt;
+  p.mtiles = (T + BT - 1) / BT;
+  p.ntiles = (N + 127) / 128;
   p.kblocks = K / kBK;
   const bool asym = Z != nullptr;
-#define SF_TC_CASE(MT_, BN_)                                                         \
-  if (c.MT == MT_ && c.BN == BN_)                                                    \
-    return asym ? launch_tc<MT_, BN_, true>(mx, mw, p, di.sms, stream)               \
-                : launch_tc<MT_, BN_, false>(mx, mw, p, di.sms, stream);
-  SF_TC_CASE(2, 256)
-  SF_TC_CASE(2, 128)
-  SF_TC_CASE(1, 256)
-  SF_TC_CASE(1, 128)
-#undef SF_TC_CASE
-  return SF_ERR_UNSUPPORTED;
+  if (BT == 256)
+    return asym ? launch_tc<256, true>(mx, mw, p, di.sms, stream) : launch_tc<256, false>(mx, mw, p, di.sms, stream);
+  return asym ? launch_tc<128, true>(mx, mw, p, di.sms, stream) : launch_tc<128, false>(mx, mw, p, di.sms, stream);
 }
 
 }  // namespace sf
