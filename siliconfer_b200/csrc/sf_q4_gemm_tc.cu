@@ -74,6 +74,7 @@ struct TcParams {
   void* Y;
   int T, N, K, G, gs, lg2gs, ydt;
   int mtiles, ntiles, kblocks, stages;
+  int dbg;  // development switches (SF_TC_DBG): 1 = no dequant work, 2 = no MMAs
 };
 
 // ---------------------------------------------------------------------------
@@ -395,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t acol = tmem + L::A_COL + 32 * s;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
-            mma_bf16_ts(dcol, acol + 8 * kk, sw128_desc(st + kk * 32), idesc, (kb | kk) != 0);
+            if (!(p.dbg & 2)) mma_bf16_ts(dcol, acol + 8 * kk, sw128_desc(st + kk * 32), idesc, (kb | kk) != 0);
           issued = 1;
           mma_commit(empty0 + 8 * s);
         }
@@ -444,6 +445,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         ld2(srow, kb + kDqLanes, sn);
         if (ASYM) ld2(zrow, kb + kDqLanes, zn);
         if (!bar_wait(full0 + 8 * s, ph, kErrDq, abort_flag)) { ok = false; break; }
+        if (p.dbg & 1) {
+          __syncwarp();
+          if (lane == 0) bar_arrive(dq0 + 8 * s);
+          continue;
+        }
         tc_fence_after();
         const uint32_t st = base + s * L::STAGE;
         // packed row r: 32 bytes in the 32-byte swizzle (16-byte chunk c at c ^ ((r >> 2) & 1))
@@ -673,6 +679,7 @@ int run_tc_gemm(const uint8_t* W, const float* S, const float* Z, const float* b
   p.mtiles = (T + BT - 1) / BT;
   p.ntiles = (N + 127) / 128;
   p.kblocks = K / kBK;
+  if (const char* d = getenv("SF_TC_DBG")) p.dbg = atoi(d);
   const bool asym = Z != nullptr;
   if (BT == 256)
     return asym ? launch_tc<256, true>(mx, mw, p, di.sms, stream) : launch_tc<256, false>(mx, mw, p, di.sms, stream);
