@@ -148,6 +148,39 @@ int sf_q4_linear_static_scratch(const uint8_t* W, const float* scales, const flo
                                 const float* bias, const void* X, int x_dtype, void* Y,
                                 int y_dtype, int N, int K, int T, int group_size, void* stream);
 
+/* ---- tensor parallelism across the GPUs of one node -----------------------
+ * The reference has no parallel form of Q4Linear (siliconfer/model/
+ * q4_linear.py:32-68 is single-device); these entry points replace the
+ * row-parallel projections (o_proj, down_proj; siliconfer/model/layers.py:133,
+ * 144) of a model sharded over P ranks, one process per GPU.  A
+ * column-parallel projection (q/k/v/gate/up) needs no exchange: each rank calls
+ * sf_q4_linear on its own block of rows.  A row-parallel rank owns a block of
+ * whole groups along K and calls sf_q4_linear_allreduce, which runs the GEMV
+ * into the rank's exchange buffer and sums the partials of all ranks over
+ * NVLink peer memory (rank order: every rank gets bitwise the same Y).
+ * Set-up (once per rank, collective):
+ *   sf_tp_comm_init    allocates this rank's exchange buffer (flags + two
+ *                      slots of slot_bytes) and writes its CUDA IPC handle
+ *                      (sf_tp_handle_bytes() bytes) to handle_out;
+ *   (exchange the handles between ranks, e.g. torch.distributed all_gather)
+ *   sf_tp_comm_connect opens every peer's buffer (handles: world x handle
+ *                      bytes, in rank order).
+ * Every rank must issue the same sequence of all-reduce calls.  Waits on
+ * peers are bounded (about 2 s); on expiry the kernel returns early and
+ * sf_q4_check_device_error() reports SF_ERR_TIMEOUT. */
+size_t sf_tp_handle_bytes(void);
+int sf_tp_comm_init(int rank, int world, size_t slot_bytes, void** comm_out, void* handle_out);
+int sf_tp_comm_connect(void* comm, const void* handles);
+/* Y[count] = sum over ranks of partial (fp32, device, count floats; NULL =
+   already in place) + bias[i % ncols]; out of out_dtype. */
+int sf_tp_allreduce(void* comm, const float* partial, void* out, int out_dtype, const float* bias,
+                    long long count, int ncols, void* stream);
+/* Row-parallel Q4Linear shard: Y = allreduce(X[T,K_shard] @ dequant(W_shard)^T) + bias. */
+int sf_q4_linear_allreduce(void* comm, const uint8_t* W, const float* scales, const float* zeros,
+                           const float* bias, const void* X, int x_dtype, void* Y, int y_dtype,
+                           int N, int K, int T, int group_size, void* stream);
+void sf_tp_comm_destroy(void* comm);
+
 /* Device dequant to fp32/fp16/bf16 [N, K].  fp32 output is bit-exact with
    dequantize_sym / dequantize_asym (siliconfer/quant/primitives.py:54-75,
    117-140); fp16/bf16 are that value rounded to nearest even. */

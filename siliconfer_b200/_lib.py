@@ -48,10 +48,16 @@ SIGNATURES = {
     "sf_q4_step_run": [_P, _P],
     "sf_q4_step_launch": [_P, _P, _I],
     "sf_q4_step_destroy": [_P],
+    "sf_tp_handle_bytes": [],
+    "sf_tp_comm_init": [_I, _I, _SZ, ctypes.POINTER(_P), _P],
+    "sf_tp_comm_connect": [_P, _P],
+    "sf_tp_allreduce": [_P, _P, _P, _I, _P, _LL, _I, _P],
+    "sf_q4_linear_allreduce": [_P, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P],
+    "sf_tp_comm_destroy": [_P],
 }
 _RESTYPES = {"sf_status_string": ctypes.c_char_p, "sf_last_error": ctypes.c_char_p,
              "sf_q4_launch_count": _LL, "sf_q4_step_workspace_bytes": _SZ,
-             "sf_q4_step_destroy": None}
+             "sf_q4_step_destroy": None, "sf_tp_handle_bytes": _SZ, "sf_tp_comm_destroy": None}
 
 _lib = None
 

@@ -396,7 +396,7 @@ int sf_q4_quantize_pack(const float* W, uint8_t* packed, float* scales, float* z
 
 int sf_q4_check_device_error(void) {
   const unsigned int a = take_dev_error_gemv(), b = take_dev_error_tc(),
-                     c = take_dev_error_gemv_tc() | take_dev_error_tile();
+                     c = take_dev_error_gemv_tc() | take_dev_error_tile() | take_dev_error_tp();
   if (a == 0xffffffffu || b == 0xffffffffu || c == 0xffffffffu)
     return fail(SF_ERR_CUDA, "reading the device error word failed");
   if (a | b | c) return fail(SF_ERR_TIMEOUT, "a device-side wait expired (code %u)", a | b | c);

@@ -101,6 +101,7 @@ unsigned int take_dev_error_gemv();
 unsigned int take_dev_error_gemv_tc();
 unsigned int take_dev_error_tc();
 unsigned int take_dev_error_tile();
+unsigned int take_dev_error_tp();
 
 // Decode GEMV (1 <= T <= kMaxGemvT) on the warp-unit kernel; SF_ERR_UNSUPPORTED
 // when the shape is not one it takes.

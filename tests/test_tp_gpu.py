@@ -1,0 +1,112 @@
+"""Tensor-parallel Q4Linear on 2+ GPUs of one box (one process per GPU).
+
+Row-parallel shards summed by the library's NVLink all-reduce
+(sf_q4_linear_allreduce) and by NCCL must both match the unsharded oracle
+(normwise 1e-3 for the fp32 GEMV, 5e-3 when T reaches the bf16 prefill GEMM),
+every rank must hold bitwise the same Y from the peer all-reduce, and
+alternating exchange slots must stay correct over repeated calls.  A rank
+that does not join a call makes the other rank's bounded wait expire with
+SF_ERR_TIMEOUT instead of hanging.  NVLS is off (NCCL_NVLS_ENABLE=0) and the
+peer kernel uses plain peer loads/stores.  Skipped with fewer than 2 GPUs.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    out = {"rank": rank}
+    try:
+        from oracle import q4_oracle as O
+        from siliconfer_b200 import _lib, quant as Q
+        from siliconfer_b200.tensor_parallel import ColumnParallelQ4Linear, PeerComm, RowParallelQ4Linear
+        comm = PeerComm(slot_bytes=8 << 20)
+        errs, same = [], []
+        for case, (n, k, t, asym, xdt) in enumerate([(512, 2048, 1, False, torch.float32),
+                                                     (1024, 4096, 4, True, torch.float16),
+                                                     (256, 1024, 64, False, torch.bfloat16),
+                                                     (384, 3072, 2, True, torch.float32)]):
+            rng = np.random.default_rng(100 + case)
+            w = rng.normal(0, 0.02, (n, k)).astype(np.float32)
+            p, s, z = Q.pack_weights_asym(w, 128) if asym else (*Q.pack_weights_sym(w, 128), None)
+            bias = rng.normal(0, 0.1, n).astype(np.float32)
+            peer = RowParallelQ4Linear(p, s, z, bias, 128, rank=rank, world=world, device=dev, comm=comm)
+            nccl = RowParallelQ4Linear(p, s, z, bias, 128, rank=rank, world=world, device=dev, mode="nccl")
+            col = ColumnParallelQ4Linear(p, s, z, bias, 128, rank=rank, world=world, device=dev)
+            k0, k1 = peer.k_range
+            for rep in range(3):
+                x = rng.normal(0, 1, (t, k)).astype(np.float32)
+                xd = torch.from_numpy(x).to(dev).to(xdt)
+                xq = xd.float().cpu().numpy()
+                ref = O.gemm(p, s, z, xq, 128) + bias
+                tol = 5e-3 if t >= 48 else 1e-3
+                ya = peer(xd[:, k0:k1].contiguous())
+                yb = nccl(xd[:, k0:k1].contiguous())
+                yc = col(xd)
+                torch.cuda.synchronize()
+                lo, hi = col.rows
+                errs.append((case, rep, O.normwise_rel_err(ya.cpu().numpy(), ref),
+                             O.normwise_rel_err(yb.cpu().numpy(), ref),
+                             O.normwise_rel_err(yc.cpu().numpy(), ref[:, lo:hi]), tol))
+                g = [torch.empty_like(ya) for _ in range(world)]
+                dist.all_gather(g, ya)
+                same.append(all(torch.equal(g[0], gi) for gi in g))
+        out["errs"], out["same"] = errs, same
+        out["dev_err_ok"] = _lib.load().sf_q4_check_device_error()
+        # bounded wait: rank 0 starts an all-reduce that rank 1 never joins
+        dist.barrier()
+        lib = _lib.load()
+        if rank == 0:
+            buf = torch.zeros(256, device=dev)
+            _lib.check(lib.sf_tp_allreduce(comm.comm, buf.data_ptr(), buf.data_ptr(), 0, None, 256, 256,
+                                           torch.cuda.current_stream().cuda_stream))
+            torch.cuda.synchronize()
+            out["timeout_status"] = lib.sf_q4_check_device_error()
+            out["after"] = lib.sf_q4_check_device_error()
+        dist.barrier()
+        comm.close()
+    except Exception as exc:  # reported to the parent
+        import traceback
+        out["exc"] = traceback.format_exc()
+    q.put(out)
+    dist.destroy_process_group()
+
+
+def test_row_parallel_peer_and_nccl_match_oracle():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 4)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=600) for _ in range(world)], key=lambda d: d["rank"])
+    for p in procs:
+        p.join(timeout=120)
+    for r in res:
+        assert "exc" not in r, r["exc"]
+        assert r["dev_err_ok"] == 0
+        assert all(r["same"]), "ranks disagree on the peer all-reduce result"
+        for case, rep, ea, eb, ec, tol in r["errs"]:
+            assert ea <= tol and eb <= tol and ec <= tol, (r["rank"], case, rep, ea, eb, ec)
+    assert res[0]["timeout_status"] == 7        # SF_ERR_TIMEOUT
+    assert res[0]["after"] == 0                 # the error word was read and cleared
