@@ -16,8 +16,10 @@ metric/value: algorithmic bytes per step / device time per step, in GB/s
 output).  decode_step_us is the same step as latency.
 
 With N > 1 (torchrun) every rank runs the same workload on its own GPU
-(replicas, weak scaling) unless --workload 70b selects the tensor-parallel
-70B step (column/row-parallel shards with an all-reduce after o/down).
+(replicas, weak scaling).  --workload 70b selects BASELINE config 5 instead:
+the 70B-shaped step sharded over the N GPUs (column-parallel q/k/v/gate/up,
+row-parallel o/down with an all-reduce after each; strong scaling), timed with
+this library's NVLink peer all-reduce and with NCCL.
 
 --impl reference times the reference's own CPU kernels (oracle/_ref, built
 from the reference sources; else the oracle's C port) on the host cores with
@@ -317,6 +319,167 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def run_tp(args, rank, world, local_rank):
+    """70B-shaped decode step sharded over `world` GPUs.
+
+    q/k/v/gate/up column-parallel, o/down row-parallel with one all-reduce of
+    [batch, 8192] after each (160 per step).  Both exchanges are timed: this
+    library's NVLink peer all-reduce (headline) and NCCL (baseline)."""
+    import torch
+    from siliconfer_b200 import _lib
+    from siliconfer_b200.tensor_parallel import PeerComm, TPStepRunner
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist = None
+    comm = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=device)
+        n_layers = args.layers or HIDDEN[args.workload][2]
+        comm = PeerComm(slot_bytes=max(1 << 20, args.batch * 8192 * 4),
+                        arena_bytes=TPStepRunner.arena_bytes(n_layers, args.batch, HIDDEN[args.workload][0], world))
+    t_build = time.perf_counter()
+    flat = build_layers(args.workload, device, tp_rank=rank, tp_size=world, seed=1234 + 7919 * rank,
+                        n_layers=args.layers)
+    groups = [flat[i:i + 7] for i in range(0, len(flat), 7)]
+    runners = {"fused": TPStepRunner(groups, tokens=args.batch, x_dtype=torch.bfloat16, mode="fused",
+                                     comm=comm, device=device)}
+    if world > 1:
+        runners["peer"] = TPStepRunner(groups, tokens=args.batch, x_dtype=torch.bfloat16, mode="peer",
+                                       comm=comm, device=device)
+        runners["nccl"] = TPStepRunner(groups, tokens=args.batch, x_dtype=torch.bfloat16, mode="nccl",
+                                       device=device)
+    g = torch.Generator(device=device)
+    g.manual_seed(7 + rank)
+    for r in runners.values():
+        r.x.copy_(torch.randn(r.x.shape, generator=g, device=device).to(r.x.dtype))
+        r.x_host.copy_(r.x.cpu())
+        r.capture()
+    build_s = time.perf_counter() - t_build
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+            torch.cuda.synchronize(device)
+
+    def timed(r, n):
+        for _ in range(args.warmup):
+            r.run()
+        r.stream.synchronize()
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(r.stream)
+        for _ in range(n):
+            r.run()
+        s1.record(r.stream)
+        s1.synchronize()
+        barrier()
+        return s0.elapsed_time(s1) / n
+
+    main_r = runners["fused"]
+    for _ in range(args.warmup):
+        main_r.run()
+    main_r.stream.synchronize()
+    barrier()
+    with ClockSampler(local_rank) as clocks:
+        t_end = time.perf_counter() + 5.0
+        while len(clocks.lines) < 2 and time.perf_counter() < t_end:
+            main_r.run()
+            main_r.stream.synchronize()
+        ms = timed(main_r, args.steps)
+    nccl_ms = timed(runners["nccl"], args.steps) if "nccl" in runners else None
+    peer_ms = timed(runners["peer"], args.steps) if "peer" in runners else None
+    # end to end: pinned host activations in, all-reduced outputs out
+    for _ in range(args.warmup):
+        main_r.run_host()
+    main_r.stream.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(main_r.stream)
+    for _ in range(args.steps):
+        main_r.run_host()
+    e1.record(main_r.stream)
+    e1.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    dev_err = _lib.load().sf_q4_check_device_error()
+    if dev_err != 0:
+        raise RuntimeError(f"device-side wait expired during the bench (status {dev_err})")
+    step_bytes = main_r.algorithmic_bytes()
+    if dist is not None:
+        t = torch.tensor([ms, e2e_ms, nccl_ms or 0.0, peer_ms or 0.0, float(step_bytes)], device=device,
+                         dtype=torch.float64)
+        tmax = t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        tsum = t.clone()
+        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+        ms, e2e_ms, nccl_ms, peer_ms = tmax[0].item(), tmax[1].item(), tmax[2].item(), tmax[3].item()
+        total_bytes = int(tsum[4].item())
+    else:
+        total_bytes = step_bytes
+    peak, peak_kind = measured_peak()
+    value = total_bytes / (ms * 1e-3) / 1e9
+    per_gpu = step_bytes / (ms * 1e-3) / 1e9
+    xin = main_r.x.numel() * main_r.x.element_size()
+    yout = main_r.red.numel() * 4
+    result = {
+        "metric": f"int4 GEMV HBM GB/s, {args.workload} tensor-parallel decode step (batch {args.batch})",
+        "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 5), "decode_step_us": round(ms * 1e3, 2),
+        "decode_step_us_nccl": None if nccl_ms is None else round(nccl_ms * 1e3, 2),
+        "decode_step_us_unfused_peer": None if peer_ms is None else round(peer_ms * 1e3, 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int4 weights (u8 nibbles) x bf16 activations, exact int32 products, fp32 accumulate",
+        "data": "synthetic: seeded N(0,0.02) weights per shard, RTN int4 sym g128 (device pack); bf16 N(0,1) activations",
+        "config": {"workload": f"BASELINE config 5: {args.workload}-shaped decode step, {len(groups)} layers x 7 "
+                               f"projections sharded over {world} GPU(s), each projection reading its own "
+                               f"pre-supplied input",
+                   "batch": args.batch, "group_size": 128, "layout": "sym",
+                   "parallelism": f"tp{world}: q/k/v/gate/up column-parallel, o/down row-parallel + "
+                                  f"all-reduce ({2 * len(groups)} per step); headline: the whole step as one "
+                                  f"persistent launch with the all-reduces fused (tiles pushed over NVLink); "
+                                  f"beside it: one launch per half layer + peer all-reduce kernel, and + NCCL",
+                   "l2": "weights >> L2 (no flush needed)"},
+        "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(per_gpu / peak, 4), "peak_kind": peak_kind,
+                     "kernel": "whole step per GPU (one persistent GEMV launch with fused all-reduces)",
+                     "bytes_per_launch": step_bytes, "traffic": None},
+        "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": xin, "d2h_bytes_per_step": yout,
+                "api": "siliconfer_b200.tensor_parallel.TPStepRunner.run_host (pinned host in/out)"},
+        "gpu_launches": main_r.launches_per_step() * args.steps,
+        "clocks": clocks.summary(),
+        "build_s": round(build_s, 1),
+    }
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    _teardown(dist, comm, runners, main_r)
+
+
+def _teardown(dist, comm, runners, *refs):
+    """Release captured graphs before the process group, then exit.  A
+    watchdog ends the process if a library's teardown blocks (the result line
+    is already printed)."""
+    import gc
+    import torch
+    def _force_exit():
+        time.sleep(60)
+        os._exit(0)
+    threading.Thread(target=_force_exit, daemon=True).start()
+    torch.cuda.synchronize()
+    runners.clear()
+    del refs
+    gc.collect()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    if comm is not None:
+        comm.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def traffic_from_profile(workload, batch):
     """DRAM bytes per launch of the GEMV kernel, from the committed ncu summary
     (profiles/traffic.txt: lines "<workload>_b<batch> <bytes> <how>"), if any."""
@@ -437,6 +600,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         run_reference(args, rank, world)
+    elif args.workload == "70b":
+        run_tp(args, rank, world, local_rank)
     else:
         run_ours(args, rank, world, local_rank)
 

@@ -40,7 +40,10 @@ typedef enum {
   SF_ERR_CUDA = 5,        /* a CUDA runtime call failed                        */
   SF_ERR_UNSUPPORTED = 6, /* valid request this build does not implement       */
   SF_ERR_TIMEOUT = 7,     /* a device-side bounded wait expired                */
-  SF_ERR_COMM = 8         /* tensor-parallel peer exchange failed              */
+  SF_ERR_COMM = 8,        /* tensor-parallel peer exchange failed              */
+  SF_ERR_CAPTURE = 9      /* library scratch must grow while the stream is being
+                             captured: run the same shape once on that stream
+                             before capturing                                  */
 } sf_status;
 
 typedef enum { SF_F32 = 0, SF_F16 = 1, SF_BF16 = 2 } sf_dtype;
@@ -159,8 +162,10 @@ int sf_q4_linear_static_scratch(const uint8_t* W, const float* scales, const flo
  * into the rank's exchange buffer and sums the partials of all ranks over
  * NVLink peer memory (rank order: every rank gets bitwise the same Y).
  * Set-up (once per rank, collective):
- *   sf_tp_comm_init    allocates this rank's exchange buffer (flags + two
- *                      slots of slot_bytes) and writes its CUDA IPC handle
+ *   sf_tp_comm_init    allocates this rank's exchange buffer (flags, two
+ *                      slots of slot_bytes, then arena_bytes for the
+ *                      regions of fused step tasks, see
+ *                      sf_q4_step_create_tp) and writes its CUDA IPC handle
  *                      (sf_tp_handle_bytes() bytes) to handle_out;
  *   (exchange the handles between ranks, e.g. torch.distributed all_gather)
  *   sf_tp_comm_connect opens every peer's buffer (handles: world x handle
@@ -169,7 +174,8 @@ int sf_q4_linear_static_scratch(const uint8_t* W, const float* scales, const flo
  * peers are bounded (about 2 s); on expiry the kernel returns early and
  * sf_q4_check_device_error() reports SF_ERR_TIMEOUT. */
 size_t sf_tp_handle_bytes(void);
-int sf_tp_comm_init(int rank, int world, size_t slot_bytes, void** comm_out, void* handle_out);
+int sf_tp_comm_init(int rank, int world, size_t slot_bytes, size_t arena_bytes, void** comm_out,
+                    void* handle_out);
 int sf_tp_comm_connect(void* comm, const void* handles);
 /* Y[count] = sum over ranks of partial (fp32, device, count floats; NULL =
    already in place) + bias[i % ncols]; out of out_dtype. */
@@ -180,6 +186,32 @@ int sf_q4_linear_allreduce(void* comm, const uint8_t* W, const float* scales, co
                            const float* bias, const void* X, int x_dtype, void* Y, int y_dtype,
                            int N, int K, int T, int group_size, void* stream);
 void sf_tp_comm_destroy(void* comm);
+
+/* A tensor-parallel decode step as ONE persistent launch, the all-reduces
+ * fused into the GEMV kernel.  Same tasks as sf_q4_step_create plus a role
+ * per task:
+ *   SF_ROLE_GEMV        an ordinary GEMV (column-parallel projections);
+ *   SF_ROLE_PUSH        a row-parallel shard: each finished 32-row tile of its
+ *                       fp32 partial is stored into every rank's exchange
+ *                       region over NVLink (peer stores), followed by a
+ *                       per-tile flag; Y may be NULL;
+ *   SF_ROLE_REDUCE + i  the all-reduce of earlier task i (a PUSH task of the
+ *                       same N): waits (bounded) for every rank's flag of each
+ *                       tile, sums the ranks in rank order (+ bias) and
+ *                       writes Y of y_dtype.  Give it task i's W, scales,
+ *                       zeros, X, K and group_size (unused) and its own Y,
+ *                       bias and y_dtype.
+ * Regions are carved from the communicator's arena at creation (the same
+ * task lists on every rank give the same offsets), two parities per region
+ * so that consecutive runs never overwrite data a peer is still reading.
+ * Every rank must create the same step and run it the same number of times;
+ * the launch is cooperative.  The workspace is sized by
+ * sf_q4_step_workspace_bytes on the same task list. */
+#define SF_ROLE_GEMV 0
+#define SF_ROLE_PUSH 1
+#define SF_ROLE_REDUCE 2
+int sf_q4_step_create_tp(const sf_q4_task* tasks, const int* roles, int ntasks, void* comm,
+                         void* workspace, size_t workspace_bytes, void** handle_out);
 
 /* Device dequant to fp32/fp16/bf16 [N, K].  fp32 output is bit-exact with
    dequantize_sym / dequantize_asym (siliconfer/quant/primitives.py:54-75,

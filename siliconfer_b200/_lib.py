@@ -49,7 +49,8 @@ SIGNATURES = {
     "sf_q4_step_launch": [_P, _P, _I],
     "sf_q4_step_destroy": [_P],
     "sf_tp_handle_bytes": [],
-    "sf_tp_comm_init": [_I, _I, _SZ, ctypes.POINTER(_P), _P],
+    "sf_tp_comm_init": [_I, _I, _SZ, _SZ, ctypes.POINTER(_P), _P],
+    "sf_q4_step_create_tp": [ctypes.POINTER(Q4Task), ctypes.POINTER(_I), _I, _P, _P, _SZ, ctypes.POINTER(_P)],
     "sf_tp_comm_connect": [_P, _P],
     "sf_tp_allreduce": [_P, _P, _P, _I, _P, _LL, _I, _P],
     "sf_q4_linear_allreduce": [_P, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P],

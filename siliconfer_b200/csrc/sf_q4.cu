@@ -310,6 +310,7 @@ const char* sf_status_string(int status) {
     case SF_ERR_UNSUPPORTED: return "unsupported";
     case SF_ERR_TIMEOUT: return "device wait timed out";
     case SF_ERR_COMM: return "peer exchange failed";
+    case SF_ERR_CAPTURE: return "scratch must grow during stream capture";
     default: return "unknown status";
   }
 }

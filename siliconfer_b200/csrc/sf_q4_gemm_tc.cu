@@ -590,8 +590,9 @@ int xbuf_get(cudaStream_t st, size_t bytes, void** out) {
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(st, &cs);
     if (cs != cudaStreamCaptureStatusNone)
-      return fail(SF_ERR_UNSUPPORTED,
-                  "prefill activation buffer must grow during stream capture: run the same shape once before capturing");
+      return fail(SF_ERR_CAPTURE,
+                  "prefill activation buffer must grow during stream capture: run the same shape once on the "
+                  "capturing stream before capturing");
     if (e.first) {
       cudaStreamSynchronize(st);
       cudaFree(e.first);

@@ -103,6 +103,14 @@ unsigned int take_dev_error_tc();
 unsigned int take_dev_error_tile();
 unsigned int take_dev_error_tp();
 
+// Carves one exchange region for a pushed task from a tensor-parallel
+// communicator's arena (same order on every rank, so the same offsets):
+// data = 2 parities x world x `src_bytes`, then `tiles` x world u64 flags.
+// Fills every rank's mapped data/flag pointers, this rank, the world size and
+// the byte size of one parity half.
+int tp_region(void* comm, size_t src_bytes, size_t tiles, uint8_t** data, unsigned long long** flags, int* rank,
+              int* world, size_t* par_bytes);
+
 // Decode GEMV (1 <= T <= kMaxGemvT) on the warp-unit kernel; SF_ERR_UNSUPPORTED
 // when the shape is not one it takes.
 int run_tile_linear(const uint8_t* W, const float* S, const float* Z, const float* bias,

@@ -126,6 +126,16 @@ struct alignas(64) TileTask {
   // phase has written all its tiles.  Phase 0 reads inputs that exist at launch.
   int phase, ph_first, ph_tiles, ph_chunks, ph_last;
   long long ph_ubase, ph_units;
+  // Tensor-parallel exchange (row-parallel projections), see sf_q4_step_create_tp:
+  //  kind 0: GEMV; push != 0: its fp32 tiles go to every rank's exchange
+  //          region (data[parity][src rank][T][N]) instead of Y, each tile
+  //          followed by flag[tile][src] = launch epoch in every rank;
+  //  kind 1: all-reduce of a pushed task: waits for flag[tile][*] >= epoch in
+  //          this rank's region, sums the ranks in order (+ bias), writes Y.
+  int kind, push, tp_rank, tp_world;
+  size_t xpar;                         // bytes of one parity half of a region's data
+  uint8_t* xdata[8];                   // region data of every rank, as mapped here
+  unsigned long long* xflag[8];        // region flags of every rank, as mapped here
 };
 
 struct TileLaunch {
@@ -138,6 +148,7 @@ struct TileLaunch {
   int prefetch;           // pull a waiting unit's weights into L2 before the wait
   int dbg;                // development: 2 = copies only, 3 = arithmetic only (wrong results)
   unsigned long long* trace;   // development: per unit [start, dependency met, inputs ready, end] ns
+  unsigned long long* epoch;   // launch counter (tensor-parallel exchange), advanced by the pre-pass, or null
 };
 
 __device__ __forceinline__ const TileTask* tile_task(const TileLaunch& L, int i) {
@@ -398,6 +409,32 @@ __device__ __forceinline__ void publish(unsigned int* flags, int word, unsigned 
     asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(flags + c * 32 + word), "r"(val) : "memory");
 }
 
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long launch_epoch(const TileLaunch& L) {
+  return *reinterpret_cast<volatile const unsigned long long*>(L.epoch);
+}
+// One fp32 value of a pushed task's tile into every rank's region (peer stores).
+__device__ __forceinline__ void push_val(const TileTask* p, unsigned long long ep, int T, int tok, int row, float v) {
+  const size_t off = (size_t)(ep & 1) * p->xpar + (((size_t)p->tp_rank * T + tok) * p->N + row) * 4;
+  for (int q = 0; q < p->tp_world; ++q) __stcg(reinterpret_cast<float*>(p->xdata[q] + off), v);
+}
+// The warp's pushes of one tile are complete: flag it in every rank (whole warp).
+__device__ __forceinline__ void push_flag(const TileTask* p, unsigned long long ep, int tile, int lane) {
+  __syncwarp();
+  if (lane < p->tp_world) {
+    __threadfence_system();
+    st_release_sys_u64(p->xflag[lane] + (size_t)tile * p->tp_world + p->tp_rank, ep);
+  }
+  __syncwarp();
+}
+
 // A 32-row tile of task p has been written (whole warp): count it towards its
 // phase; the tile that completes the phase tells every CTA.
 __device__ __forceinline__ void tile_written(const TileLaunch& L, const TileTask* p, int lane) {
@@ -478,6 +515,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
   }
 
   const long long W_all = (long long)gridDim.x * (blockDim.x >> 5);
+  const unsigned long long ep = L.epoch ? launch_epoch(L) : 0ull;   // this launch's exchange epoch
   uint32_t gseg = 0;   // segments this warp has consumed (ring position and phase)
   int ti = 0;
   bool ok = true;
@@ -548,6 +586,36 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       if (!ok) break;
     }
 
+    if (p->kind == 1) {
+      // ---- all-reduce of a pushed task: tile = lu (one unit per 32-row tile) ----
+      const unsigned long long* fl = p->xflag[p->tp_rank] + (size_t)lu * p->tp_world;
+      int okf = 1;
+      if (lane < p->tp_world && ld_acquire_sys_u64(fl + lane) < ep) {
+        const long long t0 = clock64();
+        while (ld_acquire_sys_u64(fl + lane) < ep) {
+          if (clock64() - t0 > kWaitCycles) {
+            atomicOr(&g_dev_error, 0x2000u);
+            okf = 0;
+            break;
+          }
+          __nanosleep(32);
+        }
+      }
+      ok = __all_sync(0xffffffffu, okf) != 0;
+      if (!ok) break;
+      const int row = lu * kUnitRows + lane;
+      if (row < N) {
+        const float bv = p->bias ? __ldg(p->bias + row) : 0.f;
+        const float* src = reinterpret_cast<const float*>(p->xdata[p->tp_rank] + (size_t)(ep & 1) * p->xpar);
+        for (int tok = 0; tok < T; ++tok) {
+          float a = 0.f;
+          for (int q = 0; q < p->tp_world; ++q) a += __ldcv(src + ((size_t)q * T + tok) * N + row);
+          st_y(p->Y, (size_t)tok * N + row, a + bv, p->ydt);
+        }
+      }
+      tile_written(L, p, lane);
+      continue;
+    }
     if (tr && lane == 0) tr[2] = globaltimer_ns();
     // ---- operand streaming ---------------------------------------------------
     // Stage j holds k [kb + 256 j, kb + 256 j + 256): the weight tile, the
@@ -727,11 +795,13 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
               const int row = r0 + rloc[2 * mt + h];
               if (row < N) {
                 const float a = acc[mt][tg][h];
-                st_y(p->Y, (size_t)tok * N + row, p->bias ? a + __ldg(p->bias + row) : a, p->ydt);
+                if (p->push) push_val(p, ep, T, tok, row, a);
+                else st_y(p->Y, (size_t)tok * N + row, p->bias ? a + __ldg(p->bias + row) : a, p->ydt);
               }
             }
         }
       }
+      if (p->push) push_flag(p, ep, tile, lane);
       tile_written(L, p, lane);
     } else {
 #pragma unroll
@@ -771,9 +841,11 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
 #pragma unroll
               for (int j = 0; j < 8; ++j) a += v[j];
             }
-            st_y(p->Y, (size_t)tok * N + row, a + bv, p->ydt);
+            if (p->push) push_val(p, ep, T, tok, row, a);
+            else st_y(p->Y, (size_t)tok * N + row, a + bv, p->ydt);
           }
         }
+        if (p->push) push_flag(p, ep, tile, lane);
         tile_written(L, p, lane);
       }
     }
@@ -783,10 +855,13 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
 // Activation blocks of the tasks whose input exists at launch: one CTA per task.
 template <int T, int LB>
 __global__ void __launch_bounds__(256) q4_xblocks_kernel(const __grid_constant__ TileLaunch L) {
+  if (L.epoch && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *L.epoch += 1;   // next exchange epoch
   const TileTask* p = tile_task(L, blockIdx.x);
   if (!p->xpre) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int c = warp; c < p->nchunk; c += blockDim.x >> 5) convert_chunk<T, LB>(p, c, lane);
+  // blockIdx.y spreads one task's chunks over several CTAs
+  const int wpb = blockDim.x >> 5;
+  for (int c = blockIdx.y * wpb + warp; c < p->nchunk; c += gridDim.y * wpb) convert_chunk<T, LB>(p, c, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -960,24 +1035,28 @@ cudaError_t launch_tile(const TileConfig& c, const TileLaunch& L, bool coop, cud
 }
 
 template <int LB>
-cudaError_t launch_xblocks_lb(int T, int ntasks, const TileLaunch& L, cudaStream_t st) {
+cudaError_t launch_xblocks_lb(int T, int ntasks, const TileLaunch& L, cudaStream_t st, int ny) {
+  const dim3 grid((unsigned)ntasks, (unsigned)(ny < 1 ? 1 : ny));
   switch (T) {
-    case 1: q4_xblocks_kernel<1, LB><<<ntasks, 256, 0, st>>>(L); break;
-    case 2: q4_xblocks_kernel<2, LB><<<ntasks, 256, 0, st>>>(L); break;
-    case 3: q4_xblocks_kernel<3, LB><<<ntasks, 256, 0, st>>>(L); break;
-    case 4: q4_xblocks_kernel<4, LB><<<ntasks, 256, 0, st>>>(L); break;
-    case 5: q4_xblocks_kernel<5, LB><<<ntasks, 256, 0, st>>>(L); break;
-    case 6: q4_xblocks_kernel<6, LB><<<ntasks, 256, 0, st>>>(L); break;
-    case 7: q4_xblocks_kernel<7, LB><<<ntasks, 256, 0, st>>>(L); break;
-    default: q4_xblocks_kernel<8, LB><<<ntasks, 256, 0, st>>>(L); break;
+    case 1: q4_xblocks_kernel<1, LB><<<grid, 256, 0, st>>>(L); break;
+    case 2: q4_xblocks_kernel<2, LB><<<grid, 256, 0, st>>>(L); break;
+    case 3: q4_xblocks_kernel<3, LB><<<grid, 256, 0, st>>>(L); break;
+    case 4: q4_xblocks_kernel<4, LB><<<grid, 256, 0, st>>>(L); break;
+    case 5: q4_xblocks_kernel<5, LB><<<grid, 256, 0, st>>>(L); break;
+    case 6: q4_xblocks_kernel<6, LB><<<grid, 256, 0, st>>>(L); break;
+    case 7: q4_xblocks_kernel<7, LB><<<grid, 256, 0, st>>>(L); break;
+    default: q4_xblocks_kernel<8, LB><<<grid, 256, 0, st>>>(L); break;
   }
   return cudaGetLastError();
 }
 
-cudaError_t launch_xblocks(int T, int LB, int ntasks, const TileLaunch& L, cudaStream_t st) {
-  if (LB == 16) return launch_xblocks_lb<16>(T, ntasks, L, st);
-  if (LB == 8) return launch_xblocks_lb<8>(T, ntasks, L, st);
-  return launch_xblocks_lb<4>(T, ntasks, L, st);
+// ny: CTAs per task (each converts every ny-th run of 8 chunks); chunks per
+// task = T*K/256, so ny = ceil(chunks / 8) gives every warp one chunk.
+cudaError_t launch_xblocks(int T, int LB, int ntasks, const TileLaunch& L, cudaStream_t st, int ny) {
+  if (ny > 64) ny = 64;
+  if (LB == 16) return launch_xblocks_lb<16>(T, ntasks, L, st, ny);
+  if (LB == 8) return launch_xblocks_lb<8>(T, ntasks, L, st, ny);
+  return launch_xblocks_lb<4>(T, ntasks, L, st, ny);
 }
 
 // Library-owned scratch of the single-GEMV entry, one pair of buffers per
@@ -1001,8 +1080,9 @@ int grow(cudaStream_t st, void** buf, size_t* have, size_t need, bool zero) {
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   cudaStreamIsCapturing(st, &cs);
   if (cs != cudaStreamCaptureStatusNone)
-    return fail(SF_ERR_UNSUPPORTED,
-                "GEMV scratch must grow during stream capture: run the same shape once before capturing");
+    return fail(SF_ERR_CAPTURE,
+                "GEMV scratch must grow during stream capture: run the same shape once on the capturing "
+                "stream before capturing");
   if (*buf) {
     cudaStreamSynchronize(st);
     cudaFree(*buf);
@@ -1076,7 +1156,7 @@ int run_tile_linear(const uint8_t* W, const float* S, const float* Z, const floa
   L.dbg = 0;
   const int need = (int)((L.total + c.wpc - 1) / c.wpc);
   if (c.grid > need) c.grid = need;
-  cudaError_t e = launch_xblocks(T, c.LB, 1, L, stream);
+  cudaError_t e = launch_xblocks(T, c.LB, 1, L, stream, (q.nchunk + 7) / 8);
   if (e != cudaSuccess) return cuda_fail(e, "activation pre-pass launch");
   e = launch_tile(c, L, false, stream);
   if (e != cudaSuccess) return cuda_fail(e, "q4_tile_kernel launch");
@@ -1143,12 +1223,16 @@ StepSizes step_sizes(const sf_q4_task* tasks, int n, const std::vector<int>& ksp
   return z;
 }
 
+constexpr size_t kEpochBytes = 256;   // launch epoch of a step with exchange tasks (after the workspace)
+
 struct StepHandle {
   TileConfig cfg;
   TileLaunch L;
   void* workspace;
   size_t clear_bytes;
   bool coop, prepass;
+  int xny;                  // pre-pass CTAs per task (largest task's chunks / 8)
+  bool tp;                  // has tensor-parallel exchange tasks (epoch at the workspace end)
 };
 
 bool step_config(const sf_q4_task* tasks, TileConfig& c) {
@@ -1165,11 +1249,14 @@ size_t sf_q4_step_workspace_bytes(const sf_q4_task* tasks, int ntasks) {
       return 0;
   TileConfig c;
   if (!step_config(tasks, c)) return 0;
-  return step_sizes(tasks, ntasks, plan_ksplit(tasks, ntasks, c.grid * c.wpc), c.grid).total();
+  return step_sizes(tasks, ntasks, plan_ksplit(tasks, ntasks, c.grid * c.wpc), c.grid).total() + kEpochBytes;
 }
 
-int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size_t workspace_bytes,
-                      void** handle_out) {
+}  // extern "C"
+
+namespace {
+int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void* comm, void* workspace,
+                     size_t workspace_bytes, void** handle_out) {
   if (!tasks || !workspace || !handle_out) return fail(SF_ERR_NULL, "null pointer argument");
   if (ntasks < 1) return fail(SF_ERR_SHAPE, "ntasks must be >= 1");
   if (reinterpret_cast<uintptr_t>(workspace) & 255)
@@ -1177,9 +1264,23 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
   const int T = tasks[0].T;
   const bool asym = tasks[0].zeros != nullptr;
   if (T < 1 || T > kMaxGemvT) return fail(SF_ERR_UNSUPPORTED, "step tasks need 1 <= T <= %d", kMaxGemvT);
+  bool has_tp = false;
   for (int i = 0; i < ntasks; ++i) {
     const sf_q4_task& a = tasks[i];
-    if (!a.W || !a.scales || !a.X || !a.Y) return fail(SF_ERR_NULL, "task %d: null pointer", i);
+    const int role = roles ? roles[i] : SF_ROLE_GEMV;
+    if (role != SF_ROLE_GEMV) {
+      has_tp = true;
+      if (!comm) return fail(SF_ERR_NULL, "task %d: an exchange role needs a tensor-parallel communicator", i);
+      if (role >= SF_ROLE_REDUCE) {
+        const int src = role - SF_ROLE_REDUCE;
+        if (src >= i || roles[src] != SF_ROLE_PUSH || tasks[src].N != a.N)
+          return fail(SF_ERR_SHAPE, "task %d: reduce role must name an earlier pushed task of the same N", i);
+      } else if (role != SF_ROLE_PUSH) {
+        return fail(SF_ERR_SHAPE, "task %d: unknown role %d", i, role);
+      }
+    }
+    if (!a.W || !a.scales || !a.X || (!a.Y && role != SF_ROLE_PUSH))
+      return fail(SF_ERR_NULL, "task %d: null pointer", i);
     if (a.T != T || (a.zeros != nullptr) != asym || a.group_size <= 0 ||
         lb_for(a.group_size) != lb_for(tasks[0].group_size))
       return fail(SF_ERR_UNSUPPORTED, "task %d: all tasks need the same T, layout and group class", i);
@@ -1196,8 +1297,8 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
   if (!step_config(tasks, c)) return fail(SF_ERR_UNSUPPORTED, "no launch configuration for T=%d", T);
   const std::vector<int> want = plan_ksplit(tasks, ntasks, c.grid * c.wpc);
   const StepSizes z = step_sizes(tasks, ntasks, want, c.grid);
-  if (workspace_bytes < z.total())
-    return fail(SF_ERR_SHAPE, "workspace too small: need %zu bytes", z.total());
+  if (workspace_bytes < z.total() + kEpochBytes)
+    return fail(SF_ERR_SHAPE, "workspace too small: need %zu bytes", z.total() + kEpochBytes);
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint8_t* tiles = ws + z.ctr;
@@ -1206,7 +1307,7 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
   uint8_t* xblk = part + z.part;
   std::vector<TileTask> h(ntasks);
   long long ub = 0;
-  int nph = 0;
+  int nph = 0, xny = 1;
   for (int i = 0; i < ntasks; ++i) {
     const sf_q4_task& a = tasks[i];
     TileTask& q = h[i];
@@ -1230,6 +1331,26 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
     if (i == 0 || a.wait_before) ++nph;
     q.phase = nph - 1;
     q.xpre = q.phase == 0 ? 1 : 0;
+    const int role = roles ? roles[i] : SF_ROLE_GEMV;
+    if (role != SF_ROLE_GEMV) {
+      q.push = role == SF_ROLE_PUSH;
+      q.kind = role >= SF_ROLE_REDUCE ? 1 : 0;
+      if (q.kind == 1) {   // sums an earlier pushed task: no weights, one unit per tile
+        const TileTask& sq = h[role - SF_ROLE_REDUCE];
+        q.ksplit = 1;
+        q.xpre = 0;
+        q.nchunk = 0;
+        q.xpar = sq.xpar;
+        for (int r = 0; r < 8; ++r) { q.xdata[r] = sq.xdata[r]; q.xflag[r] = sq.xflag[r]; }
+        q.tp_rank = sq.tp_rank;
+        q.tp_world = sq.tp_world;
+      } else {
+        const size_t data = (size_t)T * a.N * 4;   // one source rank's [T][N] fp32
+        int rc2 = tp_region(comm, data, (size_t)q.ntile, q.xdata, q.xflag, &q.tp_rank, &q.tp_world, &q.xpar);
+        if (rc2 != SF_OK) return rc2;
+      }
+    }
+    if (q.xpre && (q.nchunk + 7) / 8 > xny) xny = (q.nchunk + 7) / 8;
     q.ubase = ub;
     ub += (long long)q.ntile * q.ksplit;
   }
@@ -1256,8 +1377,10 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
   hd->cfg = c;
   hd->workspace = workspace;
   hd->clear_bytes = z.ctr + z.tiles;
-  hd->coop = nph > 1;
+  hd->coop = nph > 1 || has_tp;   // exchange waits need every CTA resident
   hd->prepass = true;
+  hd->xny = xny;
+  hd->tp = has_tp;
   TileLaunch& L = hd->L;
   L.tasks = reinterpret_cast<const TileTask*>(table);
   L.ntasks = ntasks;
@@ -1266,7 +1389,12 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
   L.phctr = reinterpret_cast<unsigned int*>(ws + align256((size_t)128 * c.grid));
   L.prefetch = env_int("SF_TILE_PREFETCH", 1);
   L.dbg = env_int("SF_TILE_DBG", 0);
+  L.epoch = nullptr;
   cudaError_t e = cudaMemcpy(table, h.data(), (size_t)ntasks * sizeof(TileTask), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && has_tp) {
+    L.epoch = reinterpret_cast<unsigned long long*>(ws + z.total());
+    e = cudaMemset(L.epoch, 0, kEpochBytes);
+  }
   if (e != cudaSuccess) {
     delete hd;
     return cuda_fail(e, "uploading the task table");
@@ -1274,13 +1402,28 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
   *handle_out = hd;
   return SF_OK;
 }
+}  // namespace
+
+extern "C" {
+
+int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size_t workspace_bytes,
+                      void** handle_out) {
+  return step_create_impl(tasks, nullptr, ntasks, nullptr, workspace, workspace_bytes, handle_out);
+}
+
+int sf_q4_step_create_tp(const sf_q4_task* tasks, const int* roles, int ntasks, void* comm, void* workspace,
+                         size_t workspace_bytes, void** handle_out) {
+  if (!roles) return fail(SF_ERR_NULL, "null pointer argument");
+  return step_create_impl(tasks, roles, ntasks, comm, workspace, workspace_bytes, handle_out);
+}
 
 int sf_q4_step_launch(void* handle, void* stream, int part) {
   if (!handle) return fail(SF_ERR_NULL, "null handle");
   if (part < 0 || part > 2) return fail(SF_ERR_SHAPE, "part must be 0, 1 or 2");
   StepHandle* hd = static_cast<StepHandle*>(handle);
   if (part == 2 && hd->coop)
-    return fail(SF_ERR_UNSUPPORTED, "the GEMV kernel alone needs a single-phase step (no wait_before)");
+    return fail(SF_ERR_UNSUPPORTED,
+                "the GEMV kernel alone needs a single-phase step without exchange tasks (no wait_before)");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSuccess;
   if (part != 2) {
@@ -1288,7 +1431,7 @@ int sf_q4_step_launch(void* handle, void* stream, int part) {
     if (e != cudaSuccess) return cuda_fail(e, "clearing the step counters");
   }
   if (part != 2 && hd->prepass) {
-    e = launch_xblocks(hd->cfg.T, hd->cfg.LB, hd->L.ntasks, hd->L, st);
+    e = launch_xblocks(hd->cfg.T, hd->cfg.LB, hd->L.ntasks, hd->L, st, hd->xny);
     if (e != cudaSuccess) return cuda_fail(e, "activation pre-pass launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);
   }
@@ -1434,7 +1577,7 @@ extern "C" int sf_q4_linear_static_scratch(const uint8_t* W, const float* scales
   L.dbg = 0;
   const int need = (int)((L.total + c.wpc - 1) / c.wpc);
   if (c.grid > need) c.grid = need;
-  e = launch_xblocks(T, c.LB, 1, L, st);
+  e = launch_xblocks(T, c.LB, 1, L, st, (q.nchunk + 7) / 8);
   if (e != cudaSuccess) return cuda_fail(e, "activation pre-pass launch");
   e = launch_tile(c, L, false, st);
   if (e != cudaSuccess) return cuda_fail(e, "q4_tile_kernel launch");

@@ -6,20 +6,24 @@
 // rank owns a block of whole groups along K and produces a partial Y that
 // must be summed across ranks).
 //
-// The exchange is a one-shot all-reduce over NVLink peer memory:
+// The exchange is a one-shot all-reduce over NVLink peer memory, with all of
+// its state on the device (so a captured CUDA graph can replay it):
 //  * every rank owns one exchange buffer (cudaMalloc, exported as a CUDA IPC
-//    handle and opened by every peer): a flag line per source rank, then two
-//    fp32 partial slots used on alternate calls;
-//  * call e writes this rank's partial [T, N] into slot e & 1 (the row-parallel
-//    GEMV writes there directly), then the reduce kernel publishes
-//    "epoch e ready" into every peer's flag line (system-scope release), waits
-//    (bounded) until every peer's flag for epoch e has arrived in its own
-//    buffer (acquire), and sums the partials of ranks 0..P-1 in rank order
-//    with peer loads -- every rank produces bitwise the same Y;
-//  * slot reuse is safe: a rank writes slot e & 1 again at epoch e + 2 only
-//    after its reduce of epoch e + 1 saw every peer's e + 1 flag, which each
-//    peer stores only after its own reduce of epoch e (stream order) has
-//    finished reading that slot.
+//    handle and opened by every peer): a header (call epoch, finished-block
+//    count), a flag word per (reduce block, source rank), then two fp32 slots
+//    used on alternate calls; and a private partial buffer that the
+//    row-parallel GEMV writes;
+//  * call e (e = device epoch + 1, read by every block at start) splits the
+//    result into chunks; block b copies its chunks of this rank's partial into
+//    slot e & 1, then stores flag[b][rank] = e into every peer's buffer
+//    (system-scope release), waits (bounded) until flag[b][p] >= e for every
+//    peer p in its own buffer (acquire), and sums the chunks of ranks
+//    0..P-1 in rank order with peer loads -- every rank produces bitwise the
+//    same Y; the last block to finish advances the epoch;
+//  * slot reuse is safe: a rank writes slot e & 1 again at call e + 2 only
+//    after its call e + 1 saw a flag of call e + 1 from every peer, which a
+//    peer stores only after its own call e (stream order) has finished
+//    reading that slot.
 // A wait that expires sets the library's device error word and the kernel
 // returns; the host reads SF_ERR_TIMEOUT from sf_q4_check_device_error().
 #include <cuda_runtime.h>
@@ -44,27 +48,31 @@ int run_linear(const uint8_t* W, const float* S, const float* Z, const float* bi
 namespace {
 
 constexpr int kMaxRanks = 8;
-constexpr size_t kFlagLine = 128;                       // one 128-byte line per source rank
-constexpr size_t kHeader = kFlagLine * kMaxRanks;       // flags area at the start of the buffer
+constexpr int kMaxBlocks = 1024;                        // reduce blocks per call (chunks beyond: grid stride)
+constexpr int kChunk = 1024;                            // floats per chunk (4 per thread, 256 threads)
+constexpr size_t kHeader = 256;                         // epoch, finished-block count
+constexpr size_t kFlags = (size_t)kMaxBlocks * kMaxRanks * 8;
+constexpr size_t kSlot0 = kHeader + kFlags;
 constexpr unsigned kErrTpWait = 1u << 16;
 
 struct Comm {
   int rank = 0, world = 1, device = 0;
   size_t slot_bytes = 0;
+  size_t arena_bytes = 0, arena_used = 0;   // exchange regions of fused step tasks, after the slots
   uint8_t* local = nullptr;                 // this rank's exchange buffer
+  float* partial = nullptr;                 // the row-parallel GEMV's output (private)
   uint8_t* peer[kMaxRanks] = {};            // every rank's buffer as mapped here (peer[rank] = local)
   bool opened[kMaxRanks] = {};
-  unsigned long long epoch = 0;
 };
 
 struct ReduceArgs {
   uint8_t* peer[kMaxRanks];
   int rank, world;
-  unsigned long long epoch;
-  size_t slot_off;                          // byte offset of this epoch's slot in every buffer
+  size_t slot_bytes;
+  const float* partial;                     // this rank's partial [count]
   long long count;                          // T * N
-  const float* bias;                        // [N] or null
-  int ncols;                                // N (bias index = i % N)
+  const float* bias;                        // [ncols] or null
+  int ncols;
   void* out;
   int out_dtype;
 };
@@ -78,72 +86,99 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   return v;
 }
 
-__global__ void tp_allreduce_kernel(const ReduceArgs a) {
+__global__ void __launch_bounds__(256) tp_allreduce_kernel(const ReduceArgs a) {
+  __shared__ unsigned long long ep_s;
   __shared__ int ok;
-  // 1. publish: this rank's partial (written by the previous kernel on this
-  //    stream) is complete; tell every peer.  Block 0 only.
-  if (blockIdx.x == 0 && threadIdx.x < (unsigned)a.world) {
-    __threadfence_system();
-    auto* f = reinterpret_cast<unsigned long long*>(a.peer[threadIdx.x] + kFlagLine * a.rank);
-    st_release_sys(f, a.epoch);
+  uint8_t* mine = a.peer[a.rank];
+  auto* hdr = reinterpret_cast<unsigned long long*>(mine);   // [0] epoch, [1] finished blocks
+  if (threadIdx.x == 0) ep_s = *reinterpret_cast<volatile unsigned long long*>(hdr) + 1;
+  __syncthreads();
+  const unsigned long long ep = ep_s;
+  const size_t slot = kSlot0 + (size_t)(ep & 1) * a.slot_bytes;
+  const long long nchunks = (a.count + kChunk - 1) / kChunk;
+  // 1. this rank's chunks of the partial -> own slot
+  for (long long c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    const long long i = c * kChunk + 4 * threadIdx.x;
+    float* dst = reinterpret_cast<float*>(mine + slot);
+    if (i + 4 <= a.count) {
+      *reinterpret_cast<float4*>(dst + i) = *reinterpret_cast<const float4*>(a.partial + i);
+    } else {
+      for (long long j = i; j < a.count && j < i + 4; ++j) dst[j] = a.partial[j];
+    }
   }
-  // 2. wait (bounded) until every peer's partial of this epoch is published
+  __syncthreads();
+  // 2. publish block b's chunks to every peer, then wait for theirs (bounded)
+  if (threadIdx.x < (unsigned)a.world) {
+    __threadfence_system();
+    auto* f = reinterpret_cast<unsigned long long*>(a.peer[threadIdx.x] + kHeader) +
+              (size_t)blockIdx.x * kMaxRanks + a.rank;
+    st_release_sys(f, ep);
+  }
   if (threadIdx.x == 0) {
     int good = 1;
+    const auto* fl = reinterpret_cast<const unsigned long long*>(mine + kHeader) + (size_t)blockIdx.x * kMaxRanks;
     for (int p = 0; p < a.world && good; ++p) {
-      const auto* f = reinterpret_cast<const unsigned long long*>(a.peer[a.rank] + kFlagLine * p);
-      if (ld_acquire_sys(f) >= a.epoch) continue;
+      if (ld_acquire_sys(fl + p) >= ep) continue;
       const long long t0 = clock64();
-      while (ld_acquire_sys(f) < a.epoch) {
+      while (ld_acquire_sys(fl + p) < ep) {
         if (clock64() - t0 > kWaitCycles) {
           atomicOr(&g_dev_error, kErrTpWait);
           good = 0;
           break;
         }
-        __nanosleep(64);
+        __nanosleep(32);
       }
     }
     ok = good;
   }
   __syncthreads();
-  if (!ok) return;
-  // 3. Y = sum over ranks in rank order (+ bias), 4 elements per thread
-  const long long n4 = a.count / 4;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (a.count + 3) / 4;
-       i += (long long)gridDim.x * blockDim.x) {
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (i < n4) {
-      for (int p = 0; p < a.world; ++p) {
-        const float4 q = reinterpret_cast<const float4*>(a.peer[p] + a.slot_off)[i];
-        v[0] += q.x; v[1] += q.y; v[2] += q.z; v[3] += q.w;
+  // 3. Y = sum over ranks in rank order (+ bias)
+  if (ok) {
+    for (long long c = blockIdx.x; c < nchunks; c += gridDim.x) {
+      const long long i = c * kChunk + 4 * threadIdx.x;
+      if (i >= a.count) continue;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (i + 4 <= a.count) {
+        for (int p = 0; p < a.world; ++p) {
+          const float4 q = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.peer[p] + slot) + i);
+          v[0] += q.x; v[1] += q.y; v[2] += q.z; v[3] += q.w;
+        }
+      } else {
+        for (int p = 0; p < a.world; ++p) {
+          const float* q = reinterpret_cast<const float*>(a.peer[p] + slot);
+          for (int j = 0; j < 4 && i + j < a.count; ++j) v[j] += q[i + j];
+        }
       }
-    } else {
-      for (int p = 0; p < a.world; ++p) {
-        const float* q = reinterpret_cast<const float*>(a.peer[p] + a.slot_off);
-        for (int j = 0; j < 4 && 4 * i + j < a.count; ++j) v[j] += q[4 * i + j];
+      for (int j = 0; j < 4 && i + j < a.count; ++j) {
+        const long long e = i + j;
+        const float y = v[j] + (a.bias ? a.bias[e % a.ncols] : 0.f);
+        if (a.out_dtype == SF_F32) static_cast<float*>(a.out)[e] = y;
+        else if (a.out_dtype == SF_BF16) static_cast<__nv_bfloat16*>(a.out)[e] = __float2bfloat16_rn(y);
+        else static_cast<__half*>(a.out)[e] = __float2half_rn(y);
       }
     }
-    for (int j = 0; j < 4; ++j) {
-      const long long e = 4 * i + j;
-      if (e >= a.count) break;
-      float y = v[j] + (a.bias ? a.bias[e % a.ncols] : 0.f);
-      if (a.out_dtype == SF_F32) static_cast<float*>(a.out)[e] = y;
-      else if (a.out_dtype == SF_BF16) static_cast<__nv_bfloat16*>(a.out)[e] = __float2bfloat16_rn(y);
-      else static_cast<__half*>(a.out)[e] = __float2half_rn(y);
+  }
+  // 4. the last block to finish advances the epoch for the next call
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(reinterpret_cast<unsigned long long*>(hdr + 1), 1ull) == (unsigned long long)gridDim.x - 1) {
+      hdr[1] = 0;
+      __threadfence();
+      *reinterpret_cast<volatile unsigned long long*>(hdr) = ep;
     }
   }
 }
 
-int reduce(Comm* c, long long count, const float* bias, int ncols, void* out, int out_dtype, cudaStream_t st) {
+int reduce(Comm* c, const float* partial, long long count, const float* bias, int ncols, void* out, int out_dtype,
+           cudaStream_t st) {
+  if (count == 0) return SF_OK;
   ReduceArgs a{};
   for (int p = 0; p < c->world; ++p) a.peer[p] = c->peer[p];
-  a.rank = c->rank; a.world = c->world; a.epoch = c->epoch;
-  a.slot_off = kHeader + (size_t)(c->epoch & 1) * c->slot_bytes;
-  a.count = count; a.bias = bias; a.ncols = ncols; a.out = out; a.out_dtype = out_dtype;
-  const DeviceInfo& di = device_info();
-  long long blocks = ((count + 3) / 4 + 255) / 256;
-  if (blocks > 4LL * di.sms) blocks = 4LL * di.sms;
-  if (blocks < 1) blocks = 1;
+  a.rank = c->rank; a.world = c->world; a.slot_bytes = c->slot_bytes;
+  a.partial = partial; a.count = count; a.bias = bias; a.ncols = ncols; a.out = out; a.out_dtype = out_dtype;
+  long long blocks = (count + kChunk - 1) / kChunk;
+  if (blocks > kMaxBlocks) blocks = kMaxBlocks;
   tp_allreduce_kernel<<<(unsigned)blocks, 256, 0, st>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tp_allreduce_kernel launch");
@@ -154,6 +189,28 @@ int reduce(Comm* c, long long count, const float* bias, int ncols, void* out, in
 Comm* as_comm(void* h) { return static_cast<Comm*>(h); }
 
 }  // namespace
+
+int tp_region(void* comm, size_t src_bytes, size_t tiles, uint8_t** data, unsigned long long** flags, int* rank,
+              int* world, size_t* par_bytes) {
+  Comm* c = as_comm(comm);
+  for (int p = 0; p < c->world; ++p)
+    if (!c->peer[p]) return fail(SF_ERR_COMM, "rank %d is not connected (call sf_tp_comm_connect)", p);
+  const size_t par = ((size_t)c->world * src_bytes + 255) & ~(size_t)255;
+  const size_t fl = (tiles * c->world * 8 + 255) & ~(size_t)255;
+  if (c->arena_used + 2 * par + fl > c->arena_bytes)
+    return fail(SF_ERR_SHAPE, "tensor-parallel arena too small: %zu of %zu bytes used, %zu more needed",
+                c->arena_used, c->arena_bytes, 2 * par + fl);
+  const size_t off = kSlot0 + 2 * c->slot_bytes + c->arena_used;
+  c->arena_used += 2 * par + fl;
+  for (int p = 0; p < 8; ++p) {
+    data[p] = p < c->world ? c->peer[p] + off : nullptr;
+    flags[p] = p < c->world ? reinterpret_cast<unsigned long long*>(c->peer[p] + off + 2 * par) : nullptr;
+  }
+  *rank = c->rank;
+  *world = c->world;
+  *par_bytes = par;
+  return SF_OK;
+}
 }  // namespace sf
 
 using namespace sf;
@@ -162,22 +219,31 @@ extern "C" {
 
 size_t sf_tp_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
 
-int sf_tp_comm_init(int rank, int world, size_t slot_bytes, void** comm_out, void* handle_out) {
+int sf_tp_comm_init(int rank, int world, size_t slot_bytes, size_t arena_bytes, void** comm_out,
+                    void* handle_out) {
   if (!comm_out || !handle_out) return fail(SF_ERR_NULL, "null pointer argument");
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
     return fail(SF_ERR_SHAPE, "tensor-parallel world size must be 1..%d and 0 <= rank < world", kMaxRanks);
   slot_bytes = (slot_bytes + 255) & ~(size_t)255;
+  arena_bytes = (arena_bytes + 255) & ~(size_t)255;
   Comm* c = new Comm();
-  c->rank = rank; c->world = world; c->slot_bytes = slot_bytes;
+  c->rank = rank; c->world = world; c->slot_bytes = slot_bytes; c->arena_bytes = arena_bytes;
   cudaGetDevice(&c->device);
-  const size_t bytes = kHeader + 2 * slot_bytes;
+  const size_t bytes = kSlot0 + 2 * slot_bytes + arena_bytes;
   cudaError_t e = cudaMalloc(&c->local, bytes);
   if (e != cudaSuccess) { delete c; return cuda_fail(e, "allocating the tensor-parallel exchange buffer"); }
+  e = cudaMalloc(&c->partial, slot_bytes);
+  if (e != cudaSuccess) {
+    cudaFree(c->local);
+    delete c;
+    return cuda_fail(e, "allocating the tensor-parallel partial buffer");
+  }
   e = cudaMemset(c->local, 0, bytes);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle_out), c->local);
   if (e != cudaSuccess) {
     cudaFree(c->local);
+    cudaFree(c->partial);
     delete c;
     return cuda_fail(e, "exporting the tensor-parallel exchange buffer");
   }
@@ -203,21 +269,14 @@ int sf_tp_comm_connect(void* comm, const void* handles) {
 
 int sf_tp_allreduce(void* comm, const float* partial, void* out, int out_dtype, const float* bias, long long count,
                     int ncols, void* stream) {
-  if (!comm || !out) return fail(SF_ERR_NULL, "null pointer argument");
+  if (!comm || !out || !partial) return fail(SF_ERR_NULL, "null pointer argument");
   Comm* c = as_comm(comm);
   if (out_dtype < 0 || out_dtype > 2) return fail(SF_ERR_DTYPE, "unknown dtype code");
   if (count < 0 || (size_t)count * 4 > c->slot_bytes || ncols <= 0)
     return fail(SF_ERR_SHAPE, "all-reduce of %lld floats exceeds the %zu-byte exchange slot", count, c->slot_bytes);
   for (int p = 0; p < c->world; ++p)
     if (!c->peer[p]) return fail(SF_ERR_COMM, "rank %d is not connected (call sf_tp_comm_connect)", p);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  c->epoch += 1;
-  uint8_t* slot = c->local + kHeader + (size_t)(c->epoch & 1) * c->slot_bytes;
-  if (partial && partial != reinterpret_cast<const float*>(slot)) {
-    cudaError_t e = cudaMemcpyAsync(slot, partial, (size_t)count * 4, cudaMemcpyDeviceToDevice, st);
-    if (e != cudaSuccess) return cuda_fail(e, "staging the partial sum");
-  }
-  return reduce(c, count, bias, ncols, out, out_dtype, st);
+  return reduce(c, partial, count, bias, ncols, out, out_dtype, static_cast<cudaStream_t>(stream));
 }
 
 int sf_q4_linear_allreduce(void* comm, const uint8_t* W, const float* scales, const float* zeros, const float* bias,
@@ -230,12 +289,9 @@ int sf_q4_linear_allreduce(void* comm, const uint8_t* W, const float* scales, co
   for (int p = 0; p < c->world; ++p)
     if (!c->peer[p]) return fail(SF_ERR_COMM, "rank %d is not connected (call sf_tp_comm_connect)", p);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // the shard's partial goes straight into the next epoch's slot
-  float* slot = reinterpret_cast<float*>(c->local + kHeader + (size_t)((c->epoch + 1) & 1) * c->slot_bytes);
-  int rc = run_linear(W, scales, zeros, nullptr, X, x_dtype, slot, SF_F32, N, K, T, group_size, 0, st, false);
+  int rc = run_linear(W, scales, zeros, nullptr, X, x_dtype, c->partial, SF_F32, N, K, T, group_size, 0, st, false);
   if (rc != SF_OK) return rc;
-  c->epoch += 1;
-  return reduce(c, (long long)T * N, bias, N, Y, y_dtype, st);
+  return reduce(c, c->partial, (long long)T * N, bias, N, Y, y_dtype, st);
 }
 
 void sf_tp_comm_destroy(void* comm) {
@@ -248,6 +304,7 @@ void sf_tp_comm_destroy(void* comm) {
   for (int p = 0; p < c->world; ++p)
     if (c->opened[p]) cudaIpcCloseMemHandle(c->peer[p]);
   cudaFree(c->local);
+  cudaFree(c->partial);
   cudaSetDevice(prev);
   delete c;
 }

@@ -75,7 +75,7 @@ class PeerComm:
 
     Collective: every rank constructs it with the same ``slot_bytes``."""
 
-    def __init__(self, group=None, slot_bytes: int = 64 << 20):
+    def __init__(self, group=None, slot_bytes: int = 64 << 20, arena_bytes: int = 0):
         import torch
         import torch.distributed as dist
         self.lib = _lib.load()
@@ -85,7 +85,7 @@ class PeerComm:
         hb = int(self.lib.sf_tp_handle_bytes())
         handle = (ctypes.c_ubyte * hb)()
         comm = ctypes.c_void_p()
-        _lib.check(self.lib.sf_tp_comm_init(self.rank, self.world, slot_bytes, ctypes.byref(comm),
+        _lib.check(self.lib.sf_tp_comm_init(self.rank, self.world, slot_bytes, arena_bytes, ctypes.byref(comm),
                                             ctypes.cast(handle, ctypes.c_void_p)))
         self.comm = comm
         mine = torch.tensor(bytearray(handle), dtype=torch.uint8)
@@ -178,3 +178,234 @@ class RowParallelQ4Linear:
 
 __all__ = ["shard_bounds", "shard_column", "shard_row", "PeerComm", "ColumnParallelQ4Linear",
            "RowParallelQ4Linear"]
+
+
+class TPStepRunner:
+    """A tensor-parallel decode step as one CUDA graph per rank.
+
+    ``layers``: per decoder layer, the rank's seven Q4Linear shards in the
+    order q, k, v, o, gate, up, down (q/k/v/gate/up column-parallel, o/down
+    row-parallel).  Each half layer is one persistent multi-GEMV launch
+    (sf_q4_step_run: q/k/v/o-partial, then gate/up/down-partial), followed by
+    the all-reduce of the row-parallel partial -- the library's NVLink
+    all-reduce (``mode="peer"``) or NCCL (``mode="nccl"``).  ``mode="fused"``
+    runs the whole step as ONE persistent launch: row-parallel tiles are pushed
+    to every rank over NVLink as they finish and summed by reduce tasks inside
+    the same kernel (sf_q4_step_create_tp; the communicator needs
+    ``arena_bytes(...)`` of arena).  With one rank the all-reduces are skipped.  As in the single-GPU step, every projection
+    reads its own input slot (attention, norms and SwiGLU are outside this
+    path); only the exchange points of the decoder are kept.
+    """
+
+    ROW_PARALLEL = (False, False, False, True, False, False, True)
+
+    def __init__(self, layers, tokens: int = 1, x_dtype=None, mode: str = "peer",
+                 comm: PeerComm | None = None, group=None, device=None):
+        import torch
+        import torch.distributed as dist
+        self.torch = torch
+        self.layers = [list(l) for l in layers]
+        self.tokens = int(tokens)
+        self.x_dtype = x_dtype or torch.float16
+        self.mode, self.comm, self.group = mode, comm, group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if self.world > 1 and mode in ("peer", "fused") and comm is None:
+            raise ValueError(f"mode={mode!r} needs a PeerComm")
+        self.device = torch.device(device) if device is not None else self.layers[0][0].packed_d.device
+        self.lib = _lib.load()
+        align = 64
+        xo = yo = 0
+        self.slots = []           # per layer: list of (x_off, y_off)
+        for lay in self.layers:
+            s = []
+            for m in lay:
+                s.append((xo, yo))
+                xo += -(-self.tokens * m.in_features // align) * align
+                yo += -(-self.tokens * m.out_features // align) * align
+            self.slots.append(s)
+        self.x = torch.zeros(xo, dtype=self.x_dtype, device=self.device)
+        self.y = torch.zeros(yo, dtype=torch.float32, device=self.device)   # GEMV outputs / partials
+        hidden = self.layers[0][3].out_features
+        # all-reduced outputs of o and down, per layer
+        self.red = torch.zeros((len(self.layers), 2, self.tokens, hidden), dtype=torch.float32, device=self.device)
+        self.x_host = torch.zeros(xo, dtype=self.x_dtype, pin_memory=True)
+        self.red_host = torch.zeros(self.red.shape, dtype=torch.float32, pin_memory=True)
+        self.stream = torch.cuda.Stream(self.device)
+        self._handles, self._ws = [], []
+        if mode == "fused":
+            self._handles.append(self._make_fused())
+        else:
+            for li, lay in enumerate(self.layers):
+                for half in ((0, 1, 2, 3), (4, 5, 6)):
+                    self._handles.append(self._make_step(li, half))
+        self.graph = None
+
+    @staticmethod
+    def arena_bytes(n_layers: int, tokens: int, hidden: int, world: int) -> int:
+        """Communicator arena a fused step needs (two exchange regions per layer)."""
+        par = -(-(world * tokens * hidden * 4) // 256) * 256
+        flags = -(-((hidden + 31) // 32 * world * 8) // 256) * 256
+        return 2 * n_layers * (2 * par + flags)
+
+    def _make_fused(self):
+        """Every layer's seven projections and two all-reduces as one step."""
+        from .kernels.cuda import _dtype_code
+        torch = self.torch
+        tasks, roles = [], []
+        xs = self.x.element_size()
+        for li, lay in enumerate(self.layers):
+            for i, m in enumerate(lay):
+                xo, yo = self.slots[li][i]
+                row = self.ROW_PARALLEL[i]
+                base = (m.packed_d.data_ptr(), m.scales_d.data_ptr(),
+                        None if m.zeros_d is None else m.zeros_d.data_ptr())
+                xp = self.x.data_ptr() + xo * xs
+                if not row:
+                    tasks.append(_lib.Q4Task(*base, None if m.bias_d is None else m.bias_d.data_ptr(), xp,
+                                             self.y.data_ptr() + yo * 4, m.out_features, m.in_features,
+                                             self.tokens, m.group_size, _dtype_code(self.x), _lib.SF_F32, 0))
+                    roles.append(0)
+                    continue
+                out = self.red[li, 0 if i == 3 else 1]
+                if self.world == 1:
+                    tasks.append(_lib.Q4Task(*base, None, xp, out.data_ptr(), m.out_features, m.in_features,
+                                             self.tokens, m.group_size, _dtype_code(self.x), _lib.SF_F32, 0))
+                    roles.append(0)
+                    continue
+                src = len(tasks)
+                tasks.append(_lib.Q4Task(*base, None, xp, None, m.out_features, m.in_features, self.tokens,
+                                         m.group_size, _dtype_code(self.x), _lib.SF_F32, 0))
+                roles.append(1)
+                tasks.append(_lib.Q4Task(*base, None, xp, out.data_ptr(), m.out_features, m.in_features,
+                                         self.tokens, m.group_size, _dtype_code(self.x), _lib.SF_F32, 0))
+                roles.append(2 + src)
+        n = len(tasks)
+        arr = (_lib.Q4Task * n)(*tasks)
+        rl = (_lib.ctypes.c_int * n)(*roles)
+        nbytes = int(self.lib.sf_q4_step_workspace_bytes(arr, n))
+        ws = torch.zeros(nbytes + 256, dtype=torch.uint8, device=self.device)
+        self._ws.append(ws)
+        h = _lib.ctypes.c_void_p()
+        comm = self.comm.comm if (self.comm is not None and self.world > 1) else None
+        with torch.cuda.device(self.device):
+            if self.world > 1:
+                _lib.check(self.lib.sf_q4_step_create_tp(arr, rl, n, comm, (ws.data_ptr() + 255) & ~255, nbytes,
+                                                         _lib.ctypes.byref(h)))
+            else:
+                _lib.check(self.lib.sf_q4_step_create(arr, n, (ws.data_ptr() + 255) & ~255, nbytes,
+                                                      _lib.ctypes.byref(h)))
+        return h
+
+    def _make_step(self, li, idx):
+        from .kernels.cuda import _dtype_code
+        torch = self.torch
+        n = len(idx)
+        arr = (_lib.Q4Task * n)()
+        xs = self.x.element_size()
+        for j, i in enumerate(idx):
+            m = self.layers[li][i]
+            xo, yo = self.slots[li][i]
+            arr[j] = _lib.Q4Task(
+                m.packed_d.data_ptr(), m.scales_d.data_ptr(),
+                None if m.zeros_d is None else m.zeros_d.data_ptr(),
+                None if m.bias_d is None else m.bias_d.data_ptr(),
+                self.x.data_ptr() + xo * xs, self.y.data_ptr() + yo * 4,
+                m.out_features, m.in_features, self.tokens, m.group_size,
+                _dtype_code(self.x), _lib.SF_F32, 0)
+        nbytes = int(self.lib.sf_q4_step_workspace_bytes(arr, n))
+        ws = torch.zeros(nbytes + 256, dtype=torch.uint8, device=self.device)
+        self._ws.append(ws)
+        h = _lib.ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.sf_q4_step_create(arr, n, (ws.data_ptr() + 255) & ~255, nbytes,
+                                                  _lib.ctypes.byref(h)))
+        return h
+
+    def y_slot(self, li, i):
+        m = self.layers[li][i]
+        yo = self.slots[li][i][1]
+        return self.y[yo:yo + self.tokens * m.out_features].view(self.tokens, m.out_features)
+
+    def _reduce(self, li, which, st):
+        torch = self.torch
+        i = 3 if which == 0 else 6
+        part = self.y_slot(li, i)
+        out = self.red[li, which]
+        if self.world == 1:
+            out.copy_(part)
+        elif self.mode == "nccl":
+            import torch.distributed as dist
+            dist.all_reduce(part, group=self.group)
+            out.copy_(part)
+        else:
+            _lib.check(self.lib.sf_tp_allreduce(self.comm.comm, part.data_ptr(), out.data_ptr(), _lib.SF_F32,
+                                                None, part.numel(), part.shape[1], st.cuda_stream))
+
+    def launches_per_step(self) -> int:
+        """Kernels of this library per step: 2 per step launch (activation
+        pre-pass + GEMV kernel), plus one peer all-reduce per row-parallel
+        projection when mode is 'peer' and world > 1."""
+        red = 2 * len(self.layers) if (self.world > 1 and self.mode == "peer") else 0
+        return 2 * len(self._handles) + red
+
+    def _launch_all(self, st):
+        if self.mode == "fused":
+            _lib.check(self.lib.sf_q4_step_run(self._handles[0], st.cuda_stream))
+            return
+        for li in range(len(self.layers)):
+            for half in range(2):
+                _lib.check(self.lib.sf_q4_step_run(self._handles[2 * li + half], st.cuda_stream))
+                self._reduce(li, half, st)
+
+    def capture(self):
+        torch = self.torch
+        with torch.cuda.device(self.device):
+            self.stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.stream):
+                self._launch_all(self.stream)
+            self.stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self.stream):
+                self._launch_all(self.stream)
+            self.graph = g
+
+    def run(self):
+        if self.graph is None:
+            self.capture()
+        with self.torch.cuda.stream(self.stream):
+            self.graph.replay()
+
+    def run_host(self):
+        """One step from pinned host activations to the pinned host copy of the
+        all-reduced o/down outputs."""
+        if self.graph is None:
+            self.capture()
+        with self.torch.cuda.stream(self.stream):
+            self.x.copy_(self.x_host, non_blocking=True)
+            self.graph.replay()
+            self.red_host.copy_(self.red, non_blocking=True)
+
+    def algorithmic_bytes(self) -> int:
+        """This rank's bytes per step: packed weights, fp32 scales, activations
+        in, GEMV outputs out (the all-reduce traffic is not counted)."""
+        tot = 0
+        xe = self.x.element_size()
+        for lay in self.layers:
+            for m in lay:
+                g = m.in_features // m.group_size
+                tot += m.out_features * m.in_features // 2 + m.out_features * g * 4
+                if m.is_asym:
+                    tot += m.out_features * g * 4
+                tot += self.tokens * (m.in_features * xe + m.out_features * 4)
+        return tot
+
+    def __del__(self):
+        for h in getattr(self, "_handles", []):
+            try:
+                self.lib.sf_q4_step_destroy(h)
+            except Exception:
+                pass
+        self._handles = []
+
+
+__all__.append("TPStepRunner")

@@ -252,3 +252,25 @@ def test_c_abi_reference_named_entries(cuda):
     _lib.check(lib.sf_q4_gemv_sym(P.data_ptr(), S.data_ptr(), X.data_ptr(), y.data_ptr(),
                                   96, 512, 64, st))
     assert O.normwise_rel_err(y.cpu().numpy(), O.gemv_sym(p, s, x[0], 64)) <= TOL
+
+
+def test_capture_without_warmup_fails_loudly(cuda):
+    """A shape whose scratch would have to grow inside a stream capture is
+    refused with SF_ERR_CAPTURE (never silently run on another kernel)."""
+    p, s, _, x = rand_case(77, 4352, 12288, 128, False, t=3)
+    P, S, X = dev(p), dev(s), dev(x)
+    st = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with pytest.raises(RuntimeError, match="capture"):
+        with torch.cuda.graph(g, stream=st):
+            K.linear(P, S, None, X, 128)
+    # after a warm-up on the capturing stream the same capture succeeds
+    with torch.cuda.stream(st):
+        ref = K.linear(P, S, None, X, 128)
+    st.synchronize()
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2, stream=st):
+        out = K.linear(P, S, None, X, 128)
+    g2.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)

@@ -36,7 +36,7 @@ def _worker(rank, world, port, q):
         from oracle import q4_oracle as O
         from siliconfer_b200 import _lib, quant as Q
         from siliconfer_b200.tensor_parallel import ColumnParallelQ4Linear, PeerComm, RowParallelQ4Linear
-        comm = PeerComm(slot_bytes=8 << 20)
+        comm = PeerComm(slot_bytes=8 << 20, arena_bytes=64 << 20)
         errs, same = [], []
         for case, (n, k, t, asym, xdt) in enumerate([(512, 2048, 1, False, torch.float32),
                                                      (1024, 4096, 4, True, torch.float16),
@@ -68,6 +68,46 @@ def _worker(rank, world, port, q):
                 dist.all_gather(g, ya)
                 same.append(all(torch.equal(g[0], gi) for gi in g))
         out["errs"], out["same"] = errs, same
+        # the fused step: two layers of 7 projections, all-reduces inside one launch,
+        # checked against the unfused step (local GEMV + NCCL) on the same inputs
+        from siliconfer_b200.tensor_parallel import TPStepRunner
+        from siliconfer_b200.q4_linear import Q4Linear
+        H, F = 512, 1536
+        shapes = [(H, H), (128, H), (128, H), (H, H), (F, H), (F, H), (H, F)]
+        layers = []
+        for li in range(2):
+            lay = []
+            for pi, (n, k) in enumerate(shapes):
+                rng = np.random.default_rng(1000 * li + pi)
+                w = rng.normal(0, 0.02, (n, k)).astype(np.float32)
+                pq, sq = Q.pack_weights_sym(w, 128)
+                if pi in (3, 6):
+                    from siliconfer_b200.tensor_parallel import shard_row
+                    pq, sq, _, _ = shard_row(pq, sq, None, 128, rank, world)
+                else:
+                    from siliconfer_b200.tensor_parallel import shard_column
+                    pq, sq, _, _ = shard_column(pq, sq, None, rank, world)
+                lay.append(Q4Linear(pq, sq, group_size=128, device=dev))
+            layers.append(lay)
+        fused = TPStepRunner(layers, tokens=2, mode="fused", comm=comm, device=dev)
+        ref = TPStepRunner(layers, tokens=2, mode="nccl", device=dev)
+        g = torch.Generator(device=dev).manual_seed(5)
+        fused.x.copy_(torch.randn(fused.x.shape, generator=g, device=dev).to(fused.x.dtype))
+        ref.x.copy_(fused.x)
+        fused.capture()
+        ref.capture()
+        fe = []
+        for rep in range(4):
+            fused.run()
+            ref.run()
+            torch.cuda.synchronize()
+            a, b = fused.red.double(), ref.red.double()
+            fe.append(((a - b).abs().max() / b.abs().max()).item())
+        out["fused_err"] = fe
+        gg = [torch.empty_like(fused.red) for _ in range(world)]
+        dist.all_gather(gg, fused.red)
+        out["fused_same"] = all(torch.equal(gg[0], x) for x in gg)
+        del fused, ref
         out["dev_err_ok"] = _lib.load().sf_q4_check_device_error()
         # bounded wait: rank 0 starts an all-reduce that rank 1 never joins
         dist.barrier()
@@ -108,5 +148,8 @@ def test_row_parallel_peer_and_nccl_match_oracle():
         assert all(r["same"]), "ranks disagree on the peer all-reduce result"
         for case, rep, ea, eb, ec, tol in r["errs"]:
             assert ea <= tol and eb <= tol and ec <= tol, (r["rank"], case, rep, ea, eb, ec)
+    for r in res:
+        assert max(r["fused_err"]) <= 1e-5, r["fused_err"]
+        assert r["fused_same"]
     assert res[0]["timeout_status"] == 7        # SF_ERR_TIMEOUT
     assert res[0]["after"] == 0                 # the error word was read and cleared
