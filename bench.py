@@ -311,6 +311,8 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clocks.summary(),
         "build_s": round(build_s, 1),
     }
+    if world == 1 and args.workload == "7b" and not args.no_prefill:
+        result["prefill"] = prefill_measure(device, runner.stream)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args, layers)
     if rank == 0:
@@ -480,6 +482,55 @@ def _teardown(dist, comm, runners, *refs):
         dist.destroy_process_group()
 
 
+def prefill_measure(device, stream, iters=20):
+    """gemm_asym prefill at 7B shapes on the tcgen05 path.
+
+    Asymmetric int4 g128 (device RTN), bf16 activations N(0,1), bf16 out.
+    Each shape: warm-up on `stream`, then `iters` calls captured in a CUDA
+    graph and timed with CUDA events around one replay (inputs stay resident;
+    weights + X + Y of the largest shape are 61 MB, below L2, so this is the
+    kernel's compute-bound speed with warm operands)."""
+    import torch
+    from siliconfer_b200 import quant as Q
+    from siliconfer_b200.kernels import cuda as K
+    peak = None
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peak = float(json.loads(pk.read_text())["bf16_tflops"])
+    out = []
+    g = torch.Generator(device=device)
+    for m in (512, 2048):
+        for k, n in ((4096, 4096), (4096, 11008), (11008, 4096)):
+            g.manual_seed(m + k + n)
+            W = torch.randn((n, k), generator=g, device=device) * 0.02
+            p, s, z = Q.pack_weights_device(W, 128, sym=False)
+            del W
+            X = torch.randn((m, k), generator=g, device=device).to(torch.bfloat16)
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    K.linear(p, s, z, X, 128, out_dtype=torch.bfloat16)
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for _ in range(iters):
+                    K.linear(p, s, z, X, 128, out_dtype=torch.bfloat16)
+            with torch.cuda.stream(stream):
+                graph.replay()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                graph.replay()
+                e1.record(stream)
+            e1.synchronize()
+            us = e0.elapsed_time(e1) / iters * 1e3
+            tf = 2.0 * m * n * k / us / 1e6
+            out.append({"M": m, "K": k, "N": n, "us": round(us, 1), "tflops": round(tf, 1),
+                        "frac": None if peak is None else round(tf / peak, 4)})
+            del graph, p, s, z, X
+    return {"workload": "BASELINE config 4: gemm_asym prefill, 7B shapes, asym int4 g128, bf16 X",
+            "kernel": "q4_gemm_tc_kernel (tcgen05, dequant to bf16 in TMEM)", "peak_tflops": peak,
+            "peak_kind": "measured bf16 burst" if peak else None, "shapes": out}
+
+
 def traffic_from_profile(workload, batch):
     """DRAM bytes per launch of the GEMV kernel, from the committed ncu summary
     (profiles/traffic.txt: lines "<workload>_b<batch> <bytes> <how>"), if any."""
@@ -589,6 +640,7 @@ def main():
     ap.add_argument("--workload", default="7b", choices=sorted(HIDDEN))
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill measurement")
     ap.add_argument("--layers", type=int, default=0,
                     help="decoder layers of the workload (default: all); smaller values are "
                          "profiling cases, not bench lines")
