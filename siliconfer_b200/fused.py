@@ -4,8 +4,9 @@ q/k/v read the same normed hidden state (siliconfer/model/layers.py:93-95) and
 so do gate/up (layers.py:144).  Stacking their packed rows, scales, zeros and
 biases gives one GEMV over N = sum of the parts: the input is read and
 converted once, one kernel task replaces two or three, and every output row
-is computed exactly as before (a row's arithmetic does not depend on the
-other rows), so the split results are bitwise those of the separate layers.
+is computed with the same per-group arithmetic as before (a row does not
+depend on the other rows); only the decode kernel's k-split, which is chosen
+from N, may change the fp32 summation order.
 """
 from __future__ import annotations
 

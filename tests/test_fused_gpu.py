@@ -1,4 +1,6 @@
-"""Fused same-input projections give bitwise the separate layers' outputs."""
+"""Fused same-input projections give the separate layers' outputs (the
+k-split of the decode kernel depends on N, so fp32 summation order may differ:
+normwise 1e-6)."""
 import numpy as np
 import pytest
 import torch
@@ -26,4 +28,5 @@ def test_qkv_and_gate_up_fused_equal_separate(cuda, asym, t):
         fused = FusedQ4Linear(group)
         ys = fused(x)
         for m, y in zip(group, ys):
-            assert torch.equal(y, m(x))
+            r = m(x).double()
+            assert ((y.double() - r).abs().max() / r.abs().max()).item() <= 1e-6
