@@ -531,6 +531,22 @@ def prefill_measure(device, stream, iters=20):
             "peak_kind": "measured bf16 burst" if peak else None, "shapes": out}
 
 
+def profile_prefill(m, k, n):
+    """Three prefill GEMMs of one config-4 shape (asym int4 g128, bf16 X and Y)."""
+    import torch
+    from siliconfer_b200 import quant as Q
+    from siliconfer_b200.kernels import cuda as K
+    g = torch.Generator(device="cuda")
+    g.manual_seed(m + k + n)
+    W = torch.randn((n, k), generator=g, device="cuda") * 0.02
+    p, s, z = Q.pack_weights_device(W, 128, sym=False)
+    X = torch.randn((m, k), generator=g, device="cuda").to(torch.bfloat16)
+    for _ in range(3):
+        K.linear(p, s, z, X, 128, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_prefill": [m, k, n], "ok": True}))
+
+
 def traffic_from_profile(workload, batch):
     """DRAM bytes per launch of the GEMV kernel, from the committed ncu summary
     (profiles/traffic.txt: lines "<workload>_b<batch> <bytes> <how>"), if any."""
@@ -641,6 +657,8 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill measurement")
+    ap.add_argument("--profile-prefill", type=int, nargs=3, metavar=("M", "K", "N"),
+                    help="run the config-4 prefill GEMM three times on one shape and exit (a profiling case)")
     ap.add_argument("--layers", type=int, default=0,
                     help="decoder layers of the workload (default: all); smaller values are "
                          "profiling cases, not bench lines")
@@ -650,7 +668,9 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
-    if args.impl == "reference":
+    if args.profile_prefill:
+        profile_prefill(*args.profile_prefill)
+    elif args.impl == "reference":
         run_reference(args, rank, world)
     elif args.workload == "70b":
         run_tp(args, rank, world, local_rank)
