@@ -213,6 +213,24 @@ void sf_tp_comm_destroy(void* comm);
 int sf_q4_step_create_tp(const sf_q4_task* tasks, const int* roles, int ntasks, void* comm,
                          void* workspace, size_t workspace_bytes, void** handle_out);
 
+/* ---- decode attention over an int8-quantized KV cache --------------------
+ * Replaces fused_quantized_attention_decode (siliconfer/kernels/metal/
+ * q4_attention.py:200-260) over the cache of siliconfer/model/kv_cache.py:49-69:
+ *   q        [B, H, D] of q_dtype (one decode token per sequence)
+ *   k_codes  [B, Hkv, T, D] int8, k_scales [B, Hkv, T] fp32 (per-vector scale)
+ *   v_codes, v_scales likewise
+ *   out      [B, H, D] of out_dtype = softmax(q.k / sqrt(D)) . v, fp32 math.
+ * H % Hkv == 0 (GQA; group sizes 1, 2, 4, 7, 8), D in {64, 128, 256}.
+ * n_split <= 0 picks the T-split count (sf_kv_attention_splits); the
+ * caller-owned workspace holds the splits' partial results and must have
+ * sf_kv_attention_workspace_bytes(B, H, D, n_split) bytes. */
+size_t sf_kv_attention_workspace_bytes(int B, int H, int D, int n_split);
+int sf_kv_attention_splits(int B, int Hkv, int T);
+int sf_kv_attention_decode(const void* q, int q_dtype, const int8_t* k_codes, const float* k_scales,
+                           const int8_t* v_codes, const float* v_scales, void* out, int out_dtype,
+                           int B, int H, int Hkv, int T, int D, int n_split, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* Device dequant to fp32/fp16/bf16 [N, K].  fp32 output is bit-exact with
    dequantize_sym / dequantize_asym (siliconfer/quant/primitives.py:54-75,
    117-140); fp16/bf16 are that value rounded to nearest even. */

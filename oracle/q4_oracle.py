@@ -186,3 +186,65 @@ def algorithmic_bytes(n: int, k: int, t: int, group_size: int, asym: bool,
     g = k // group_size
     return (n * k // 2 + n * g * 4 + (n * g * zero_bytes if asym else 0)
             + t * k * x_bytes + t * n * y_bytes)
+
+
+# ---------------------------------------------------------------------------
+# Decode attention over the int8 KV cache (siliconfer/model/kv_cache.py:49-69,
+# siliconfer/kernels/metal/q4_attention.py:80-175, 200-260).  Parity for this
+# part is UNPINNED against reference outputs: the reference runs it through
+# MLX/Metal, absent here; these functions restate its arithmetic and are
+# checked in tests against an independent fp64 dequant + softmax.
+# ---------------------------------------------------------------------------
+
+def quantize_kv(x: np.ndarray):
+    """kv_cache.py:49-62: scale = absmax/127 (1 where absmax == 0),
+    q = clip(round(x / scale), -128, 127); returns (int8 codes, fp32 scales [..., ])."""
+    x32 = x.astype(np.float32)
+    amax = np.max(np.abs(x32), axis=-1, keepdims=True)
+    scale = np.where(amax == 0, np.float32(1.0), amax / np.float32(127.0)).astype(np.float32)
+    q = np.clip(np.round(x32 / scale), -128, 127).astype(np.int8)
+    return q, scale[..., 0]
+
+
+def kv_attention_decode(q, k_codes, k_scales, v_codes, v_scales, n_tiles: int = 1):
+    """q4_attention.py:80-175 + 248-256 in fp32: per tile an online softmax
+    over its timesteps (score = q.(k*s)/sqrt(D)), then the flash-attention
+    merge of the tiles' (m, l, acc)."""
+    B, H, D = q.shape
+    Hkv, T = k_codes.shape[1], k_codes.shape[2]
+    G = H // Hkv
+    ts = -(-T // n_tiles)
+    out = np.zeros((B, H, D), np.float32)
+    sf = np.float32(1.0 / np.sqrt(D))
+    for b in range(B):
+        for h in range(H):
+            kvh = h // G
+            k = k_codes[b, kvh].astype(np.float32) * k_scales[b, kvh][:, None].astype(np.float32)
+            v = v_codes[b, kvh].astype(np.float32) * v_scales[b, kvh][:, None].astype(np.float32)
+            ms, ls, accs = [], [], []
+            for t0 in range(0, T, ts):
+                sc = (k[t0:t0 + ts] @ q[b, h].astype(np.float32)) * sf
+                m = sc.max()
+                p = np.exp(sc - m)
+                ms.append(m); ls.append(p.sum()); accs.append(p @ v[t0:t0 + ts])
+            M = max(ms)
+            c = np.exp(np.array(ms, np.float32) - M)
+            L = float(np.sum(np.array(ls) * c))
+            out[b, h] = np.sum(np.stack(accs) * c[:, None], axis=0) / max(L, 1e-20)
+    return out
+
+
+def kv_attention_fp64(q, k_codes, k_scales, v_codes, v_scales):
+    """Independent check: full fp64 dequant, softmax, weighted sum."""
+    B, H, D = q.shape
+    Hkv = k_codes.shape[1]
+    G = H // Hkv
+    k = k_codes.astype(np.float64) * k_scales[..., None]
+    v = v_codes.astype(np.float64) * v_scales[..., None]
+    out = np.zeros((B, H, D))
+    for h in range(H):
+        s = np.einsum("bd,btd->bt", q[:, h].astype(np.float64), k[:, h // G]) / np.sqrt(D)
+        s = np.exp(s - s.max(axis=1, keepdims=True))
+        s /= s.sum(axis=1, keepdims=True)
+        out[:, h] = np.einsum("bt,btd->bd", s, v[:, h // G])
+    return out

@@ -55,10 +55,14 @@ SIGNATURES = {
     "sf_tp_allreduce": [_P, _P, _P, _I, _P, _LL, _I, _P],
     "sf_q4_linear_allreduce": [_P, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P],
     "sf_tp_comm_destroy": [_P],
+    "sf_kv_attention_workspace_bytes": [_I, _I, _I, _I],
+    "sf_kv_attention_splits": [_I, _I, _I],
+    "sf_kv_attention_decode": [_P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _SZ, _P],
 }
 _RESTYPES = {"sf_status_string": ctypes.c_char_p, "sf_last_error": ctypes.c_char_p,
              "sf_q4_launch_count": _LL, "sf_q4_step_workspace_bytes": _SZ,
-             "sf_q4_step_destroy": None, "sf_tp_handle_bytes": _SZ, "sf_tp_comm_destroy": None}
+             "sf_q4_step_destroy": None, "sf_tp_handle_bytes": _SZ, "sf_tp_comm_destroy": None,
+             "sf_kv_attention_workspace_bytes": _SZ}
 
 _lib = None
 

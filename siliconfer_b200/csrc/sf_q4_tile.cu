@@ -146,7 +146,6 @@ struct TileLaunch {
   long long total;        // units in the launch
   int ntasks;
   int prefetch;           // pull a waiting unit's weights into L2 before the wait
-  int xpf;                // bytes per row of the warp's next unit pulled into L2 near the end of a unit (0: off)
   int dbg;                // development: 2 = copies only, 3 = arithmetic only (wrong results)
   unsigned long long* trace;   // development: per unit [start, dependency met, inputs ready, end] ns
   unsigned long long* epoch;   // launch counter (tensor-parallel exchange), advanced by the pre-pass, or null
@@ -778,23 +777,6 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       }
       __syncwarp();
       if (j + kD - 1 < nstage) issue(j + kD - 1);
-      // A few stages before the unit ends, start the first k of this warp's
-      // next unit towards L2, so that its first TMA copies do not see a full
-      // DRAM latency while this warp's ring is empty.
-      if (L.xpf && j == (nstage > kD ? nstage - kD : 0)) {
-        const long long un = u + W_all;
-        if (un < L.total) {
-          int tn = ti;
-          while (tn + 1 < L.ntasks && un >= tile_task(L, tn + 1)->ubase) ++tn;
-          const TileTask* pn = tile_task(L, tn);
-          const int lun = (int)(un - pn->ubase);
-          const int rown = (lun % pn->ntile) * kUnitRows + lane;
-          const int kbn = (lun / pn->ntile) * pn->kper;
-          const int bytes = min(L.xpf, (min(pn->K, kbn + pn->kper) - kbn) >> 1);
-          if (pn->kind == 0 && rown < pn->N && bytes > 0)
-            prefetch_l2(pn->W + (size_t)rown * (pn->K >> 1) + (kbn >> 1), (uint32_t)bytes);
-        }
-      }
     }
     if (!ok) break;
     gseg += (uint32_t)nstage;
@@ -1406,7 +1388,6 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
   L.flags = reinterpret_cast<unsigned int*>(ws);
   L.phctr = reinterpret_cast<unsigned int*>(ws + align256((size_t)128 * c.grid));
   L.prefetch = env_int("SF_TILE_PREFETCH", 1);
-  L.xpf = env_int("SF_TILE_XPF", 256);
   L.dbg = env_int("SF_TILE_DBG", 0);
   L.epoch = nullptr;
   cudaError_t e = cudaMemcpy(table, h.data(), (size_t)ntasks * sizeof(TileTask), cudaMemcpyHostToDevice);
