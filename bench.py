@@ -313,6 +313,7 @@ def run_ours(args, rank, world, local_rank):
     }
     if world == 1 and args.workload == "7b" and not args.no_prefill:
         result["prefill"] = prefill_measure(device, runner.stream)
+        result["kv_attention"] = kv_attention_measure(device, runner.stream)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args, layers)
     if rank == 0:
@@ -529,6 +530,39 @@ def prefill_measure(device, stream, iters=20):
     return {"workload": "BASELINE config 4: gemm_asym prefill, 7B shapes, asym int4 g128, bf16 X",
             "kernel": "q4_gemm_tc_kernel (tcgen05, dequant to bf16 in TMEM)", "peak_tflops": peak,
             "peak_kind": "measured bf16 burst" if peak else None, "shapes": out}
+
+
+def kv_attention_measure(device, stream, iters=20):
+    """Decode attention over the int8 KV cache (siliconfer's
+    fused_quantized_attention_decode) at cache sizes above L2: HBM-bound,
+    bytes = int8 K and V codes + fp32 scales (+ q, out)."""
+    import torch
+    from siliconfer_b200.kv_attention import fused_quantized_attention_decode, quantize_kv
+    peak, _ = measured_peak()
+    out = []
+    g = torch.Generator(device=device)
+    g.manual_seed(3)
+    for B, H, Hkv, T, D in ((16, 64, 8, 8192, 128), (8, 32, 32, 4096, 128)):
+        kc, ks = quantize_kv(torch.randn((B, Hkv, T, D), generator=g, device=device, dtype=torch.bfloat16))
+        vc, vs = quantize_kv(torch.randn((B, Hkv, T, D), generator=g, device=device, dtype=torch.bfloat16))
+        q = torch.randn((B, H, D), generator=g, device=device, dtype=torch.bfloat16)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                fused_quantized_attention_decode(q, kc, ks, vc, vs)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(iters):
+                fused_quantized_attention_decode(q, kc, ks, vc, vs)
+            e1.record(stream)
+        e1.synchronize()
+        us = e0.elapsed_time(e1) / iters * 1e3
+        nbytes = 2 * B * Hkv * T * (D + 4) + B * H * D * 2 + B * H * D * 4
+        out.append({"B": B, "H": H, "Hkv": Hkv, "T": T, "D": D, "us": round(us, 1),
+                    "gbs": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / peak, 4)})
+        del kc, ks, vc, vs, q
+    return {"kernel": "kv_attn_split_kernel + kv_attn_merge_kernel (int8 KV, fp32 online softmax)",
+            "bound": "hbm", "peak_gbs": peak, "timing": "CUDA events around 20 back-to-back calls",
+            "shapes": out}
 
 
 def profile_prefill(m, k, n):
