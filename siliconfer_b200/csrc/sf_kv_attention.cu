@@ -11,7 +11,10 @@
 // flash-attention rule M = max m_i, L = sum l_i e^(m_i - M),
 // out = sum acc_i e^(m_i - M) / max(L, 1e-20)  (q4_attention.py:248-256).
 //
-// B200 layout of the work:
+// Two kernels share this file: a tensor-core kernel for head_dim 64/128 and
+// GQA groups up to 16 (the default, described before kv_attn_tc_kernel), and
+// the CUDA-core kernel below (head_dim 256, or SF_ATTN_SIMT=1).
+// B200 layout of the work (CUDA-core kernel):
 //  * one CTA per (T split, batch, kv head) serves every query head of that kv
 //    head (GQA group), so each K/V byte is read once per group, not once per
 //    query head as in the reference;
@@ -31,6 +34,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 
 #include "sf_q4.h"
 #include "sf_q4_internal.h"
@@ -221,6 +225,290 @@ __global__ void __launch_bounds__(256) kv_attn_merge_kernel(const AttnArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core variant (head_dim 64 or 128, GQA group <= 16): one warp takes 32
+// tokens at a time.
+//  * S = Q K^T on mma.sync m16n8k16 (fp16 in, fp32 accumulate): the G query
+//    rows of the group, padded to 16, are the A operand, split into an fp16
+//    high and low part (two MMAs) so that q keeps about 22 bits; the int8
+//    keys are the B operand, converted exactly (0x6400 | (v + 128) - 1152).
+//    Inside each 16-wide block of head_dim, the order is permuted the same
+//    way in Q and K (logical k 2t, 2t+1, 2t+8, 2t+9 = physical 4t .. 4t+3),
+//    which leaves q.k unchanged and lets each lane fetch its key bytes with
+//    one 32-bit load;
+//  * the scores are scaled per token by k_scale, online softmax per row;
+//  * O += P V with P' = p * v_scale * 2^10 (split high/low, the power of two
+//    keeps P' clear of fp16 subnormals and is divided out at the end) as the
+//    A operand straight from the score accumulators, and the int8 values
+//    staged as fp16 in shared memory and read with ldmatrix.trans.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+// two signed bytes (b0 low) -> exact half2
+__device__ __forceinline__ void i8x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  uint32_t a, b;
+  asm("prmt.b32 %0, %1, %2, 0x4140;" : "=r"(a) : "r"(u), "r"(0x64646464u));
+  asm("prmt.b32 %0, %1, %2, 0x4342;" : "=r"(b) : "r"(u), "r"(0x64646464u));
+  const __half2 off = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+  lo = h2u(__hsub2(*reinterpret_cast<__half2*>(&a), off));
+  hi = h2u(__hsub2(*reinterpret_cast<__half2*>(&b), off));
+}
+__device__ __forceinline__ void split_h2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+  hi = h2u(__halves2half2(h0, h1));
+  lo = h2u(__halves2half2(__float2half_rn(x0 - __half2float(h0)), __float2half_rn(x1 - __half2float(h1))));
+}
+
+// Per-warp shared memory of the tensor-core kernel: two stages of raw int8
+// K and V rows (32 tokens, row pitch D + 16: the 32-bit key-fragment reads of
+// 8 rows land on 8 different bank groups), then the block's values as fp16
+// (row pitch 2D + 16: conflict-free ldmatrix).
+template <int D>
+struct TcAttnLayout {
+  static constexpr int RP = D + 16;                 // raw row pitch
+  static constexpr int RAW = 32 * RP;               // one K or V block
+  static constexpr int STAGE = 2 * RAW;             // K then V
+  static constexpr int PITCH = 2 * D + 16;          // fp16 value rows
+  static constexpr int WARP = 2 * STAGE + 32 * PITCH;
+  static constexpr int SMEM = 4 * WARP;             // kAttnWarps = 4
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(32 * kAttnWarps, 2) kv_attn_tc_kernel(const AttnArgs a) {
+  using Ly = TcAttnLayout<D>;
+  constexpr int KS = D / 16;            // k-steps of S
+  constexpr int DT = D / 8;             // d tiles of O
+  constexpr int CH = D / 16;            // 16-byte chunks per row
+  constexpr float kPScale = 1024.f;
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ float wm[kAttnWarps][16], wl[kAttnWarps][16];
+  const int split = blockIdx.x, bk = blockIdx.y;
+  const int b = bk / a.Hkv, kvh = bk % a.Hkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int G = a.G;
+  // Q fragments (rows g and g + 8 of the group, pre-scaled by 1/sqrt(D)), permuted as above
+  uint32_t qh[KS][4], ql[KS][4];
+#pragma unroll
+  for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {          // r = 0: row g, r = 1: row g + 8
+      const int row = g + 8 * r;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (row < G) {
+        const size_t qo = ((size_t)b * a.H + kvh * G + row) * D + 16 * ks + 4 * t;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = ld_q(a.q, qo + e, a.q_dtype) * a.inv_sqrt_d;
+      }
+      uint32_t h0, l0, h1, l1;
+      split_h2(v[0], v[1], h0, l0);
+      split_h2(v[2], v[3], h1, l1);
+      qh[ks][r] = h0; ql[ks][r] = l0;          // a0 / a1: logical k 2t, 2t+1
+      qh[ks][2 + r] = h1; ql[ks][2 + r] = l1;  // a2 / a3: logical k 2t+8, 2t+9
+    }
+  }
+  const int t0 = split * a.tsplit, t1 = min(a.T, t0 + a.tsplit);
+  const int8_t* kb = a.kc + (size_t)bk * a.T * D;
+  const int8_t* vb = a.vc + (size_t)bk * a.T * D;
+  const float* ksb = a.ks + (size_t)bk * a.T;
+  const float* vsb = a.vs + (size_t)bk * a.T;
+  const uint32_t wbase = smem_u32(smem + warp * Ly::WARP);
+  const uint32_t vtile = wbase + 2 * Ly::STAGE;
+
+  // this warp's blocks: base = t0 + 32 * (warp + kAttnWarps * i)
+  auto issue = [&](int i) {
+    const int base = t0 + 32 * (warp + kAttnWarps * i);
+    if (base < t1) {
+      const uint32_t st = wbase + (uint32_t)(i & 1) * Ly::STAGE;
+#pragma unroll
+      for (int c = lane; c < 32 * CH; c += 32) {
+        const int tok = c / CH, dp = (c % CH) * 16;
+        const bool v = base + tok < t1;
+        const size_t go = (size_t)(v ? base + tok : t0) * D + dp;
+        cp_async16(st + tok * Ly::RP + dp, kb + go, v);
+        cp_async16(st + Ly::RAW + tok * Ly::RP + dp, vb + go, v);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+  float o[DT][4];
+#pragma unroll
+  for (int i = 0; i < DT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+  issue(0);
+  issue(1);
+  for (int i = 0;; ++i) {
+    const int base = t0 + 32 * (warp + kAttnWarps * i);
+    if (base >= t1) break;
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncwarp();
+    const uint32_t st = wbase + (uint32_t)(i & 1) * Ly::STAGE;
+    // the block's values as fp16 (exact)
+#pragma unroll
+    for (int c = lane; c < 32 * CH; c += 32) {
+      const int tok = c / CH, dp = (c % CH) * 16;
+      uint32_t w[4];
+      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                   : "r"(st + Ly::RAW + tok * Ly::RP + dp));
+      uint32_t h[8];
+      i8x4_to_h2x2(w[0], h[0], h[1]);
+      i8x4_to_h2x2(w[1], h[2], h[3]);
+      i8x4_to_h2x2(w[2], h[4], h[5]);
+      i8x4_to_h2x2(w[3], h[6], h[7]);
+      const uint32_t sa = vtile + tok * Ly::PITCH + dp * 2;
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sa), "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3]) : "memory");
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sa + 16), "r"(h[4]), "r"(h[5]), "r"(h[6]), "r"(h[7]) : "memory");
+    }
+    // S = Q K^T for 4 tiles of 8 tokens
+    float s[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+      const uint32_t kr = st + (8 * j + g) * Ly::RP + 4 * t;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        uint32_t w;
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w) : "r"(kr + 16 * ks));
+        uint32_t b0, b1;
+        i8x4_to_h2x2(w, b0, b1);
+        mma16816(s[j], qh[ks], b0, b1);
+        mma16816(s[j], ql[ks], b0, b1);
+      }
+    }
+    // per-token key scale, mask past t1, online softmax on rows g and g + 8
+    float rmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int tok = base + 8 * j + 2 * t + e;
+        const float sk = tok < t1 ? ksb[tok] : 0.f;
+        s[j][e] = tok < t1 ? s[j][e] * sk : -INFINITY;
+        s[j][2 + e] = tok < t1 ? s[j][2 + e] * sk : -INFINITY;
+        rmax[0] = fmaxf(rmax[0], s[j][e]);
+        rmax[1] = fmaxf(rmax[1], s[j][2 + e]);
+      }
+    float corr[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      rmax[r] = fmaxf(rmax[r], __shfl_xor_sync(0xffffffffu, rmax[r], 1));
+      rmax[r] = fmaxf(rmax[r], __shfl_xor_sync(0xffffffffu, rmax[r], 2));
+      const float mn = fmaxf(m[r], rmax[r]);
+      corr[r] = expf(m[r] - mn);
+      m[r] = mn;
+    }
+    float rsum[2] = {0.f, 0.f};
+    uint32_t ph[2][4], pl[2][4];     // A fragments of P' for the two 16-token k-steps
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float pv[4];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int tok = base + 8 * j + 2 * t + e;
+        const float sv = tok < t1 ? vsb[tok] * kPScale : 0.f;
+        const float p0 = expf(s[j][e] - m[0]), p1 = expf(s[j][2 + e] - m[1]);
+        rsum[0] += p0;
+        rsum[1] += p1;
+        pv[e] = p0 * sv;
+        pv[2 + e] = p1 * sv;
+      }
+      const int kk = j >> 1, hf = j & 1;     // tile j is k 0-7 (hf 0) or 8-15 (hf 1) of k-step kk
+      split_h2(pv[0], pv[1], ph[kk][2 * hf], pl[kk][2 * hf]);          // row g
+      split_h2(pv[2], pv[3], ph[kk][2 * hf + 1], pl[kk][2 * hf + 1]);  // row g + 8
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      rsum[r] += __shfl_xor_sync(0xffffffffu, rsum[r], 1);
+      rsum[r] += __shfl_xor_sync(0xffffffffu, rsum[r], 2);
+      l[r] = l[r] * corr[r] + rsum[r];
+    }
+#pragma unroll
+    for (int q = 0; q < DT; ++q) {
+      o[q][0] *= corr[0]; o[q][1] *= corr[0];
+      o[q][2] *= corr[1]; o[q][3] *= corr[1];
+    }
+    __syncwarp();
+    // O += P' V: B fragments of two d tiles per ldmatrix.x4.trans
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+#pragma unroll
+      for (int dn = 0; dn < DT; dn += 2) {
+        const int mi = lane >> 3, rr = lane & 7;
+        const uint32_t addr = vtile + (16 * kk + (mi & 1) * 8 + rr) * Ly::PITCH + (8 * (dn + (mi >> 1))) * 2;
+        uint32_t v0, v1, v2, v3;
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3)
+                     : "r"(addr));
+        mma16816(o[dn], ph[kk], v0, v1);
+        mma16816(o[dn], pl[kk], v0, v1);
+        mma16816(o[dn + 1], ph[kk], v2, v3);
+        mma16816(o[dn + 1], pl[kk], v2, v3);
+      }
+    }
+    __syncwarp();          // stage i & 1 and the fp16 tile are free again
+    issue(i + 2);
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  // merge the warps of this CTA (rows < G), write the split's partial
+  __syncthreads();   // every warp is done with its shared memory
+  auto wacc = reinterpret_cast<float (*)[16][D]>(smem);
+  if (t == 0) {
+    wm[warp][g] = m[0]; wl[warp][g] = l[0];
+    wm[warp][g + 8] = m[1]; wl[warp][g + 8] = l[1];
+  }
+#pragma unroll
+  for (int q = 0; q < DT; ++q) {
+    const int d = 8 * q + 2 * t;
+    wacc[warp][g][d] = o[q][0] / kPScale;
+    wacc[warp][g][d + 1] = o[q][1] / kPScale;
+    wacc[warp][g + 8][d] = o[q][2] / kPScale;
+    wacc[warp][g + 8][d + 1] = o[q][3] / kPScale;
+  }
+  __syncthreads();
+  const size_t nbh = (size_t)a.B * a.H;
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int gg = i / D, d = i % D;
+    float M = -INFINITY;
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w][gg]);
+    float L = 0.f, A = 0.f;
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float c = M == -INFINITY ? 0.f : expf(wm[w][gg] - M);
+      L += wl[w][gg] * c;
+      A += wacc[w][gg][d] * c;
+    }
+    const size_t bhs = ((size_t)b * a.H + kvh * G + gg) * a.nsplit + split;
+    a.part[2 * nbh * a.nsplit + bhs * D + d] = A;
+    if (d == 0) {
+      a.part[2 * bhs] = M;
+      a.part[2 * bhs + 1] = L;
+    }
+  }
+}
+
+template <int D>
+cudaError_t launch_tc_d(const AttnArgs& a, dim3 grid, cudaStream_t st) {
+  using Ly = TcAttnLayout<D>;
+  static_assert(Ly::SMEM >= kAttnWarps * 16 * D * 4, "merge buffer must fit");
+  cudaError_t e = cudaFuncSetAttribute(kv_attn_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM);
+  if (e != cudaSuccess) return e;
+  kv_attn_tc_kernel<D><<<grid, 32 * kAttnWarps, Ly::SMEM, st>>>(a);
+  return cudaGetLastError();
+}
+
 template <int D>
 cudaError_t launch_split_d(const AttnArgs& a, dim3 grid, cudaStream_t st) {
   switch (a.G) {
@@ -235,9 +523,10 @@ cudaError_t launch_split_d(const AttnArgs& a, dim3 grid, cudaStream_t st) {
 }
 
 int choose_splits(int T, int BHkv, int sms) {
-  // enough CTAs for about four per SM, at least 64 tokens per split
-  int want = (4 * sms + BHkv - 1) / BHkv;
-  int cap = (T + 63) / 64;
+  // about two CTAs per SM (the resident count of the tensor-core kernel), at
+  // least 256 tokens per split
+  int want = (2 * sms + BHkv - 1) / BHkv;
+  int cap = (T + 255) / 256;
   if (want > cap) want = cap;
   return want < 1 ? 1 : want;
 }
@@ -287,8 +576,13 @@ int sf_kv_attention_decode(const void* q, int q_dtype, const int8_t* k_codes, co
   a.inv_sqrt_d = 1.0f / sqrtf((float)D);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid((unsigned)n_split, (unsigned)(B * Hkv));
-  cudaError_t e = D == 64 ? launch_split_d<64>(a, grid, st)
-                          : (D == 128 ? launch_split_d<128>(a, grid, st) : launch_split_d<256>(a, grid, st));
+  cudaError_t e;
+  if (D <= 128 && G <= 16 && !getenv("SF_ATTN_SIMT")) {
+    e = D == 64 ? launch_tc_d<64>(a, grid, st) : launch_tc_d<128>(a, grid, st);
+  } else {
+    e = D == 64 ? launch_split_d<64>(a, grid, st)
+                : (D == 128 ? launch_split_d<128>(a, grid, st) : launch_split_d<256>(a, grid, st));
+  }
   if (e != cudaSuccess) return cuda_fail(e, "kv_attn_split_kernel launch");
   kv_attn_merge_kernel<<<(unsigned)(B * H), 128, 0, st>>>(a);
   e = cudaGetLastError();
