@@ -353,6 +353,9 @@ def run_tp(args, rank, world, local_rank):
                                        comm=comm, device=device)
         runners["nccl"] = TPStepRunner(groups, tokens=args.batch, x_dtype=torch.bfloat16, mode="nccl",
                                        device=device)
+    if dist is not None:
+        torch.cuda.synchronize(device)
+        dist.barrier()   # every rank has built its shards before any exchange kernel runs
     g = torch.Generator(device=device)
     g.manual_seed(7 + rank)
     for r in runners.values():
@@ -381,6 +384,7 @@ def run_tp(args, rank, world, local_rank):
         return s0.elapsed_time(s1) / n
 
     main_r = runners["fused"]
+    barrier()
     for _ in range(args.warmup):
         main_r.run()
     main_r.stream.synchronize()

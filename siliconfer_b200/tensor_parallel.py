@@ -357,8 +357,19 @@ class TPStepRunner:
                 _lib.check(self.lib.sf_q4_step_run(self._handles[2 * li + half], st.cuda_stream))
                 self._reduce(li, half, st)
 
+    def _sync_ranks(self):
+        """Line the ranks up before a run whose kernels wait on peers: the
+        exchange waits are bounded (about 2 s), so a rank that is still
+        building its shards would otherwise make the others' waits expire."""
+        if self.world > 1 and self.mode in ("peer", "fused"):
+            import torch.distributed as dist
+            self.torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            self.torch.cuda.synchronize(self.device)
+
     def capture(self):
         torch = self.torch
+        self._sync_ranks()
         with torch.cuda.device(self.device):
             self.stream.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(self.stream):
