@@ -67,3 +67,19 @@ def test_empty_problem_is_a_noop():
     lib = _lib.load()
     assert lib.sf_q4_linear(FAKE, FAKE, None, None, FAKE, 0, FAKE, 0, 0, 128, 1, 64, 0, None) == 0
     assert lib.sf_q4_linear(FAKE, FAKE, None, None, FAKE, 0, FAKE, 0, 8, 128, 0, 64, 0, None) == 0
+
+
+@pytest.mark.parametrize("args,code,msg", [
+    # q, qdt, kc, ks, vc, vs, out, odt, B, H, Hkv, T, D, nsplit, ws, wsbytes, stream
+    ((None, 0, FAKE, FAKE, FAKE, FAKE, FAKE, 0, 1, 8, 2, 16, 64, 1, FAKE, 1 << 20, None), 1, "null"),
+    ((FAKE, 5, FAKE, FAKE, FAKE, FAKE, FAKE, 0, 1, 8, 2, 16, 64, 1, FAKE, 1 << 20, None), 3, "dtype"),
+    ((FAKE, 0, FAKE, FAKE, FAKE, FAKE, FAKE, 0, 1, 8, 3, 16, 64, 1, FAKE, 1 << 20, None), 2, "divisible"),
+    ((FAKE, 0, FAKE, FAKE, FAKE, FAKE, FAKE, 0, 1, 12, 4, 16, 64, 1, FAKE, 1 << 20, None), 6, "group size"),
+    ((FAKE, 0, FAKE, FAKE, FAKE, FAKE, FAKE, 0, 1, 8, 2, 16, 96, 1, FAKE, 1 << 20, None), 6, "head_dim"),
+    ((FAKE, 0, FAKE, FAKE, FAKE, FAKE, FAKE, 0, 1, 8, 2, 16, 64, 4, FAKE, 16, None), 2, "workspace"),
+])
+def test_kv_attention_validation_without_gpu(args, code, msg):
+    lib = _lib.load()
+    assert lib.sf_kv_attention_decode(*args) == code
+    assert msg in lib.sf_last_error().decode()
+    assert lib.sf_kv_attention_workspace_bytes(2, 8, 64, 4) == 2 * 8 * 4 * 66 * 4
