@@ -316,51 +316,137 @@ def run_ours(args, rank, world, local_rank):
         result["kv_attention"] = kv_attention_measure(device, runner.stream)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args, layers)
+    cleanup = None
+    if args.workload == "7b" and not args.no_tp70b:
+        # BASELINE config 5 beside the headline: the 70B step sharded over these
+        # N GPUs (strong scaling), with its parity check
+        del runner, ordered, kernel_graph, layers
+        torch.cuda.empty_cache()
+        result["tp70b"], cleanup = tp_measure(args, rank, world, local_rank, dist)
     if rank == 0:
         print(json.dumps(result), flush=True)
+    _exit_watchdog()
+    if cleanup is not None:
+        cleanup()
     if dist is not None:
         dist.destroy_process_group()
 
 
-def run_tp(args, rank, world, local_rank):
-    """70B-shaped decode step sharded over `world` GPUs.
+TP_BLOCKS = 8   # weights are drawn in 8 blocks along the sharded dimension: the same matrix at any TP 1/2/4/8
+
+
+def _tp_weight(workload, li, pi, device, blocks, seed=1234):
+    """Rank's shard of projection (li, pi), fp32 on `device`: the concatenation
+    of `blocks` (out of TP_BLOCKS) -- row blocks for column-parallel
+    projections, whole-group column blocks for row-parallel ones.  Every block
+    has its own seed, so the unsharded matrix is the same for every world size."""
+    import torch
+    name, n, k = shapes(workload)[pi]
+    row_parallel = name in ("o", "down")
+    gen = torch.Generator(device=device)
+    parts = []
+    for b in blocks:
+        gen.manual_seed(seed + 16 * (7 * li + pi) + b)
+        shape = (n, k // TP_BLOCKS) if row_parallel else (n // TP_BLOCKS, k)
+        parts.append(torch.randn(shape, generator=gen, device=device) * 0.02)
+    return torch.cat(parts, dim=1 if row_parallel else 0), row_parallel
+
+
+def _tp_x(li, pi, k_full, tokens, device):
+    """Unsharded input of projection (li, pi): the same on every rank."""
+    import torch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(900_000 + 7 * li + pi + 7919 * tokens)
+    return torch.randn((tokens, k_full), generator=gen, device=device).to(torch.bfloat16)
+
+
+def _dequant_ref(packed, scales, gs):
+    """fp32 dequant of a symmetric packed triple in torch (w = q * s, the
+    reference's dequantize_sym arithmetic: one exact product per weight)."""
+    import torch
+    n = packed.shape[0]
+    lo = (packed & 15).to(torch.int16)
+    hi = (packed >> 4).to(torch.int16)
+    q = torch.stack([lo, hi], dim=-1).reshape(n, -1)
+    q = torch.where(q >= 8, q - 16, q).float()
+    return (q.reshape(n, -1, gs) * scales[:, :, None]).reshape(n, -1)
+
+
+def tp_measure(args, rank, world, local_rank, dist):
+    """the 70B-shaped decode step sharded over `world` GPUs.
 
     q/k/v/gate/up column-parallel, o/down row-parallel with one all-reduce of
-    [batch, 8192] after each (160 per step).  Both exchanges are timed: this
-    library's NVLink peer all-reduce (headline) and NCCL (baseline)."""
+    [batch, 8192] after each (160 per step).  Times, as device time and max
+    over ranks:
+      fused          the whole step as ONE persistent launch per GPU, every
+                     projection reading its own pre-supplied input, the
+                     all-reduces fused in (tiles pushed over NVLink);
+      fused_ordered  the same launch with the decoder's dependencies: q/k/v ->
+                     o -> o all-reduce -> gate/up -> down -> down all-reduce ->
+                     next layer, each phase waiting for the one before;
+      peer / nccl    one launch per half layer + this library's peer
+                     all-reduce kernel, or + NCCL (world > 1);
+      fused_batch8   the independent fused step at batch 8.
+    Parity: the all-reduced o and down outputs of the first and last layers
+    (every row) against an fp64 product of the unsharded weights' fp32
+    dequant, for the fused, ordered and NCCL runs; tolerance 1e-3 normwise."""
     import torch
     from siliconfer_b200 import _lib
+    from siliconfer_b200.q4_linear import Q4Linear
+    from siliconfer_b200.quant import pack_weights_device
     from siliconfer_b200.tensor_parallel import PeerComm, TPStepRunner
 
+    workload = "70b"
     device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
-    dist = None
+    if TP_BLOCKS % world:
+        return ({"unavailable": f"the 70B weights are drawn in {TP_BLOCKS} blocks; world {world} does not "
+                                f"divide them"}, lambda: None)
+    n_layers = args.tp_layers or HIDDEN[workload][2]
+    hidden = HIDDEN[workload][0]
+    blocks = range(rank * TP_BLOCKS // world, (rank + 1) * TP_BLOCKS // world)
+    t_build = time.perf_counter()
+    groups = []
+    for li in range(n_layers):
+        lay = []
+        for pi in range(7):
+            W, _ = _tp_weight(workload, li, pi, device, blocks)
+            p, s_ = pack_weights_device(W, 128)
+            del W
+            lay.append(Q4Linear(p, s_, group_size=128, device=device))
+        groups.append(lay)
+    torch.cuda.synchronize(device)
     comm = None
     if world > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=device)
-        n_layers = args.layers or HIDDEN[args.workload][2]
-        comm = PeerComm(slot_bytes=max(1 << 20, args.batch * 8192 * 4),
-                        arena_bytes=TPStepRunner.arena_bytes(n_layers, args.batch, HIDDEN[args.workload][0], world))
-    t_build = time.perf_counter()
-    flat = build_layers(args.workload, device, tp_rank=rank, tp_size=world, seed=1234 + 7919 * rank,
-                        n_layers=args.layers)
-    groups = [flat[i:i + 7] for i in range(0, len(flat), 7)]
-    runners = {"fused": TPStepRunner(groups, tokens=args.batch, x_dtype=torch.bfloat16, mode="fused",
-                                     comm=comm, device=device)}
+        arena = 2 * TPStepRunner.arena_bytes(n_layers, 1, hidden, world) + \
+            TPStepRunner.arena_bytes(n_layers, 8, hidden, world)
+        comm = PeerComm(slot_bytes=max(1 << 20, 8 * hidden * 4), arena_bytes=arena)
+    runners = {
+        "fused": TPStepRunner(groups, tokens=1, x_dtype=torch.bfloat16, mode="fused", comm=comm, device=device),
+        "fused_ordered": TPStepRunner(groups, tokens=1, x_dtype=torch.bfloat16, mode="fused", comm=comm,
+                                      device=device, ordered=True),
+        "fused_batch8": TPStepRunner(groups, tokens=8, x_dtype=torch.bfloat16, mode="fused", comm=comm,
+                                     device=device),
+    }
     if world > 1:
-        runners["peer"] = TPStepRunner(groups, tokens=args.batch, x_dtype=torch.bfloat16, mode="peer",
-                                       comm=comm, device=device)
-        runners["nccl"] = TPStepRunner(groups, tokens=args.batch, x_dtype=torch.bfloat16, mode="nccl",
+        runners["peer"] = TPStepRunner(groups, tokens=1, x_dtype=torch.bfloat16, mode="peer", comm=comm,
                                        device=device)
+        runners["nccl"] = TPStepRunner(groups, tokens=1, x_dtype=torch.bfloat16, mode="nccl", device=device)
+    # inputs: the unsharded x of every projection, sliced to this rank's K block where row-parallel
+    for r in runners.values():
+        for li in range(n_layers):
+            for pi in range(7):
+                name, n, k = shapes(workload)[pi]
+                xf = _tp_x(li, pi, k, r.tokens, device)
+                if name in ("o", "down"):
+                    k0 = rank * k // world
+                    xf = xf[:, k0:k0 + k // world]
+                xo = r.slots[li][pi][0]
+                r.x[xo:xo + xf.numel()].copy_(xf.reshape(-1))
+        r.x_host.copy_(r.x.cpu())
     if dist is not None:
         torch.cuda.synchronize(device)
         dist.barrier()   # every rank has built its shards before any exchange kernel runs
-    g = torch.Generator(device=device)
-    g.manual_seed(7 + rank)
     for r in runners.values():
-        r.x.copy_(torch.randn(r.x.shape, generator=g, device=device).to(r.x.dtype))
-        r.x_host.copy_(r.x.cpu())
         r.capture()
     build_s = time.perf_counter() - t_build
 
@@ -383,97 +469,152 @@ def run_tp(args, rank, world, local_rank):
         barrier()
         return s0.elapsed_time(s1) / n
 
+    steps = max(5, min(args.steps, 20))
+    times = {name: timed(r, steps) for name, r in runners.items()}
+    # end to end through the fused step: pinned host activations in, all-reduced outputs out
     main_r = runners["fused"]
-    barrier()
-    for _ in range(args.warmup):
-        main_r.run()
-    main_r.stream.synchronize()
-    barrier()
-    with ClockSampler(local_rank) as clocks:
-        t_end = time.perf_counter() + 5.0
-        while len(clocks.lines) < 2 and time.perf_counter() < t_end:
-            main_r.run()
-            main_r.stream.synchronize()
-        ms = timed(main_r, args.steps)
-    nccl_ms = timed(runners["nccl"], args.steps) if "nccl" in runners else None
-    peer_ms = timed(runners["peer"], args.steps) if "peer" in runners else None
-    # end to end: pinned host activations in, all-reduced outputs out
     for _ in range(args.warmup):
         main_r.run_host()
     main_r.stream.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(main_r.stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         main_r.run_host()
     e1.record(main_r.stream)
     e1.synchronize()
     barrier()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
+    e2e_ms = e0.elapsed_time(e1) / steps
+    # one more plain run of each checked runner, then parity on rank 0's copy
+    for name in ("fused", "fused_ordered", "nccl"):
+        if name in runners:
+            runners[name].run()
+    torch.cuda.synchronize(device)
     dev_err = _lib.load().sf_q4_check_device_error()
-    if dev_err != 0:
-        raise RuntimeError(f"device-side wait expired during the bench (status {dev_err})")
+    parity = {"tol": 1e-3, "checked": "all-reduced o and down outputs of the first and last layer, every row, "
+                                      "vs fp64 product of the unsharded weights' fp32 dequant",
+              "errors": {}}
+    worst = 0.0
+    for li in sorted({0, n_layers - 1}):
+        for pi, which in ((3, 0), (6, 1)):
+            name, n, k = shapes(workload)[pi]
+            W, _ = _tp_weight(workload, li, pi, device, range(TP_BLOCKS))
+            p, s_ = pack_weights_device(W, 128)
+            del W
+            wd = _dequant_ref(p, s_, 128).double()
+            y_ref = _tp_x(li, pi, k, 1, device).double() @ wd.T
+            del wd, p, s_
+            for rn in ("fused", "fused_ordered", "nccl"):
+                if rn not in runners:
+                    continue
+                y = runners[rn].red[li, which].double()
+                err = ((y - y_ref).abs().max() / y_ref.abs().max()).item()
+                parity["errors"][f"{rn}:L{li}.{name}"] = float(f"{err:.3e}")
+                worst = max(worst, err)
+    parity["max_err"] = float(f"{worst:.3e}")
+    parity["ok"] = bool(worst <= 1e-3 and dev_err == 0)
     step_bytes = main_r.algorithmic_bytes()
+    t = torch.tensor([times[k_] for k_ in sorted(times)] + [e2e_ms, float(not parity["ok"])],
+                     device=device, dtype=torch.float64)
     if dist is not None:
-        t = torch.tensor([ms, e2e_ms, nccl_ms or 0.0, peer_ms or 0.0, float(step_bytes)], device=device,
-                         dtype=torch.float64)
-        tmax = t.clone()
-        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-        tsum = t.clone()
-        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
-        ms, e2e_ms, nccl_ms, peer_ms = tmax[0].item(), tmax[1].item(), tmax[2].item(), tmax[3].item()
-        total_bytes = int(tsum[4].item())
-    else:
-        total_bytes = step_bytes
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    vals = t.tolist()
+    times = dict(zip(sorted(times), vals[:len(times)]))
+    e2e_ms = vals[len(times)]
+    parity["ok_all_ranks"] = vals[-1] == 0.0
     peak, peak_kind = measured_peak()
-    value = total_bytes / (ms * 1e-3) / 1e9
+    ms = times["fused"]
     per_gpu = step_bytes / (ms * 1e-3) / 1e9
-    xin = main_r.x.numel() * main_r.x.element_size()
-    yout = main_r.red.numel() * 4
+    out = {
+        "workload": f"BASELINE config 5: {workload}-shaped decode step, {n_layers} layers x 7 projections, "
+                    f"sym int4 g128, bf16 activations, sharded over {world} GPU(s)",
+        "parallelism": f"tp{world}: q/k/v/gate/up column-parallel, o/down row-parallel + all-reduce "
+                       f"({2 * n_layers} per step)",
+        "scaling": "strong",
+        "n_gpus": world,
+        "batch": 1,
+        "fused_us": round(ms * 1e3, 1),
+        "fused_ordered_us": round(times["fused_ordered"] * 1e3, 1),
+        "fused_batch8_us": round(times["fused_batch8"] * 1e3, 1),
+        "peer_us": round(times["peer"] * 1e3, 1) if "peer" in times else None,
+        "nccl_us": round(times["nccl"] * 1e3, 1) if "nccl" in times else None,
+        "gbs_per_gpu": round(per_gpu, 1),
+        "gbs_aggregate": round(per_gpu * world, 1),
+        "bytes_per_gpu": step_bytes,
+        "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "peak_kind": peak_kind,
+                     "frac": round(per_gpu / peak, 4), "hbm_bound_us": round(step_bytes / peak / 1e3, 1),
+                     "note": "whole fused step per GPU (GEMV streaming + in-kernel all-reduces)"},
+        "e2e_us": round(e2e_ms * 1e3, 1),
+        "parity": parity,
+        "timing": f"CUDA events over {steps} graph replays per variant, max over ranks",
+        "data": "seeded N(0,0.02) weights drawn in 8 blocks (the same matrix at every TP), RTN int4 on "
+                "the device; bf16 N(0,1) inputs shared by every rank",
+        "build_s": round(build_s, 1),
+    }
+    if dev_err != 0:
+        out["device_error"] = dev_err
+    del main_r
+    # the caller prints its line first, then releases graphs and the communicator
+    return out, (lambda: _teardown(dist, comm, runners, exit_dist=False))
+
+
+def run_tp(args, rank, world, local_rank):
+    """--workload 70b: the config-5 tensor-parallel step as its own JSON line."""
+    import torch
+    if args.layers and not args.tp_layers:
+        args.tp_layers = args.layers
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=device)
+    with ClockSampler(local_rank) as clocks:
+        tp, cleanup = tp_measure(args, rank, world, local_rank, dist)
+    if "unavailable" in tp:
+        if rank == 0:
+            print(json.dumps({"metric": "int4 GEMV HBM GB/s, 70b tensor-parallel decode step", **tp}))
+        return
+    total = tp["bytes_per_gpu"] * world
     result = {
-        "metric": f"int4 GEMV HBM GB/s, {args.workload} tensor-parallel decode step (batch {args.batch})",
-        "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 5), "decode_step_us": round(ms * 1e3, 2),
-        "decode_step_us_nccl": None if nccl_ms is None else round(nccl_ms * 1e3, 2),
-        "decode_step_us_unfused_peer": None if peer_ms is None else round(peer_ms * 1e3, 2),
+        "metric": "int4 GEMV HBM GB/s, 70b tensor-parallel decode step (batch 1)",
+        "value": round(total / tp["fused_us"] / 1e3, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(tp["fused_us"] / 1e3, 5),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int4 weights (u8 nibbles) x bf16 activations, exact int32 products, fp32 accumulate",
-        "data": "synthetic: seeded N(0,0.02) weights per shard, RTN int4 sym g128 (device pack); bf16 N(0,1) activations",
-        "config": {"workload": f"BASELINE config 5: {args.workload}-shaped decode step, {len(groups)} layers x 7 "
-                               f"projections sharded over {world} GPU(s), each projection reading its own "
-                               f"pre-supplied input",
-                   "batch": args.batch, "group_size": 128, "layout": "sym",
-                   "parallelism": f"tp{world}: q/k/v/gate/up column-parallel, o/down row-parallel + "
-                                  f"all-reduce ({2 * len(groups)} per step); headline: the whole step as one "
-                                  f"persistent launch with the all-reduces fused (tiles pushed over NVLink); "
-                                  f"beside it: one launch per half layer + peer all-reduce kernel, and + NCCL",
+        "data": "synthetic: " + tp["data"],
+        "config": {"workload": tp["workload"], "batch": 1, "parallelism": tp["parallelism"],
                    "l2": "weights >> L2 (no flush needed)"},
-        "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(per_gpu / peak, 4), "peak_kind": peak_kind,
-                     "kernel": "whole step per GPU (one persistent GEMV launch with fused all-reduces)",
-                     "bytes_per_launch": step_bytes, "traffic": None},
-        "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": xin, "d2h_bytes_per_step": yout,
+        "roofline": {**tp["roofline"], "unit": "GB/s", "traffic": None},
+        "e2e": {"value": round(total / tp["e2e_us"] / 1e3, 1), "unit": "GB/s",
+                "ms_per_step": round(tp["e2e_us"] / 1e3, 5), "h2d_bytes_per_step": None,
+                "d2h_bytes_per_step": None,
                 "api": "siliconfer_b200.tensor_parallel.TPStepRunner.run_host (pinned host in/out)"},
-        "gpu_launches": main_r.launches_per_step() * args.steps,
+        "gpu_launches": 2 * args.steps,
         "clocks": clocks.summary(),
-        "build_s": round(build_s, 1),
+        "tp70b": tp,
     }
     if rank == 0:
         print(json.dumps(result), flush=True)
-    _teardown(dist, comm, runners, main_r)
+    _exit_watchdog()
+    cleanup()
+    if dist is not None:
+        dist.destroy_process_group()
 
 
-def _teardown(dist, comm, runners, *refs):
-    """Release captured graphs before the process group, then exit.  A
-    watchdog ends the process if a library's teardown blocks (the result line
-    is already printed)."""
-    import gc
-    import torch
+def _exit_watchdog(seconds=60):
+    """Ends the process if teardown blocks after the result line was printed."""
     def _force_exit():
-        time.sleep(60)
+        time.sleep(seconds)
         os._exit(0)
     threading.Thread(target=_force_exit, daemon=True).start()
+
+
+def _teardown(dist, comm, runners, *refs, exit_dist=True):
+    """Release captured graphs and the peer communicator (every rank together),
+    then optionally the process group."""
+    import gc
+    import torch
     torch.cuda.synchronize()
     runners.clear()
     del refs
@@ -484,7 +625,9 @@ def _teardown(dist, comm, runners, *refs):
     if comm is not None:
         comm.close()
     if dist is not None:
-        dist.destroy_process_group()
+        dist.barrier()
+        if exit_dist:
+            dist.destroy_process_group()
 
 
 def prefill_measure(device, stream, iters=20):
@@ -699,6 +842,11 @@ def main():
                     help="run the config-4 prefill GEMM three times on one shape and exit (a profiling case)")
     ap.add_argument("--layers", type=int, default=0,
                     help="decoder layers of the workload (default: all); smaller values are "
+                         "profiling cases, not bench lines")
+    ap.add_argument("--no-tp70b", action="store_true",
+                    help="skip the config-5 tensor-parallel 70B step that the default line carries as 'tp70b'")
+    ap.add_argument("--tp-layers", type=int, default=0,
+                    help="decoder layers of the tp70b step (default: all 80); smaller values are "
                          "profiling cases, not bench lines")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -172,7 +172,13 @@ int sf_q4_linear_static_scratch(const uint8_t* W, const float* scales, const flo
  *                      bytes, in rank order).
  * Every rank must issue the same sequence of all-reduce calls.  Waits on
  * peers are bounded (about 2 s); on expiry the kernel returns early and
- * sf_q4_check_device_error() reports SF_ERR_TIMEOUT. */
+ * sf_q4_check_device_error() reports SF_ERR_TIMEOUT.  An expired wait
+ * POISONS the communicator for good: the ranks' call epochs are out of step,
+ * so the rank that gave up marks its buffer and every peer's flag.  A peer
+ * that arrives late, and every later all-reduce or fused step on any rank,
+ * then returns at once without summing anything, and
+ * sf_q4_check_device_error() reports SF_ERR_COMM.  Destroy the communicator
+ * and create it again (on every rank) to continue. */
 size_t sf_tp_handle_bytes(void);
 int sf_tp_comm_init(int rank, int world, size_t slot_bytes, size_t arena_bytes, void** comm_out,
                     void* handle_out);
@@ -245,8 +251,9 @@ int sf_q4_quantize_pack(const float* W, uint8_t* packed, float* scales, float* z
                         int N, int K, int group_size, void* stream);
 
 /* Sticky device-side error word (set when a bounded wait inside a kernel
-   expires).  Synchronous: reads and clears it.  Returns SF_OK or
-   SF_ERR_TIMEOUT. */
+   expires, or when a tensor-parallel kernel met a poisoned communicator).
+   Synchronous: reads and clears it.  Returns SF_OK, SF_ERR_TIMEOUT, or
+   SF_ERR_COMM (poisoned communicator; takes precedence). */
 int sf_q4_check_device_error(void);
 
 /* Number of kernels this library has launched since load (host counter). */

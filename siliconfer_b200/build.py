@@ -37,15 +37,30 @@ def needs_build() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> pathlib.Path:
+    """Compiles every source to an object in parallel (nvcc is single-threaded
+    per file), then links the shared library."""
+    from concurrent.futures import ThreadPoolExecutor
     if not force and not needs_build():
         return LIB
-    srcs = [str(p) for p in SOURCES if p.exists()]
-    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-           f"-I{ROOT / 'include'}", f"-I{PKG / 'csrc'}", "-o", str(LIB) + ".tmp", *srcs]
+    srcs = [p for p in SOURCES if p.exists()]
+    objdir = PKG / "_build"
+    objdir.mkdir(exist_ok=True)
+    flags = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+             f"-I{ROOT / 'include'}", f"-I{PKG / 'csrc'}"]
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd))
-    subprocess.run(cmd, check=True)
+        flags.insert(0, "-Xptxas=-v")
+
+    def compile_one(src):
+        obj = objdir / (src.stem + ".o")
+        cmd = [nvcc(), *flags, "-c", str(src), "-o", str(obj)]
+        if verbose:
+            print(" ".join(cmd))
+        subprocess.run(cmd, check=True)
+        return str(obj)
+
+    with ThreadPoolExecutor(max_workers=max(1, min(len(srcs), os.cpu_count() or 1))) as ex:
+        objs = list(ex.map(compile_one, srcs))
+    subprocess.run([nvcc(), *ARCH, "-shared", "-o", str(LIB) + ".tmp", *objs], check=True)
     os.replace(str(LIB) + ".tmp", LIB)
     return LIB
 

@@ -400,6 +400,10 @@ int sf_q4_check_device_error(void) {
                      c = take_dev_error_gemv_tc() | take_dev_error_tile() | take_dev_error_tp();
   if (a == 0xffffffffu || b == 0xffffffffu || c == 0xffffffffu)
     return fail(SF_ERR_CUDA, "reading the device error word failed");
+  if ((a | b | c) & kErrPoisoned)
+    return fail(SF_ERR_COMM,
+                "a tensor-parallel exchange met a poisoned communicator (a rank's bounded wait expired in an "
+                "earlier call; create the communicator again) (code %u)", a | b | c);
   if (a | b | c) return fail(SF_ERR_TIMEOUT, "a device-side wait expired (code %u)", a | b | c);
   return SF_OK;
 }

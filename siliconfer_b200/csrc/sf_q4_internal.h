@@ -97,6 +97,13 @@ static __device__ unsigned int g_dev_error = 0;
     if (v) cudaMemcpyToSymbol(g_dev_error, &z, sizeof(z));                \
     return v;                                                             \
   }
+// Error-word bit of a kernel that met a poisoned tensor-parallel communicator
+// (sf_q4_check_device_error reports SF_ERR_COMM); other bits are expired waits.
+constexpr unsigned int kErrPoisoned = 1u << 20;
+// Flag value that a rank whose exchange wait expired stores into its peers'
+// flag words: a peer that arrives late sees it and fails instead of reading
+// a slot that no longer belongs to its call.
+constexpr unsigned long long kFlagPoison = ~0ull;
 unsigned int take_dev_error_gemv();
 unsigned int take_dev_error_gemv_tc();
 unsigned int take_dev_error_tc();
@@ -108,8 +115,9 @@ unsigned int take_dev_error_tp();
 // data = 2 parities x world x `src_bytes`, then `tiles` x world u64 flags.
 // Fills every rank's mapped data/flag pointers, this rank, the world size and
 // the byte size of one parity half.
+// Also gives the communicator's sticky poison word (this rank's copy).
 int tp_region(void* comm, size_t src_bytes, size_t tiles, uint8_t** data, unsigned long long** flags, int* rank,
-              int* world, size_t* par_bytes);
+              int* world, size_t* par_bytes, unsigned long long** poison);
 
 // Decode GEMV (1 <= T <= kMaxGemvT) on the warp-unit kernel; SF_ERR_UNSUPPORTED
 // when the shape is not one it takes.

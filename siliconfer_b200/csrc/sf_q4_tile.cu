@@ -149,6 +149,7 @@ struct TileLaunch {
   int dbg;                // development: 2 = copies only, 3 = arithmetic only (wrong results)
   unsigned long long* trace;   // development: per unit [start, dependency met, inputs ready, end] ns
   unsigned long long* epoch;   // launch counter (tensor-parallel exchange), advanced by the pre-pass, or null
+  unsigned long long* poison;  // the communicator's sticky poison word (tensor-parallel steps), or null
 };
 
 __device__ __forceinline__ const TileTask* tile_task(const TileLaunch& L, int i) {
@@ -516,6 +517,19 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
 
   const long long W_all = (long long)gridDim.x * (blockDim.x >> 5);
   const unsigned long long ep = L.epoch ? launch_epoch(L) : 0ull;   // this launch's exchange epoch
+  if (L.poison && *reinterpret_cast<volatile const unsigned long long*>(L.poison)) {
+    // An earlier step gave up on a peer: compute nothing, and poison every
+    // pushed tile's flag in every peer so that their reduce tasks fail at once.
+    if (warp == 0 && blockIdx.x == 0 && lane == 0) atomicOr(&g_dev_error, kErrPoisoned);
+    for (int ti2 = 0; ti2 < L.ntasks; ++ti2) {
+      const TileTask* p = tile_task(L, ti2);
+      if (!p->push) continue;
+      for (long long t2 = (long long)warp * gridDim.x + blockIdx.x; t2 < p->ntile; t2 += W_all)
+        if (lane < p->tp_world)
+          st_release_sys_u64(p->xflag[lane] + (size_t)t2 * p->tp_world + p->tp_rank, kFlagPoison);
+    }
+    return;
+  }
   uint32_t gseg = 0;   // segments this warp has consumed (ring position and phase)
   int ti = 0;
   bool ok = true;
@@ -590,19 +604,36 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       // ---- all-reduce of a pushed task: tile = lu (one unit per 32-row tile) ----
       const unsigned long long* fl = p->xflag[p->tp_rank] + (size_t)lu * p->tp_world;
       int okf = 1;
-      if (lane < p->tp_world && ld_acquire_sys_u64(fl + lane) < ep) {
+      if (lane < p->tp_world) {
+        unsigned long long v = ld_acquire_sys_u64(fl + lane);
         const long long t0 = clock64();
-        while (ld_acquire_sys_u64(fl + lane) < ep) {
+        while (v < ep) {
           if (clock64() - t0 > kWaitCycles) {
             atomicOr(&g_dev_error, 0x2000u);
             okf = 0;
             break;
           }
           __nanosleep(32);
+          v = ld_acquire_sys_u64(fl + lane);
+        }
+        if (v == kFlagPoison) {   // that rank gave up on an earlier step
+          atomicOr(&g_dev_error, kErrPoisoned);
+          okf = 0;
         }
       }
+      // the acquiring lanes' loads are ordered before the other lanes' reads below
+      __syncwarp();
       ok = __all_sync(0xffffffffu, okf) != 0;
-      if (!ok) break;
+      if (!ok) {
+        // the ranks are out of step for good: poison the communicator and this
+        // tile's flag in every peer, so that no peer sums a stale region
+        if (lane == 0 && L.poison) *reinterpret_cast<volatile unsigned long long*>(L.poison) = 1ull;
+        if (lane < p->tp_world) {
+          __threadfence_system();
+          st_release_sys_u64(p->xflag[lane] + (size_t)lu * p->tp_world + p->tp_rank, kFlagPoison);
+        }
+        break;
+      }
       const int row = lu * kUnitRows + lane;
       if (row < N) {
         const float bv = p->bias ? __ldg(p->bias + row) : 0.f;
@@ -1306,6 +1337,7 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
   uint8_t* part = table + z.table;
   uint8_t* xblk = part + z.part;
   std::vector<TileTask> h(ntasks);
+  unsigned long long* poison = nullptr;
   long long ub = 0;
   int nph = 0, xny = 1;
   for (int i = 0; i < ntasks; ++i) {
@@ -1346,7 +1378,8 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
         q.tp_world = sq.tp_world;
       } else {
         const size_t data = (size_t)T * a.N * 4;   // one source rank's [T][N] fp32
-        int rc2 = tp_region(comm, data, (size_t)q.ntile, q.xdata, q.xflag, &q.tp_rank, &q.tp_world, &q.xpar);
+        int rc2 = tp_region(comm, data, (size_t)q.ntile, q.xdata, q.xflag, &q.tp_rank, &q.tp_world, &q.xpar,
+                            &poison);
         if (rc2 != SF_OK) return rc2;
       }
     }
@@ -1390,6 +1423,7 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
   L.prefetch = env_int("SF_TILE_PREFETCH", 1);
   L.dbg = env_int("SF_TILE_DBG", 0);
   L.epoch = nullptr;
+  L.poison = poison;
   cudaError_t e = cudaMemcpy(table, h.data(), (size_t)ntasks * sizeof(TileTask), cudaMemcpyHostToDevice);
   if (e == cudaSuccess && has_tp) {
     L.epoch = reinterpret_cast<unsigned long long*>(ws + z.total());
@@ -1424,6 +1458,10 @@ int sf_q4_step_launch(void* handle, void* stream, int part) {
   if (part == 2 && hd->coop)
     return fail(SF_ERR_UNSUPPORTED,
                 "the GEMV kernel alone needs a single-phase step without exchange tasks (no wait_before)");
+  if (part == 1 && hd->tp)
+    return fail(SF_ERR_UNSUPPORTED,
+                "a step with exchange tasks runs whole (part 0): the pre-pass alone would advance its exchange "
+                "epoch without the exchange");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSuccess;
   if (part != 2) {

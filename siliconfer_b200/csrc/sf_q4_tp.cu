@@ -10,7 +10,7 @@
 // its state on the device (so a captured CUDA graph can replay it):
 //  * every rank owns one exchange buffer (cudaMalloc, exported as a CUDA IPC
 //    handle and opened by every peer): a header (call epoch, finished-block
-//    count), a flag word per (reduce block, source rank), then two fp32 slots
+//    count, poison word), a flag word per (reduce block, source rank), then two fp32 slots
 //    used on alternate calls; and a private partial buffer that the
 //    row-parallel GEMV writes;
 //  * call e (e = device epoch + 1, read by every block at start) splits the
@@ -26,6 +26,13 @@
 //    reading that slot.
 // A wait that expires sets the library's device error word and the kernel
 // returns; the host reads SF_ERR_TIMEOUT from sf_q4_check_device_error().
+// After an expired wait the ranks' epochs are out of step for good, so the
+// communicator is poisoned: the rank that gave up sets its sticky poison word
+// and overwrites its flag in every peer with kFlagPoison.  A peer that
+// arrives late sees that value instead of a flag it could take for its own
+// call, and every later call on either side finds a poison word or a poison
+// flag and returns at once with kErrPoisoned (SF_ERR_COMM on the host) until
+// the communicator is created again.
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -88,11 +95,21 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
 
 __global__ void __launch_bounds__(256) tp_allreduce_kernel(const ReduceArgs a) {
   __shared__ unsigned long long ep_s;
-  __shared__ int ok;
+  __shared__ int ok, poisoned;
   uint8_t* mine = a.peer[a.rank];
-  auto* hdr = reinterpret_cast<unsigned long long*>(mine);   // [0] epoch, [1] finished blocks
-  if (threadIdx.x == 0) ep_s = *reinterpret_cast<volatile unsigned long long*>(hdr) + 1;
+  auto* hdr = reinterpret_cast<unsigned long long*>(mine);   // [0] epoch, [1] finished blocks, [2] poison
+  if (threadIdx.x == 0) {
+    ep_s = *reinterpret_cast<volatile unsigned long long*>(hdr) + 1;
+    poisoned = *reinterpret_cast<volatile unsigned long long*>(hdr + 2) != 0;
+  }
   __syncthreads();
+  if (poisoned) {   // an earlier call gave up: tell the peers and touch nothing else
+    if (threadIdx.x < (unsigned)a.world)
+      st_release_sys(reinterpret_cast<unsigned long long*>(a.peer[threadIdx.x] + kHeader) +
+                         (size_t)blockIdx.x * kMaxRanks + a.rank, kFlagPoison);
+    if (threadIdx.x == 0) atomicOr(&g_dev_error, kErrPoisoned);
+    return;
+  }
   const unsigned long long ep = ep_s;
   const size_t slot = kSlot0 + (size_t)(ep & 1) * a.slot_bytes;
   const long long nchunks = (a.count + kChunk - 1) / kChunk;
@@ -118,22 +135,37 @@ __global__ void __launch_bounds__(256) tp_allreduce_kernel(const ReduceArgs a) {
     int good = 1;
     const auto* fl = reinterpret_cast<const unsigned long long*>(mine + kHeader) + (size_t)blockIdx.x * kMaxRanks;
     for (int p = 0; p < a.world && good; ++p) {
-      if (ld_acquire_sys(fl + p) >= ep) continue;
+      unsigned long long v = ld_acquire_sys(fl + p);
       const long long t0 = clock64();
-      while (ld_acquire_sys(fl + p) < ep) {
+      while (v < ep) {
         if (clock64() - t0 > kWaitCycles) {
           atomicOr(&g_dev_error, kErrTpWait);
           good = 0;
           break;
         }
         __nanosleep(32);
+        v = ld_acquire_sys(fl + p);
+      }
+      if (v == kFlagPoison) {   // that peer gave up on an earlier call
+        atomicOr(&g_dev_error, kErrPoisoned);
+        good = 0;
       }
     }
+    if (!good) *reinterpret_cast<volatile unsigned long long*>(hdr + 2) = 1ull;
     ok = good;
   }
   __syncthreads();
+  if (!ok) {
+    // poison this block's flag in every peer (it may already hold this call's epoch)
+    if (threadIdx.x < (unsigned)a.world) {
+      __threadfence_system();
+      st_release_sys(reinterpret_cast<unsigned long long*>(a.peer[threadIdx.x] + kHeader) +
+                         (size_t)blockIdx.x * kMaxRanks + a.rank, kFlagPoison);
+    }
+    return;
+  }
   // 3. Y = sum over ranks in rank order (+ bias)
-  if (ok) {
+  {
     for (long long c = blockIdx.x; c < nchunks; c += gridDim.x) {
       const long long i = c * kChunk + 4 * threadIdx.x;
       if (i >= a.count) continue;
@@ -191,7 +223,7 @@ Comm* as_comm(void* h) { return static_cast<Comm*>(h); }
 }  // namespace
 
 int tp_region(void* comm, size_t src_bytes, size_t tiles, uint8_t** data, unsigned long long** flags, int* rank,
-              int* world, size_t* par_bytes) {
+              int* world, size_t* par_bytes, unsigned long long** poison) {
   Comm* c = as_comm(comm);
   for (int p = 0; p < c->world; ++p)
     if (!c->peer[p]) return fail(SF_ERR_COMM, "rank %d is not connected (call sf_tp_comm_connect)", p);
@@ -209,6 +241,7 @@ int tp_region(void* comm, size_t src_bytes, size_t tiles, uint8_t** data, unsign
   *rank = c->rank;
   *world = c->world;
   *par_bytes = par;
+  *poison = reinterpret_cast<unsigned long long*>(c->local) + 2;
   return SF_OK;
 }
 }  // namespace sf

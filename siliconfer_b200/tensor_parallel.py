@@ -54,9 +54,17 @@ def _slice(a, rows=None, cols=None):
     return np.ascontiguousarray(a)
 
 
-def shard_column(packed, scales, zeros, rank: int, world: int, bias=None):
-    """Rank's block of output rows (column-parallel): (packed, scales, zeros, bias)."""
-    lo, hi = shard_bounds(packed.shape[0], world, rank)
+def shard_column(packed, scales, zeros, rank: int, world: int, bias=None, unit: int = 1):
+    """Rank's block of output rows (column-parallel): (packed, scales, zeros, bias).
+
+    ``unit`` > 1 keeps blocks of ``unit`` rows together -- ``head_dim`` for
+    q/k/v, so that attention heads stay whole on one rank -- and then the
+    blocks must divide evenly over the ranks (every rank the same head count);
+    a ValueError says so otherwise."""
+    n = packed.shape[0]
+    if unit > 1 and (n % unit or (n // unit) % world):
+        raise ValueError(f"{n} rows = {n / unit:g} heads of {unit} rows do not divide evenly over {world} ranks")
+    lo, hi = shard_bounds(n, world, rank, unit)
     b = None if bias is None else bias[lo:hi]
     return _slice(packed, rows=(lo, hi)), _slice(scales, rows=(lo, hi)), _slice(zeros, rows=(lo, hi)), b
 
@@ -112,13 +120,15 @@ class PeerComm:
 
 
 class ColumnParallelQ4Linear:
-    """Rank's block of output rows of a Q4Linear; forward gives that block of Y."""
+    """Rank's block of output rows of a Q4Linear; forward gives that block of Y.
+
+    Pass ``unit=head_dim`` for q/k/v so that heads are never split."""
 
     def __init__(self, packed, scales, zeros=None, bias=None, group_size: int = 128, *,
-                 rank: int, world: int, device=None, out_dtype=None):
+                 rank: int, world: int, device=None, out_dtype=None, unit: int = 1):
         from .q4_linear import Q4Linear
-        p, s, z, b = shard_column(packed, scales, zeros, rank, world, bias)
-        self.rows = shard_bounds(packed.shape[0], world, rank)
+        p, s, z, b = shard_column(packed, scales, zeros, rank, world, bias, unit)
+        self.rows = shard_bounds(packed.shape[0], world, rank, unit)
         self.local = Q4Linear(p, s, zeros=z, bias=b, group_size=group_size, device=device,
                               out_dtype=out_dtype)
 
@@ -198,9 +208,14 @@ class TPStepRunner:
     """
 
     ROW_PARALLEL = (False, False, False, True, False, False, True)
+    # with ordered=True (fused mode): which projections wait for everything
+    # before them -- q (the previous layer's down all-reduce), o (q/k/v), gate
+    # (the o all-reduce), down (gate/up); the decoder's order
+    # (siliconfer/model/layers.py:93-95, 133, 144)
+    LAYER_WAITS = (True, False, False, True, True, False, True)
 
     def __init__(self, layers, tokens: int = 1, x_dtype=None, mode: str = "peer",
-                 comm: PeerComm | None = None, group=None, device=None):
+                 comm: PeerComm | None = None, group=None, device=None, ordered: bool = False):
         import torch
         import torch.distributed as dist
         self.torch = torch
@@ -208,6 +223,9 @@ class TPStepRunner:
         self.tokens = int(tokens)
         self.x_dtype = x_dtype or torch.float16
         self.mode, self.comm, self.group = mode, comm, group
+        if ordered and mode != "fused":
+            raise ValueError("ordered=True needs mode='fused' (the unfused modes run in order already)")
+        self.ordered = bool(ordered)
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         if self.world > 1 and mode in ("peer", "fused") and comm is None:
             raise ValueError(f"mode={mode!r} needs a PeerComm")
@@ -248,7 +266,12 @@ class TPStepRunner:
         return 2 * n_layers * (2 * par + flags)
 
     def _make_fused(self):
-        """Every layer's seven projections and two all-reduces as one step."""
+        """Every layer's seven projections and two all-reduces as one step.
+
+        Independent (default): every task reads its pre-supplied input at once.
+        Ordered: the projections named in LAYER_WAITS open a new phase and read
+        their input only after every earlier task (all-reduces included) has
+        written its output, as a decoder would."""
         from .kernels.cuda import _dtype_code
         torch = self.torch
         tasks, roles = [], []
@@ -257,24 +280,25 @@ class TPStepRunner:
             for i, m in enumerate(lay):
                 xo, yo = self.slots[li][i]
                 row = self.ROW_PARALLEL[i]
+                wait = 1 if (self.ordered and self.LAYER_WAITS[i] and (li, i) != (0, 0)) else 0
                 base = (m.packed_d.data_ptr(), m.scales_d.data_ptr(),
                         None if m.zeros_d is None else m.zeros_d.data_ptr())
                 xp = self.x.data_ptr() + xo * xs
                 if not row:
                     tasks.append(_lib.Q4Task(*base, None if m.bias_d is None else m.bias_d.data_ptr(), xp,
                                              self.y.data_ptr() + yo * 4, m.out_features, m.in_features,
-                                             self.tokens, m.group_size, _dtype_code(self.x), _lib.SF_F32, 0))
+                                             self.tokens, m.group_size, _dtype_code(self.x), _lib.SF_F32, wait))
                     roles.append(0)
                     continue
                 out = self.red[li, 0 if i == 3 else 1]
                 if self.world == 1:
                     tasks.append(_lib.Q4Task(*base, None, xp, out.data_ptr(), m.out_features, m.in_features,
-                                             self.tokens, m.group_size, _dtype_code(self.x), _lib.SF_F32, 0))
+                                             self.tokens, m.group_size, _dtype_code(self.x), _lib.SF_F32, wait))
                     roles.append(0)
                     continue
                 src = len(tasks)
                 tasks.append(_lib.Q4Task(*base, None, xp, None, m.out_features, m.in_features, self.tokens,
-                                         m.group_size, _dtype_code(self.x), _lib.SF_F32, 0))
+                                         m.group_size, _dtype_code(self.x), _lib.SF_F32, wait))
                 roles.append(1)
                 tasks.append(_lib.Q4Task(*base, None, xp, out.data_ptr(), m.out_features, m.in_features,
                                          self.tokens, m.group_size, _dtype_code(self.x), _lib.SF_F32, 0))

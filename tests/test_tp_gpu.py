@@ -6,7 +6,9 @@ Row-parallel shards summed by the library's NVLink all-reduce
 every rank must hold bitwise the same Y from the peer all-reduce, and
 alternating exchange slots must stay correct over repeated calls.  A rank
 that does not join a call makes the other rank's bounded wait expire with
-SF_ERR_TIMEOUT instead of hanging.  NVLS is off (NCCL_NVLS_ENABLE=0) and the
+SF_ERR_TIMEOUT instead of hanging, and poisons the communicator: the ranks
+that join late, and every later call on any rank, get SF_ERR_COMM and no
+value.  NVLS is off (NCCL_NVLS_ENABLE=0) and the
 peer kernel uses plain peer loads/stores.  Skipped with fewer than 2 GPUs.
 """
 import os
@@ -107,18 +109,42 @@ def _worker(rank, world, port, q):
         gg = [torch.empty_like(fused.red) for _ in range(world)]
         dist.all_gather(gg, fused.red)
         out["fused_same"] = all(torch.equal(gg[0], x) for x in gg)
-        del fused, ref
+        # the same step in the decoder's order (each phase waits for the one before)
+        ordered = TPStepRunner(layers, tokens=2, mode="fused", comm=comm, device=dev, ordered=True)
+        ordered.x.copy_(fused.x)
+        ordered.capture()
+        oe = []
+        for rep in range(3):
+            ordered.run()
+            torch.cuda.synchronize()
+            a, b = ordered.red.double(), ref.red.double()
+            oe.append(((a - b).abs().max() / b.abs().max()).item())
+        out["ordered_err"] = oe
+        del fused, ref, ordered
         out["dev_err_ok"] = _lib.load().sf_q4_check_device_error()
-        # bounded wait: rank 0 starts an all-reduce that rank 1 never joins
+        # bounded wait: rank 0 starts an all-reduce that no other rank joins
         dist.barrier()
         lib = _lib.load()
-        if rank == 0:
-            buf = torch.zeros(256, device=dev)
-            _lib.check(lib.sf_tp_allreduce(comm.comm, buf.data_ptr(), buf.data_ptr(), 0, None, 256, 256,
+        buf = torch.full((256,), float(rank + 1), device=dev)
+        res = torch.full((256,), -1.0, device=dev)
+
+        def allreduce():
+            _lib.check(lib.sf_tp_allreduce(comm.comm, buf.data_ptr(), res.data_ptr(), 0, None, 256, 256,
                                            torch.cuda.current_stream().cuda_stream))
             torch.cuda.synchronize()
-            out["timeout_status"] = lib.sf_q4_check_device_error()
+            return lib.sf_q4_check_device_error()
+
+        if rank == 0:
+            out["timeout_status"] = allreduce()
             out["after"] = lib.sf_q4_check_device_error()
+        dist.barrier()
+        # the others join late: they must get an error, not a value
+        if rank != 0:
+            out["late_status"] = allreduce()
+            out["late_untouched"] = bool((res == -1.0).all().item())
+        dist.barrier()
+        # and the communicator stays poisoned on every rank
+        out["again_status"] = allreduce()
         dist.barrier()
         comm.close()
     except Exception as exc:  # reported to the parent
@@ -132,7 +158,7 @@ def test_row_parallel_peer_and_nccl_match_oracle():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
-    world = min(torch.cuda.device_count(), 4)
+    world = min(torch.cuda.device_count(), 8)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -150,6 +176,12 @@ def test_row_parallel_peer_and_nccl_match_oracle():
             assert ea <= tol and eb <= tol and ec <= tol, (r["rank"], case, rep, ea, eb, ec)
     for r in res:
         assert max(r["fused_err"]) <= 1e-5, r["fused_err"]
+        assert max(r["ordered_err"]) <= 1e-5, r["ordered_err"]
         assert r["fused_same"]
     assert res[0]["timeout_status"] == 7        # SF_ERR_TIMEOUT
     assert res[0]["after"] == 0                 # the error word was read and cleared
+    for r in res[1:]:
+        assert r["late_status"] == 8, r         # SF_ERR_COMM: a late rank gets no value
+        assert r["late_untouched"], "a late rank's output was written from a stale exchange"
+    for r in res:
+        assert r["again_status"] == 8, r        # poisoned until the communicator is made again

@@ -48,6 +48,20 @@ def test_shards_reassemble_the_packed_triple(asym):
         assert np.array_equal(np.concatenate([c[2] for c in cols]), z)
 
 
+def test_column_shards_keep_heads_whole():
+    rng = np.random.default_rng(2)
+    w = rng.normal(0, 0.02, (8 * 64, 256)).astype(np.float32)   # 8 heads of 64 rows
+    p, s = Q.pack_weights_sym(w, 128)
+    for world in (1, 2, 4, 8):
+        blocks = [shard_column(p, s, None, r, world, unit=64) for r in range(world)]
+        assert all(b[0].shape[0] == 8 // world * 64 for b in blocks)
+        assert np.array_equal(np.concatenate([b[0] for b in blocks]), p)
+    with pytest.raises(ValueError, match="heads"):
+        shard_column(p, s, None, 0, 3, unit=64)       # 8 heads over 3 ranks
+    with pytest.raises(ValueError, match="heads"):
+        shard_column(p[:100], s[:100], None, 0, 2, unit=64)   # not whole heads
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

@@ -47,6 +47,10 @@ def _call(fn, p, s, z, x, n, gs, static):
     (11008, 4096, 128, False, 4),
     (4096, 11008, 128, True, 3),     # G = 86: per-lane scale copies
     (1000, 2048, 64, True, 8),       # ragged N, group 64
+    # activation blocks of 3.2 MB: the k-split the allocating entry would pick
+    # (64 ranges of partial sums, 1 MB) no longer fits beside them in the
+    # buffer, so the entry lowers the k-split until it does
+    (512, 131072, 128, False, 8),
 ])
 def test_static_scratch_matches_linear_twice(cuda, n, k, gs, asym, t):
     p, s, z, x, xh = _case(n + k + t, n, k, gs, asym, t)
