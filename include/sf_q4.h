@@ -79,8 +79,9 @@ int sf_q4_gemm_asym(const uint8_t* W, const float* scales, const float* zeros,
  * Y[T,N] = X[T,K] @ dequant(W)^T (+ bias), fp32 accumulation.
  * Replaces Q4Linear.__call__'s kernel dispatch (siliconfer/model/q4_linear.py:
  * 57-66): zeros != NULL selects the asymmetric kernel, bias (fp32 [N], may be
- * NULL) is added after the product.  T <= 8 runs the decode GEMV kernel;
- * larger T runs the prefill GEMM.  flags: bit 0 = allow programmatic
+ * NULL) is added after the product.  T <= 16 (T <= 8 at group size 32) runs
+ * the decode GEMV kernel in one pass over W; T >= 48 runs the prefill GEMM;
+ * in between, the decode kernel runs on chunks of 16 tokens.  flags: bit 0 = allow programmatic
  * dependent launch (the kernel may start streaming weights before the
  * previous kernel on `stream` has finished; x is read only after it has). */
 int sf_q4_linear(const uint8_t* W, const float* scales, const float* zeros,
@@ -99,7 +100,7 @@ int sf_q4_linear(const uint8_t* W, const float* scales, const float* zeros,
  * their Y (bounded device-side waits on per-task completion counters), which
  * is how o_proj <- attention(q, k, v) is expressed.  Tasks of one phase run
  * concurrently.  Only the first phase's X must exist before the launch.
- * All tasks must share T (1..8), the layout (zeros NULL or not) and the group
+ * All tasks must share T (1..16; 1..8 at group size 32), the layout (zeros NULL or not) and the group
  * class (group_size % 128, % 64 or % 32 == 0); group_size a power of two in
  * 32..256, K % 32 == 0, W/scales/zeros/X 16-byte aligned.  `workspace` is
  * caller-owned device memory of sf_q4_step_workspace_bytes(tasks, ntasks)
@@ -129,7 +130,7 @@ int sf_q4_step_run(void* handle, void* stream);
 int sf_q4_step_launch(void* handle, void* stream, int part);
 void sf_q4_step_destroy(void* handle);
 
-/* sf_q4_linear for T <= 8 that allocates nothing.  No counterpart in the
+/* sf_q4_linear for T <= 16 that allocates nothing.  No counterpart in the
  * reference (its kernels need no device scratch).  sf_q4_linear keeps a
  * library-owned scratch buffer per stream and grows it with cudaMalloc the
  * first time it sees a shape; this entry point is for callers that cannot let

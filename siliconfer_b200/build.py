@@ -16,7 +16,7 @@ import sys
 PKG = pathlib.Path(__file__).resolve().parent
 ROOT = PKG.parent
 LIB = PKG / "libsf_q4.so"
-SOURCES = [PKG / "csrc" / "sf_q4.cu", PKG / "csrc" / "sf_q4_gemv.cu", PKG / "csrc" / "sf_q4_gemm_tc.cu", PKG / "csrc" / "sf_q4_tile.cu",
+SOURCES = [PKG / "csrc" / "sf_q4.cu", PKG / "csrc" / "sf_q4_gemm_tc.cu", PKG / "csrc" / "sf_q4_tile.cu",
            PKG / "csrc" / "sf_q4_tp.cu", PKG / "csrc" / "sf_kv_attention.cu"]
 HEADERS = [ROOT / "include" / "sf_q4.h", PKG / "csrc" / "sf_q4_internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

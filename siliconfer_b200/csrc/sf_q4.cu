@@ -1,7 +1,7 @@
 // sf_q4.cu -- B200 (sm_100a) kernels behind the siliconfer Q4Linear C ABI.
 //
 // Kernels in this file:
-//   (the decode GEMV, q4_gemv_imma_kernel, lives in sf_q4_gemv.cu)
+//   (the decode GEMV, q4_tile_kernel, lives in sf_q4_tile.cu)
 //   q4_gemv_generic_kernel   any legal shape (even group size, K % gs == 0);
 //                            also serves the reference's "scalar" entry.
 //   q4_dequant_kernel        bit-exact fp32 dequant (+ fp16/bf16 rounding).
@@ -250,36 +250,17 @@ int run_linear(const uint8_t* W, const float* S, const float* Z, const float* bi
     int rc = run_tc_gemm(W, S, Z, bias, X, xdt, Y, ydt, N, K, T, gs, flags, stream);
     if (rc != SF_ERR_UNSUPPORTED) return rc;
   }
-  if (!force_generic && aligned && !getenv("SF_GEMV_LEGACY")) {
+  if (!force_generic && aligned) {
     // Decode GEMV as independent warp units; T above kMaxGemvT that the GEMM
     // path declined is cut into chunks of kMaxGemvT tokens (weights re-read).
     int rc = SF_OK;
-    for (int t0 = 0; t0 < T && rc == SF_OK; t0 += kMaxGemvT) {
-      const int tc = T - t0 < kMaxGemvT ? T - t0 : kMaxGemvT;
+    const int tmax = gs % 64 == 0 ? kMaxGemvT : 8;   // 9-16 tokens need group size >= 64
+    for (int t0 = 0; t0 < T && rc == SF_OK; t0 += tmax) {
+      const int tc = T - t0 < tmax ? T - t0 : tmax;
       rc = run_tile_linear(W, S, Z, bias, static_cast<const uint8_t*>(X) + (size_t)t0 * K * xe, xdt,
                            static_cast<uint8_t*>(Y) + (size_t)t0 * N * ye, ydt, N, K, tc, gs, stream);
     }
     if (rc != SF_ERR_UNSUPPORTED) return rc;
-  }
-  if (!force_generic && aligned) {
-    // Decode GEMV on the tensor cores.  Larger T that the GEMM path declined
-    // is split into launches of at most kMaxGemvT tokens (weights re-read).
-    int tmax = T < kMaxGemvT ? T : kMaxGemvT;
-    StepPlan pl;
-    while (tmax > 0 && !plan_gemv_imma(N, K, tmax, gs, Z != nullptr, pl)) tmax >>= 1;
-    for (int t0 = 0; tmax > 0 && t0 < T; t0 += tmax) {
-      const int tc = T - t0 < tmax ? T - t0 : tmax;
-      if (!plan_gemv_imma(N, K, tc, gs, Z != nullptr, pl)) break;
-      ImmaParams& q = pl.sp.single;
-      q.W = W; q.S = S; q.Z = Z; q.bias = bias;
-      q.X = static_cast<const uint8_t*>(X) + (size_t)t0 * K * xe;
-      q.Y = static_cast<uint8_t*>(Y) + (size_t)t0 * N * ye;
-      q.xdt = xdt; q.ydt = ydt;
-      cudaError_t e = launch_gemv_imma(pl, stream, pdl);
-      if (e != cudaSuccess) return cuda_fail(e, "q4_gemv_imma_kernel launch");
-      g_launches.fetch_add(1, std::memory_order_relaxed);
-      if (t0 + tc == T) return SF_OK;
-    }
   }
   // Generic path: every legal shape.
   const int threads = 256;
@@ -397,7 +378,7 @@ int sf_q4_quantize_pack(const float* W, uint8_t* packed, float* scales, float* z
 
 int sf_q4_check_device_error(void) {
   const unsigned int a = take_dev_error_gemv(), b = take_dev_error_tc(),
-                     c = take_dev_error_gemv_tc() | take_dev_error_tile() | take_dev_error_tp();
+                     c = take_dev_error_tile() | take_dev_error_tp();
   if (a == 0xffffffffu || b == 0xffffffffu || c == 0xffffffffu)
     return fail(SF_ERR_CUDA, "reading the device error word failed");
   if ((a | b | c) & kErrPoisoned)

@@ -7,9 +7,7 @@
 namespace sf {
 
 constexpr int kMaxDevices = 16;
-constexpr int kMaxStages = 6;          // + 4 scale-ring slots: 20 mbarriers below 192 B
-constexpr int kMaxGemvT = 8;           // decode GEMV handles up to 8 tokens per launch
-constexpr int kGemvMaxThreads = 512;   // keeps up to 128 registers per thread
+constexpr int kMaxGemvT = 16;          // decode GEMV handles up to 16 tokens per launch (one pass over W)
 // Bound on every device-side wait, in SM clock cycles (about 2 s at 2 GHz).
 // clock64 is read only after a failed poll; it is a cheap per-SM counter
 // (%globaltimer is far slower to read and must not sit in a poll loop).
@@ -34,49 +32,6 @@ struct GemvParams {
   uint32_t stage_bytes, s_off, z_off, stage_base;
 };
 
-// Decode GEMV on the tensor cores (sf_q4_gemv.cu).  One task = one GEMV.
-// 16-byte aligned: kernels copy descriptors with 16-byte vector loads.
-struct alignas(16) ImmaParams {
-  const uint8_t* W;
-  const float* S;
-  const float* Z;
-  const float* bias;
-  const void* X;
-  void* Y;
-  int N, K, G, gs, xdt, ydt;
-  int KS, RG, R, KC, GPS;   // K-slices, row groups, rows per block, k per chunk, groups per slice
-  int lg2gs;                // log2(group size): group sizes of this kernel are powers of two
-  int contiguous;           // 1: a stage holds whole rows (one contiguous region)
-  int wait_before;          // read X only after every CTA finished tasks [wait_from, this)
-  int wait_from;
-  uint8_t* xd;              // pre-converted activations (digit columns, then scales/sums) or null
-  uint32_t RS, CSB, TS;     // stage row stride, digit column stride, token stride
-};
-
-// Launch-wide parameters: shared-memory layout sized for the largest task.
-struct StepParams {
-  const ImmaParams* tasks;  // device array, or nullptr: use `single`
-  ImmaParams single;
-  int ntasks, ncons, nst;
-  int npp;                  // consumer groups taking alternate tasks (1 or 2)
-  unsigned int* done;       // per-task completion counters (zeroed before every launch) or null
-  uint32_t stage_bytes, stage_base, red_base, red_half, xs_base, xb_base;
-  uint32_t xs_half, xb_half, tb_base;  // per-group activation areas, ring-base table
-  uint32_t sring_base, sring_bytes;
-  int trace_id;
-  int dbg;                  // development switches (SF_GEMV_DBG): 1 no weight copies, 2 no x staging
-};
-
-struct StepPlan {
-  StepParams sp;
-  int T, LB, grid, threads;
-  bool asym, coop;
-  size_t smem;
-};
-
-// Plans one GEMV as a 1-task launch; false when the shape needs another kernel.
-bool plan_gemv_imma(int N, int K, int T, int gs, bool asym, StepPlan& pl);
-cudaError_t launch_gemv_imma(const StepPlan& pl, cudaStream_t st, bool pdl);
 
 int fail(int code, const char* fmt, ...);
 int cuda_fail(cudaError_t e, const char* what);
@@ -105,7 +60,6 @@ constexpr unsigned int kErrPoisoned = 1u << 20;
 // a slot that no longer belongs to its call.
 constexpr unsigned long long kFlagPoison = ~0ull;
 unsigned int take_dev_error_gemv();
-unsigned int take_dev_error_gemv_tc();
 unsigned int take_dev_error_tc();
 unsigned int take_dev_error_tile();
 unsigned int take_dev_error_tp();

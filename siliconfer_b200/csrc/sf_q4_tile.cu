@@ -12,10 +12,18 @@
 //    s * (sum u*x - zeff * sum x) with zeff = 8 (sym) or z (asym);
 //  * activations: per (token, group) x_fix = rint(x * 2^(22-E)), E the binary
 //    exponent of the group's max |x| (the grid step is 2^-22 of the group
-//    max), split into three signed int8 digits (x_fix = d0 + 256 d1 + 65536 d2);
-//  * mma.sync m16n8k32 u8 x s8 -> s32 sums u*d exactly; one fp32 epilogue per
-//    (row, group, token) recombines the digits, removes zeff * sum(x_fix) and
-//    applies s * 2^(E-22).
+//    max), split into three signed int8 digits (x_fix = d0 + 256 d1 + 65536 d2).
+//    (Two digits would halve the MMAs from 3 tokens on, but their 2^-15
+//    rounding misses the reference's own elementwise test tolerances.)
+//  * mma.sync m16n8k32 u8 x s8 -> s32 sums u*d exactly.  Up to 2 tokens a
+//    token's digits are adjacent B columns of one n tile (4 per token, the
+//    fourth empty), so a lane's accumulator pair holds digits (0, 1) or
+//    (2, -) of one token; each lane scales its pair and the two lanes of a
+//    token are added once, at the end of the unit.  From 3 tokens on, n tile
+//    2i holds digits (0, 1) and tile 2i + 1 digit 2 of tokens 4i .. 4i + 3, so
+//    one lane holds all three digits of its token.  One fp32 epilogue per
+//    (row, group, token[, lane]) recombines the digits, removes
+//    zeff * sum(x_fix) and applies s * 2^(E-22).
 //
 // Work decomposition:
 //  * A launch owns a list of tasks (GEMVs).  Each task is cut into units of
@@ -63,12 +71,18 @@ SF_DEFINE_ERROR_READER(take_dev_error_tile)
 
 namespace {
 
-constexpr int kD = 3;                  // stages per warp ring
+// Stages per warp ring: 3; 2 above 4 tokens, whose activation blocks are
+// as large as a stage's weights or larger (so that 8 warps per CTA, or 6
+// above 8 tokens, still fit in shared memory).
+__host__ __device__ constexpr int tile_kd(int T) { return T > 4 ? 2 : 3; }
 constexpr int kUnitRows = 32;          // rows per unit (two m16 tiles)
 // At most 12 warps per CTA (168 registers per thread); more than 4 tokens
 // doubles the accumulators, and those launches hold at most 8 warps (their
 // stages are larger) with 255 registers per thread.
 __host__ __device__ constexpr int tile_max_threads(int T) { return T > 4 ? 256 : 384; }
+// Segments whose loads, nibble splits and MMAs are interleaved (one
+// accumulator set each): two up to 8 tokens, one above (registers).
+__host__ __device__ constexpr int tile_pair(int T) { return T <= 8 ? 2 : 1; }
 
 // Bytes of one segment's activation block: [T][3 digits][4 lanes][2*LB] digit
 // bytes, then [T] x (group scale 2^(E-22), sum of x_fix) as two fp32.
@@ -85,6 +99,7 @@ struct TileLayout {
   static constexpr int SBW = LB == 4 ? 8 : 4;            // groups in one stage's scale box
   static constexpr int SBYTES = 32 * SBW * 4;            // [32 rows][SBW] fp32
   static constexpr int XSTAGE = (SPS * XB + 127) & ~127;
+  static constexpr int kD = tile_kd(T);
   // per-warp area: [mbarriers 64 B][zeros 64 B][kD x activations][kD x scales][kD x zeros]
   static constexpr int XOFF = 128;
   static constexpr int SOFF = XOFF + kD * XSTAGE;
@@ -381,7 +396,8 @@ __device__ __forceinline__ void convert_chunk(const TileTask* p, int c, int lane
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] = 0.f;
   }
-  uint2 dig[3];
+  constexpr int ND = 3;
+  uint2 dig[ND];
   float gsc;
   int s;
   digits8(v, lpg, dig, gsc, s);
@@ -391,15 +407,15 @@ __device__ __forceinline__ void convert_chunk(const TileTask* p, int c, int lane
   const int tt = within / (2 * LB), j = (within - tt * 2 * LB) >> 3;
   uint8_t* blk = p->xd + (size_t)seg * XB;
 #pragma unroll
-  for (int dg = 0; dg < 3; ++dg)
-    *reinterpret_cast<uint2*>(blk + ((tok * 3 + dg) * 4 + tt) * 2 * LB + j * 8) = dig[dg];
+  for (int dg = 0; dg < ND; ++dg)
+    *reinterpret_cast<uint2*>(blk + ((tok * ND + dg) * 4 + tt) * 2 * LB + j * 8) = dig[dg];
   if ((lane & (lpg - 1)) == 0) {
     // every segment of the group carries the group's scale and sum
     const int gs = 1 << lg2gs;
     const int s0 = ((k0 >> lg2gs) << lg2gs) / SEGK;
     const float2 gv = make_float2(gsc, (float)s);
     for (int sg = s0; sg < s0 + gs / SEGK; ++sg)
-      *reinterpret_cast<float2*>(p->xd + (size_t)sg * XB + T * 24 * LB + tok * 8) = gv;
+      *reinterpret_cast<float2*>(p->xd + (size_t)sg * XB + T * 8 * ND * LB + tok * 8) = gv;
   }
 }
 
@@ -457,11 +473,12 @@ template <int T, bool ASYM, int LB>
 __global__ void __launch_bounds__(tile_max_threads(T), 1)
     q4_tile_kernel(const __grid_constant__ TileLaunch L) {
   using Ly = TileLayout<T, ASYM, LB>;
-  // n tiles: T <= 2 packs all 3T digit columns into one tile; otherwise tile
-  // pair (2 tg, 2 tg + 1) holds digits (0, 1) and digit 2 of tokens 4 tg .. 4 tg + 3
+  // CMP (T <= 2): one n tile, token t in columns 4t .. 4t + 3 (digits 0-2, empty);
+  // else NG groups of 4 tokens, n tiles (2i, 2i + 1) = digits (0, 1) and 2 of group i
   constexpr bool CMP = T <= 2;
-  constexpr int NTG = (T + 3) / 4, NT = CMP ? 1 : 2 * NTG, WPL = LB / 4, SEGK = 8 * LB, SPS = Ly::SPS;
-  constexpr int GOFF = T * 24 * LB;              // group scales / sums inside a segment's block
+  constexpr int ND = 3, NG = CMP ? 1 : (T + 3) / 4, NT = CMP ? 1 : 2 * NG;
+  constexpr int WPL = LB / 4, SEGK = 8 * LB, SPS = Ly::SPS, PS = tile_pair(T);
+  constexpr int GOFF = T * 8 * ND * LB;          // group scales / sums inside a segment's block
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -471,6 +488,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     if (threadIdx.x == 0) atomicOr(&g_dev_error, 0x800u);
     return;
   }
+  constexpr int kD = Ly::kD;
   const uint32_t astage0 = sbase + (uint32_t)warp * kD * Ly::ASTAGE;
   const uint32_t wb = sbase + (uint32_t)wpc * kD * Ly::ASTAGE + (uint32_t)warp * Ly::MISC;
   const uint32_t bar0 = wb, zblk = wb + 64, xstage0 = wb + Ly::XOFF, sstage0 = wb + Ly::SOFF,
@@ -483,25 +501,27 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
   __syncwarp();
 
   // B fragment sources: column g of tile nt is (token, digit) or absent.
-  // Accumulator columns 2t, 2t+1 of a lane are then digits 0 and 1 of token
-  // t (of its group of four); digit 2 sits in the odd tile at column 2t or,
-  // in the packed layout (T <= 2), at column 2T + t of another lane.
+  // Accumulator columns 2t, 2t+1 of a lane are then (CMP) digits (0, 1) or
+  // (2, -) of token t >> 1, else digits (0, 1) of token 4i + t in tile 2i and
+  // digit 2 of the same token in tile 2i + 1.
   int bslot[NT];
   bool bval[NT];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     int tok, dg;
     if (CMP) {
-      tok = g < 2 * T ? (g >> 1) : g - 2 * T;
-      dg = g < 2 * T ? (g & 1) : 2;
-      bval[nt] = g < 3 * T;
+      tok = g >> 2;
+      dg = g & 3;
     } else {
       tok = (nt >> 1) * 4 + (g >> 1);
-      dg = (nt & 1) ? ((g & 1) ? -1 : 2) : (g & 1);
-      bval[nt] = tok < T && dg >= 0;
+      dg = (nt & 1) ? ((g & 1) ? 3 : 2) : (g & 1);
     }
-    bslot[nt] = bval[nt] ? ((tok * 3 + dg) * 4 + t) * 2 * LB : 0;
+    bval[nt] = tok < T && dg < ND;
+    bslot[nt] = bval[nt] ? ((tok * ND + dg) * 4 + t) * 2 * LB : 0;
   }
+  const int ltok = CMP ? (t >> 1) : t;            // this lane's token inside a group
+  const bool dlead = CMP ? (t & 1) == 0 : true;   // holds digits (0, 1): carries zeff * sum(x)
+  const float lmul = dlead ? 1.f : 65536.f;       // weight of the lane's digit pair (CMP)
   // rows of this lane inside a unit and their byte offsets in a swizzled stage
   int rloc[4];
   uint32_t aoff[4][SPS];
@@ -699,12 +719,12 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     for (int j = 0; j < kD - 1; ++j)
       if (j < nstage) issue(j);
 
-    float acc[2][NTG][2];
+    float acc[2][NG][2];
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-      for (int tg = 0; tg < NTG; ++tg) acc[mt][tg][0] = acc[mt][tg][1] = 0.f;
-    int C[2][2][NT][4];   // [segment of the pair][m tile][n tile][fragment]
+      for (int tg = 0; tg < NG; ++tg) acc[mt][tg][0] = acc[mt][tg][1] = 0.f;
+    int C[PS][2][NT][4];   // [segment of the pair][m tile][n tile][fragment]
 
     // epilogue of the group that ends with segment s: recombine the digits,
     // remove zeff * sum(x), scale.  Lanes whose token does not exist compute
@@ -716,30 +736,32 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
         sc_i = 0;
       }
       const uint32_t soff = (uint32_t)sc_i * 4;
+      float sc[2][2], zp[2][2];
 #pragma unroll
-      for (int tg = 0; tg < NTG; ++tg) {
-        const uint2 xv = lds64(xs0 + GOFF + min(tg * 4 + t, T - 1) * 8);
-        const float gsc = __uint_as_float(xv.x), xsum = __uint_as_float(xv.y);
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = rloc[2 * mt + h];
+          sc[mt][h] = __uint_as_float(lds32(sst + r * (Ly::SBW * 4) + soff));
+          zp[mt][h] = ASYM ? __uint_as_float(lds32(zst + r * (Ly::SBW * 4) + soff)) : 8.f;
+        }
+#pragma unroll
+      for (int tg = 0; tg < NG; ++tg) {
+        const uint2 xv = lds64(xs0 + GOFF + min(tg * 4 + ltok, T - 1) * 8);
+        const float gsc = __uint_as_float(xv.x), xsum = dlead ? __uint_as_float(xv.y) : 0.f;
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int r = rloc[2 * mt + h];
-            const float sc = __uint_as_float(lds32(sst + r * (Ly::SBW * 4) + soff));
-            const float zp = ASYM ? __uint_as_float(lds32(zst + r * (Ly::SBW * 4) + soff)) : 8.f;
-            const int i01 = Cs[mt][CMP ? 0 : 2 * tg][2 * h] + 256 * Cs[mt][CMP ? 0 : 2 * tg][2 * h + 1];
-            int c2;
+            float v;
             if (CMP) {
-              // digit 2 of token t is column 2T + t: lane T of the quad, element t
-              const int va = __shfl_sync(0xffffffffu, Cs[mt][0][2 * h], (lane & ~3) | T);
-              const int vb = T == 2 ? __shfl_sync(0xffffffffu, Cs[mt][0][2 * h + 1], (lane & ~3) | T) : va;
-              c2 = t == 1 ? vb : va;
+              v = lmul * (float)(Cs[mt][0][2 * h] + 256 * Cs[mt][0][2 * h + 1]);
             } else {
-              c2 = Cs[mt][2 * tg + 1][2 * h];
+              const int i01 = Cs[mt][2 * tg][2 * h] + 256 * Cs[mt][2 * tg][2 * h + 1];
+              v = fmaf(65536.f, (float)Cs[mt][2 * tg + 1][2 * h], (float)i01);
             }
-            float f = fmaf(65536.f, (float)c2, (float)i01);
-            f = fmaf(-zp, xsum, f);
-            acc[mt][tg][h] = fmaf(f, sc * gsc, acc[mt][tg][h]);
+            const float f = fmaf(-zp[mt][h], xsum, v);
+            acc[mt][tg][h] = fmaf(f, sc[mt][h] * gsc, acc[mt][tg][h]);
           }
       }
     };
@@ -754,17 +776,18 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       }
       const int fgj = (kb + j * 256) >> lg2gs;
       const int sx = stma ? (fgj & ~(Ly::SBW - 1)) : fgj;
-      // The stage's segments are taken in pairs with one accumulator set each,
-      // so that the two halves' loads, nibble splits and MMAs interleave.
+      // The stage's segments are taken in pairs (PS = 2) with one accumulator
+      // set each, so that the two halves' loads, nibble splits and MMAs
+      // interleave; one at a time (PS = 1) above 8 tokens.
 #pragma unroll
-      for (int pr = 0; pr < SPS; pr += 2) {
+      for (int pr = 0; pr < SPS; pr += PS) {
         const int s0 = j * SPS + pr;
         if (L.dbg == 2 || s0 >= nseg) break;
-        const bool has1 = s0 + 1 < nseg;
-        uint32_t w[2][4][WPL];
-        uint32_t bq[2][NT][2 * WPL];
+        const bool has1 = PS == 2 && s0 + 1 < nseg;
+        uint32_t w[PS][4][WPL];
+        uint32_t bq[PS][NT][2 * WPL];
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
+        for (int h2 = 0; h2 < PS; ++h2) {
           const uint32_t xs0 = xst + (pr + h2) * Ly::XB;
 #pragma unroll
           for (int i = 0; i < 4; ++i) lds_n<LB>(ast + aoff[i][pr + h2], w[h2][i]);
@@ -779,7 +802,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
 #pragma unroll
         for (int q = 0; q < WPL; ++q)
 #pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2)
+          for (int h2 = 0; h2 < PS; ++h2)
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
               const uint32_t a0 = nib_lo<ASYM>(w[h2][2 * mt][q]), a2 = nib_hi<ASYM>(w[h2][2 * mt][q]);
@@ -791,19 +814,23 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
                 else imma(C[h2][mt][nt], a0, a1, a2, a3, bq[h2][nt][2 * q], bq[h2][nt][2 * q + 1]);
               }
             }
-        // group ends inside the pair: one per segment when a group is one
-        // segment long, else at most one (the odd segment) with the sets summed
-        if (spg_mask == 0) {
-          epilogue(C[0], s0, xst + pr * Ly::XB, sst, zst, sx);
-          if (has1) epilogue(C[1], s0 + 1, xst + (pr + 1) * Ly::XB, sst, zst, sx);
-        } else if (((s0 + 1) & spg_mask) == spg_mask) {
+        if constexpr (PS == 1) {
+          if ((s0 & spg_mask) == spg_mask) epilogue(C[0], s0, xst + pr * Ly::XB, sst, zst, sx);
+        } else {
+          // group ends inside the pair: one per segment when a group is one
+          // segment long, else at most one (the odd segment) with the sets summed
+          if (spg_mask == 0) {
+            epilogue(C[0], s0, xst + pr * Ly::XB, sst, zst, sx);
+            if (has1) epilogue(C[PS - 1], s0 + 1, xst + (pr + 1) * Ly::XB, sst, zst, sx);
+          } else if (((s0 + 1) & spg_mask) == spg_mask) {
 #pragma unroll
-          for (int mt = 0; mt < 2; ++mt)
+            for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
+              for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-              for (int e = 0; e < 4; ++e) C[0][mt][nt][e] += C[1][mt][nt][e];
-          epilogue(C[0], s0 + 1, xst + (pr + 1) * Ly::XB, sst, zst, sx);
+                for (int e = 0; e < 4; ++e) C[0][mt][nt][e] += C[PS - 1][mt][nt][e];
+            epilogue(C[0], s0 + 1, xst + (pr + 1) * Ly::XB, sst, zst, sx);
+          }
         }
       }
       __syncwarp();
@@ -814,11 +841,20 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     if (tr && lane == 0) tr[3] = globaltimer_ns();
 
     // ---- results ---------------------------------------------------------------
+    if constexpr (CMP) {
+      // a token's two lanes (digits 0-1, digit 2) hold halves of its sums
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int tg = 0; tg < NG; ++tg)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) acc[mt][tg][h] += __shfl_xor_sync(0xffffffffu, acc[mt][tg][h], 1);
+    }
     if (ksplit == 1) {
 #pragma unroll
-      for (int tg = 0; tg < NTG; ++tg) {
-        const int tok = tg * 4 + t;
-        if (tok < T) {
+      for (int tg = 0; tg < NG; ++tg) {
+        const int tok = tg * 4 + ltok;
+        if (dlead && tok < T) {
 #pragma unroll
           for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
@@ -836,9 +872,9 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       tile_written(L, p, lane);
     } else {
 #pragma unroll
-      for (int tg = 0; tg < NTG; ++tg) {
-        const int tok = tg * 4 + t;
-        if (tok < T) {
+      for (int tg = 0; tg < NG; ++tg) {
+        const int tok = tg * 4 + ltok;
+        if (dlead && tok < T) {
 #pragma unroll
           for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
@@ -909,7 +945,7 @@ int lb_for(int gs) { return (gs % 128 == 0) ? 16 : (gs % 64 == 0 ? 8 : 4); }
 
 // Shared bytes per warp: TileLayout<T, ASYM, LB>::WARP.
 int warp_bytes(int T, bool asym, int LB) {
-  const int sps = 128 / (4 * LB), sbw = LB == 4 ? 8 : 4;
+  const int sps = 128 / (4 * LB), sbw = LB == 4 ? 8 : 4, kD = tile_kd(T);
   const int xstage = (sps * xblock_bytes(T, LB) + 127) & ~127;
   return kD * 32 * 128 + 128 + kD * xstage + kD * 32 * sbw * 4 * (asym ? 2 : 1);
 }
@@ -932,6 +968,7 @@ bool shape_ok(int N, int K, int gs) {
 bool make_config(int T, bool asym, int gs, TileConfig& c) {
   const DeviceInfo& di = device_info();
   c.T = T; c.asym = asym; c.LB = lb_for(gs);
+  if (T < 1 || T > kMaxGemvT || (T > 8 && c.LB == 4)) return false;   // 9-16 tokens need group size >= 64
   const size_t per_warp = (size_t)warp_bytes(T, asym, c.LB);
   size_t cap = (size_t)env_int("SF_TILE_SMEM_KB", 227) * 1024;
   if (cap > (size_t)di.smem_optin) cap = (size_t)di.smem_optin;
@@ -941,7 +978,8 @@ bool make_config(int T, bool asym, int gs, TileConfig& c) {
   if (wpc > tile_max_threads(T) / 32) wpc = tile_max_threads(T) / 32;
   // whole multiples of the 4 schedulers: an odd warp would carry a 3-warp
   // scheduler and, since every warp gets the same share of units, slow all
-  if (wpc > 4) wpc &= ~3;
+  // (above 8 tokens shared memory allows only 5-6 warps: all of them run)
+  if (wpc > 4 && T <= 8) wpc &= ~3;
   if (wpc < 1) return false;
   c.wpc = wpc;
   c.smem = per_warp * wpc;
@@ -1050,8 +1088,23 @@ cudaError_t launch_tile_lb(const TileConfig& c, const TileLaunch& L, bool coop, 
     case 5: return launch_tile_t<5, ASYM, LB>(c, L, coop, st);
     case 6: return launch_tile_t<6, ASYM, LB>(c, L, coop, st);
     case 7: return launch_tile_t<7, ASYM, LB>(c, L, coop, st);
-    default: return launch_tile_t<8, ASYM, LB>(c, L, coop, st);
+    case 8: return launch_tile_t<8, ASYM, LB>(c, L, coop, st);
+    default: break;
   }
+  if constexpr (LB != 4) {   // 9-16 tokens: group sizes of 64 and more
+    switch (c.T) {
+      case 9: return launch_tile_t<9, ASYM, LB>(c, L, coop, st);
+      case 10: return launch_tile_t<10, ASYM, LB>(c, L, coop, st);
+      case 11: return launch_tile_t<11, ASYM, LB>(c, L, coop, st);
+      case 12: return launch_tile_t<12, ASYM, LB>(c, L, coop, st);
+      case 13: return launch_tile_t<13, ASYM, LB>(c, L, coop, st);
+      case 14: return launch_tile_t<14, ASYM, LB>(c, L, coop, st);
+      case 15: return launch_tile_t<15, ASYM, LB>(c, L, coop, st);
+      case 16: return launch_tile_t<16, ASYM, LB>(c, L, coop, st);
+      default: break;
+    }
+  }
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_tile(const TileConfig& c, const TileLaunch& L, bool coop, cudaStream_t st) {
@@ -1076,7 +1129,23 @@ cudaError_t launch_xblocks_lb(int T, int ntasks, const TileLaunch& L, cudaStream
     case 5: q4_xblocks_kernel<5, LB><<<grid, 256, 0, st>>>(L); break;
     case 6: q4_xblocks_kernel<6, LB><<<grid, 256, 0, st>>>(L); break;
     case 7: q4_xblocks_kernel<7, LB><<<grid, 256, 0, st>>>(L); break;
-    default: q4_xblocks_kernel<8, LB><<<grid, 256, 0, st>>>(L); break;
+    case 8: q4_xblocks_kernel<8, LB><<<grid, 256, 0, st>>>(L); break;
+    default:
+      if constexpr (LB != 4) {
+        switch (T) {
+          case 9: q4_xblocks_kernel<9, LB><<<grid, 256, 0, st>>>(L); break;
+          case 10: q4_xblocks_kernel<10, LB><<<grid, 256, 0, st>>>(L); break;
+          case 11: q4_xblocks_kernel<11, LB><<<grid, 256, 0, st>>>(L); break;
+          case 12: q4_xblocks_kernel<12, LB><<<grid, 256, 0, st>>>(L); break;
+          case 13: q4_xblocks_kernel<13, LB><<<grid, 256, 0, st>>>(L); break;
+          case 14: q4_xblocks_kernel<14, LB><<<grid, 256, 0, st>>>(L); break;
+          case 15: q4_xblocks_kernel<15, LB><<<grid, 256, 0, st>>>(L); break;
+          case 16: q4_xblocks_kernel<16, LB><<<grid, 256, 0, st>>>(L); break;
+          default: return cudaErrorInvalidValue;
+        }
+      } else {
+        return cudaErrorInvalidValue;
+      }
   }
   return cudaGetLastError();
 }

@@ -9,8 +9,6 @@ the reference's packers bit for bit:
 * ``quantize_asym`` -- siliconfer/quant/primitives.py:82-114
 * ``pack_weights_sym`` / ``pack_weights_asym`` --
   siliconfer/kernels/neon/__init__.py:42-81 (low nibble = even column)
-* ``hqq_quantize_weight`` -- siliconfer/quant/hqq.py:84-164, used here only to
-  produce asymmetric synthetic weights with the reference's grid choice.
 
 ``pack_weights_*_device`` run the same RTN arithmetic on the GPU
 (``sf_q4_quantize_pack``), for weights too large to quantize on the host.
@@ -88,53 +86,3 @@ def pack_weights_device(W, group_size: int = 128, sym: bool = True):
             None if zeros is None else zeros.data_ptr(), n, k, group_size,
             torch.cuda.current_stream(W.device).cuda_stream))
     return (packed, scales) if sym else (packed, scales, zeros)
-
-
-# ---------------------------------------------------------------------------
-# HQQ grid search (asymmetric, calibration-free), for synthetic asym weights.
-# ---------------------------------------------------------------------------
-_EPS = 1e-8
-DEFAULT_K_GRID = (150.0, 100.0, 80.0, None)
-
-
-def hqq_quantize_weight(W: np.ndarray, group_size: int = 128, p: float = 0.7,
-                        k_grid=DEFAULT_K_GRID, bits: int = 4) -> np.ndarray:
-    """Fake-quantized fp32 weights on the HQQ-chosen asymmetric grid.
-
-    For each group, candidate clip ranges [median - k*1.4826*MAD,
-    median + k*1.4826*MAD] (k = None: the full min-max range) are quantized in
-    float64 and the one with the lowest mean (|w - recon| + 1e-8)^p wins
-    (first best kept on ties).  Restates siliconfer/quant/hqq.py:84-164.
-    """
-    qmax = float(2 ** bits - 1)
-    n, k = W.shape
-    if k < group_size:
-        q, s, z = quantize_asym(np.asarray(W, np.float32), k)   # one group per row
-        return ((q.astype(np.float32) - z) * s).astype(np.float32)
-    g = W.reshape(n, k // group_size, group_size).astype(np.float64)
-    lo_full = g.min(axis=-1, keepdims=True)
-    hi_full = g.max(axis=-1, keepdims=True)
-    med = np.median(g, axis=-1, keepdims=True)
-    mad = np.median(np.abs(g - med), axis=-1, keepdims=True)
-    rstd = np.where(mad == 0.0, _EPS, mad) * 1.4826
-    best = None
-    for kk in k_grid:
-        if kk is None:
-            lo, hi = lo_full, hi_full
-        else:
-            lo = np.maximum(lo_full, med - kk * rstd)
-            hi = np.minimum(hi_full, med + kk * rstd)
-        scale = (hi - lo) / qmax
-        scale = np.where(scale <= 0, 1.0, scale)
-        zero = np.clip(np.round(-lo / scale), 0, qmax)
-        q = np.clip(np.round(g / scale + zero), 0, qmax)
-        loss = ((np.abs(g - scale * (q - zero)) + _EPS) ** p).mean(axis=-1, keepdims=True)
-        if best is None:
-            best = [loss, scale, zero]
-        else:
-            better = loss < best[0]
-            best = [np.where(better, loss, best[0]), np.where(better, scale, best[1]),
-                    np.where(better, zero, best[2])]
-    _, scale, zero = best
-    q = np.clip(np.round(g / scale + zero), 0, qmax)
-    return (scale * (q - zero)).reshape(n, k).astype(np.float32)

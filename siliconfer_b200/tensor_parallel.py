@@ -274,7 +274,7 @@ class TPStepRunner:
         written its output, as a decoder would."""
         from .kernels.cuda import _dtype_code
         torch = self.torch
-        tasks, roles = [], []
+        tasks, roles, pending = [], [], []
         xs = self.x.element_size()
         for li, lay in enumerate(self.layers):
             for i, m in enumerate(lay):
@@ -300,9 +300,22 @@ class TPStepRunner:
                 tasks.append(_lib.Q4Task(*base, None, xp, None, m.out_features, m.in_features, self.tokens,
                                          m.group_size, _dtype_code(self.x), _lib.SF_F32, wait))
                 roles.append(1)
-                tasks.append(_lib.Q4Task(*base, None, xp, out.data_ptr(), m.out_features, m.in_features,
-                                         self.tokens, m.group_size, _dtype_code(self.x), _lib.SF_F32, 0))
-                roles.append(2 + src)
+                red = (_lib.Q4Task(*base, None, xp, out.data_ptr(), m.out_features, m.in_features,
+                                   self.tokens, m.group_size, _dtype_code(self.x), _lib.SF_F32, 0), 2 + src)
+                if self.ordered:
+                    # the next phase reads this output: reduce right away
+                    tasks.append(red[0])
+                    roles.append(red[1])
+                else:
+                    # nothing waits for it: reduce after the next row-parallel shard, so that
+                    # the warps reaching its units find every rank's tiles long pushed
+                    for t_, r_ in pending:
+                        tasks.append(t_)
+                        roles.append(r_)
+                    pending = [red]
+        for t_, r_ in pending:
+            tasks.append(t_)
+            roles.append(r_)
         n = len(tasks)
         arr = (_lib.Q4Task * n)(*tasks)
         rl = (_lib.ctypes.c_int * n)(*roles)

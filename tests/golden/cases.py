@@ -40,6 +40,16 @@ def layer_seed(config: int, layer: int, proj: str) -> int:
     return config * 100_000 + layer * 100 + PROJ_ORDER.index(proj)
 
 
+QWEN_LAYERS = 24   # config 2: the full Qwen2.5-0.5B decode step
+
+
+def bf16_round(a: np.ndarray) -> np.ndarray:
+    """fp32 values rounded to the nearest bfloat16 (ties to even), as fp32."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    return r.view(np.float32)
+
+
 # One injected outlier of 60 sigma in a down_proj group (config 2).
 OUTLIER = {"row": 17, "col": 1234, "sigma": 60.0}
 

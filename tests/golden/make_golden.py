@@ -41,7 +41,9 @@ def _install_mlx_standin() -> None:
 
 
 def main() -> None:
-    ref = os.environ.get("SILICONFER_REF", "/root/reference")
+    ref = os.environ.get("SILICONFER_REF")
+    if not ref:
+        sys.exit("set SILICONFER_REF to the root of the siliconfer reference tree")
     _install_mlx_standin()
     sys.path.insert(0, ref)
     from siliconfer.kernels import neon as K
@@ -133,6 +135,36 @@ def main() -> None:
     meta["hashes"]["c4/q/zeros"] = C.sha(z)
     x = C.acts(C.layer_seed(4, 0, "q") + 7, 4, 4096)
     out["c4/q/y"] = K.gemm_asym(p, s, z, x, 128)
+
+    # --- config 3 at batch 16 (the sweep's largest batch): gate and down ------
+    for proj in ("gate", "down"):
+        n, k = C.LLAMA7B[proj]
+        w = C.weights(C.layer_seed(3, 0, proj), n, k)
+        p, s = K.pack_weights_sym(w, 128)
+        x = C.acts(C.layer_seed(3, 0, proj) + 7, 16, k)
+        out[f"c3b16/{proj}/y"] = K.gemm_sym(p, s, x, 128)
+
+    # --- config 4 on the tensor-core sizes: bf16 activations ----------------------
+    # T = 64 on (K, N) = (4096, 4096): every output;  T = 512 on (11008, 4096):
+    # every 16th token (the kernel computes all 512)
+    for tag, proj, t, keep in (("c4t64", "q", 64, 1), ("c4t512", "down", 512, 16)):
+        n, k = C.LLAMA7B[proj]
+        w = C.weights(C.layer_seed(4, 0, proj), n, k)
+        p, s, z = K.pack_weights_asym(w, 128)
+        meta["hashes"][f"{tag}/packed"] = C.sha(p)
+        x = C.bf16_round(C.acts(C.layer_seed(4, 0, proj) + 11, t, k))
+        out[f"{tag}/y"] = K.gemm_asym(p, s, z, x, 128)[::keep].astype(np.float32)
+
+    # --- config 2 as a 24-layer step (one input per projection, batch 1) ---------
+    # layer 0 is the HQQ layer above (60 sigma outlier); layers 1-23 are quantized
+    # with the reference's asymmetric RTN packer (the same triple format)
+    for layer in range(1, C.QWEN_LAYERS):
+        for proj, (n, k) in C.QWEN05B.items():
+            w = C.qwen_asym_weights(layer, proj)
+            p, s, z = K.pack_weights_asym(w, 128)
+            meta["hashes"][f"c2L/{layer}/{proj}/packed"] = C.sha(p)
+            x = C.acts(C.layer_seed(2, layer, proj) + 7, 1, k)
+            out[f"c2L/{layer}/{proj}/y"] = K.gemm_asym(p, s, z, x, 128)
 
     np.savez_compressed(HERE / "golden.npz", **out)
     (HERE / "golden_meta.json").write_text(json.dumps(meta, indent=1, sort_keys=True))

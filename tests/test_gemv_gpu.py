@@ -106,7 +106,7 @@ def test_config1_qwen_layer_sym(cuda, golden, proj):
 @pytest.mark.parametrize("proj", list(C.QWEN05B))
 def test_config2_qwen_layer_hqq_asym(cuda, golden, proj):
     g, _ = golden
-    p, s, z = Q.pack_weights_asym(Q.hqq_quantize_weight(C.qwen_asym_weights(0, proj), 128), 128)
+    p, s, z = Q.pack_weights_asym(O.hqq_quantize_weight(C.qwen_asym_weights(0, proj), 128), 128)
     x = C.acts(C.layer_seed(2, 0, proj) + 7, 1, p.shape[1] * 2)
     y = run_linear(p, s, z, x, 128).cpu().numpy()
     assert O.normwise_rel_err(y, g[f"c2/{proj}/y"]) <= TOL
@@ -176,7 +176,7 @@ SHAPES = [
 
 @pytest.mark.parametrize("asym", [False, True])
 @pytest.mark.parametrize("n,k,gs", SHAPES)
-@pytest.mark.parametrize("t", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("t", [1, 2, 3, 4, 8, 9, 16])
 def test_gemv_shapes(cuda, asym, n, k, gs, t):
     p, s, z, x = rand_case(n + k + t, n, k, gs, asym, t=t, shift=0.005 if asym else 0.0)
     y = run_linear(p, s, z, x, gs).cpu().numpy()
@@ -274,3 +274,17 @@ def test_capture_without_warmup_fails_loudly(cuda):
     g2.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("proj", ["gate", "down"])
+def test_config3_7b_batch16_one_pass(cuda, golden, proj):
+    """Config 3's largest batch: 16 tokens in ONE launch of the decode kernel
+    (each weight read once), against the reference's gemm_sym output."""
+    g, _ = golden
+    n, k = C.LLAMA7B[proj]
+    p, s = Q.pack_weights_device(dev(C.weights(C.layer_seed(3, 0, proj), n, k)), 128)
+    X = C.acts(C.layer_seed(3, 0, proj) + 7, 16, k)
+    n0 = _lib.launch_count()
+    y = K.linear(p, s, None, dev(X), 128).cpu().numpy()
+    assert _lib.launch_count() - n0 == 2          # activation pre-pass + one GEMV launch
+    assert O.normwise_rel_err(y, g[f"c3b16/{proj}/y"]) <= TOL

