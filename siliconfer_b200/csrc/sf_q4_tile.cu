@@ -161,8 +161,6 @@ struct TileLaunch {
   long long total;        // units in the launch
   int ntasks;
   int prefetch;           // pull a waiting unit's weights into L2 before the wait
-  int dbg;                // development: 2 = copies only, 3 = arithmetic only (wrong results)
-  unsigned long long* trace;   // development: per unit [start, dependency met, inputs ready, end] ns
   unsigned long long* epoch;   // launch counter (tensor-parallel exchange), advanced by the pre-pass, or null
   unsigned long long* poison;  // the communicator's sticky poison word (tensor-parallel steps), or null
 };
@@ -178,9 +176,11 @@ __device__ __forceinline__ void bar_init(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void bar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-// Arrives on `bar` once every cp.async this thread issued so far has landed.
+// Arrives on `bar` once every cp.async this thread issued so far has landed;
+// the barrier's expected count is raised by one first, so the arrival does
+// not count against the count it was initialised with.
 __device__ __forceinline__ void bar_arrive_cpasync(uint32_t bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ bool bar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -494,7 +494,9 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
   const uint32_t bar0 = wb, zblk = wb + 64, xstage0 = wb + Ly::XOFF, sstage0 = wb + Ly::SOFF,
                  zstage0 = wb + Ly::ZOFF;
 
-  if (lane < kD) bar_init(bar0 + lane * 8, 33);   // lane 0's expect_tx + 32 cp.async arrivals
+  // one arrival per stage: lane 0's expect_tx.  Per-lane scale copies add
+  // their own (cp.async.mbarrier.arrive raises the expected count first).
+  if (lane < kD) bar_init(bar0 + lane * 8, 1);
   if (lane < 16) asm volatile("st.shared.u32 [%0], %1;" ::"r"(zblk + lane * 4), "r"(0u) : "memory");
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -550,7 +552,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     }
     return;
   }
-  uint32_t gseg = 0;   // segments this warp has consumed (ring position and phase)
+  uint32_t cslot = 0, cpar = 0;   // this warp's ring: next slot to consume and its phase parity
   int ti = 0;
   bool ok = true;
 
@@ -569,8 +571,6 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     const int lg2spg = lg2gs - (31 - __clz(SEGK));   // segments per group = 1 << lg2spg
     const int spg_mask = (1 << lg2spg) - 1;
 
-    unsigned long long* tr = L.trace ? L.trace + 4 * u : nullptr;
-    if (tr && lane == 0) tr[0] = globaltimer_ns();
     // ---- dependencies and activation blocks --------------------------------
     if (p->phase > 0) {
       const int ph = p->phase;
@@ -589,7 +589,6 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       if (lane == 0) okw = spin_geq(fl, (unsigned)ph, 0x200u);   // previous phase written
       ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
       if (!ok) break;
-      if (tr && lane == 0) tr[1] = globaltimer_ns();
       // The first units of the phase convert its inputs: unit i takes chunks
       // i, i + CS, ... over all tasks of the phase.  Every warp has at most
       // one such unit per phase and reaches it before any other unit of the
@@ -667,17 +666,19 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       tile_written(L, p, lane);
       continue;
     }
-    if (tr && lane == 0) tr[2] = globaltimer_ns();
     // ---- operand streaming ---------------------------------------------------
     // Stage j holds k [kb + 256 j, kb + 256 j + 256): the weight tile, the
     // activation blocks of its segments and the scale box of its groups.
+    // Ring position: `cslot` / `cpar` are the slot and phase parity of the
+    // next stage to consume, `islot` the slot of the next stage to issue.
     const int nstage = (nseg + SPS - 1) / SPS;
     const uint8_t* xsrc = p->xd + (size_t)(kb / SEGK) * Ly::XB;
     const float* Sb = p->S;
     const float* Zb = p->Z;
+    uint32_t islot = cslot;
     auto issue = [&](int j) {
-      if (L.dbg == 3) return;
-      const uint32_t slot = (gseg + j) % kD;
+      const uint32_t slot = islot;
+      islot = islot + 1 == (uint32_t)kD ? 0u : islot + 1;
       const uint32_t bar = bar0 + slot * 8;
       const int nsub = min(SPS, nseg - j * SPS);
       const int fg = (kb + j * 256) >> lg2gs;                   // first group of the stage
@@ -685,16 +686,6 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       // cut in whole boxes, so the stage's groups stay inside); per-lane
       // copies start at the stage's first group
       const int sx = stma ? (fg & ~(Ly::SBW - 1)) : fg;
-      if (lane == 0) {
-        const uint32_t sbytes = stma ? (uint32_t)Ly::SBYTES * (ASYM ? 2 : 1) : 0u;
-        bar_expect_tx(bar, (uint32_t)Ly::ASTAGE + nsub * Ly::XB + sbytes);
-        tma_2d(astage0 + slot * Ly::ASTAGE, &p->tmW, (kb >> 1) + j * 128, r0, bar);
-        bulk_copy(xstage0 + slot * Ly::XSTAGE, xsrc + (size_t)j * SPS * Ly::XB, nsub * Ly::XB, bar);
-        if (stma) {
-          tma_2d(sstage0 + slot * Ly::SBYTES, &p->tmS, sx, r0, bar);
-          if (ASYM) tma_2d(zstage0 + slot * Ly::SBYTES, &p->tmZ, sx, r0, bar);
-        }
-      }
       if (!stma) {
 #pragma unroll
         for (int c = t; c < Ly::SBW; c += 4) {
@@ -709,8 +700,21 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
             }
           }
         }
+        // each lane's copies count as one more arrival on the stage's barrier;
+        // they are registered before lane 0's arrival below can end the phase
+        bar_arrive_cpasync(bar);
+        __syncwarp();
       }
-      bar_arrive_cpasync(bar);
+      if (lane == 0) {
+        const uint32_t sbytes = stma ? (uint32_t)Ly::SBYTES * (ASYM ? 2 : 1) : 0u;
+        bar_expect_tx(bar, (uint32_t)Ly::ASTAGE + nsub * Ly::XB + sbytes);
+        tma_2d(astage0 + slot * Ly::ASTAGE, &p->tmW, (kb >> 1) + j * 128, r0, bar);
+        bulk_copy(xstage0 + slot * Ly::XSTAGE, xsrc + (size_t)j * SPS * Ly::XB, nsub * Ly::XB, bar);
+        if (stma) {
+          tma_2d(sstage0 + slot * Ly::SBYTES, &p->tmS, sx, r0, bar);
+          if (ASYM) tma_2d(zstage0 + slot * Ly::SBYTES, &p->tmZ, sx, r0, bar);
+        }
+      }
     };
 
     __syncwarp();
@@ -724,18 +728,14 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
       for (int tg = 0; tg < NG; ++tg) acc[mt][tg][0] = acc[mt][tg][1] = 0.f;
-    int C[PS][2][NT][4];   // [segment of the pair][m tile][n tile][fragment]
+    int C[PS][2][NT][4];   // [segment of the pair][m tile][n tile][fragment]: one segment's sums
+    int carry[2][NT][4];   // sums of the earlier segments of a group longer than one segment
 
     // epilogue of the group that ends with segment s: recombine the digits,
     // remove zeff * sum(x), scale.  Lanes whose token does not exist compute
     // on token T-1 and never store.
     auto epilogue = [&](const int (&Cs)[2][NT][4], int s, uint32_t xs0, uint32_t sst, uint32_t zst, int sx) {
-      int sc_i = ((kb + s * SEGK) >> lg2gs) - sx;
-      if ((unsigned)sc_i >= (unsigned)Ly::SBW) {   // cannot happen; never read outside the box
-        atomicOr(&g_dev_error, 0x1000u);
-        sc_i = 0;
-      }
-      const uint32_t soff = (uint32_t)sc_i * 4;
+      const uint32_t soff = (uint32_t)(((kb + s * SEGK) >> lg2gs) - sx) * 4;   // inside the stage's box
       float sc[2][2], zp[2][2];
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt)
@@ -767,23 +767,28 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     };
 
     for (int j = 0; j < nstage; ++j) {
-      const uint32_t slot = (gseg + j) % kD;
+      const uint32_t slot = cslot;
       const uint32_t ast = astage0 + slot * Ly::ASTAGE, xst = xstage0 + slot * Ly::XSTAGE;
       const uint32_t sst = sstage0 + slot * Ly::SBYTES, zst = zstage0 + slot * Ly::SBYTES;
-      if (L.dbg != 3 && !bar_wait(bar0 + slot * 8, ((gseg + j) / kD) & 1, 0x10u)) {
+      if (!bar_wait(bar0 + slot * 8, cpar, 0x10u)) {
         ok = false;
         break;
+      }
+      if (++cslot == (uint32_t)kD) {
+        cslot = 0;
+        cpar ^= 1u;
       }
       const int fgj = (kb + j * 256) >> lg2gs;
       const int sx = stma ? (fgj & ~(Ly::SBW - 1)) : fgj;
       // The stage's segments are taken in pairs (PS = 2) with one accumulator
       // set each, so that the two halves' loads, nibble splits and MMAs
-      // interleave; one at a time (PS = 1) above 8 tokens.
+      // interleave; one at a time (PS = 1) above 8 tokens.  Every segment's
+      // sums start from zero; a group that spans several segments carries its
+      // earlier segments' sums in `carry` (integers: exact).
 #pragma unroll
       for (int pr = 0; pr < SPS; pr += PS) {
         const int s0 = j * SPS + pr;
-        if (L.dbg == 2 || s0 >= nseg) break;
-        const bool has1 = PS == 2 && s0 + 1 < nseg;
+        if (s0 >= nseg) break;
         uint32_t w[PS][4][WPL];
         uint32_t bq[PS][NT][2 * WPL];
 #pragma unroll
@@ -794,11 +799,6 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) lds_n<2 * LB>(bval[nt] ? xs0 + bslot[nt] : zblk, bq[h2][nt]);
         }
-        // a set starts afresh at its first segment of a group: with one
-        // segment per group both sets always do; with more, each set carries
-        // its half of the group and the two are added at the group's end
-        const bool first0 = (s0 & spg_mask) == 0;
-        const bool first1 = spg_mask == 0 || (s0 & spg_mask) == 0;
 #pragma unroll
         for (int q = 0; q < WPL; ++q)
 #pragma unroll
@@ -807,38 +807,38 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
             for (int mt = 0; mt < 2; ++mt) {
               const uint32_t a0 = nib_lo<ASYM>(w[h2][2 * mt][q]), a2 = nib_hi<ASYM>(w[h2][2 * mt][q]);
               const uint32_t a1 = nib_lo<ASYM>(w[h2][2 * mt + 1][q]), a3 = nib_hi<ASYM>(w[h2][2 * mt + 1][q]);
-              const bool fst = h2 == 0 ? first0 : first1;
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt) {
-                if (q == 0 && fst) imma0(C[h2][mt][nt], a0, a1, a2, a3, bq[h2][nt][0], bq[h2][nt][1]);
+                if (q == 0) imma0(C[h2][mt][nt], a0, a1, a2, a3, bq[h2][nt][0], bq[h2][nt][1]);
                 else imma(C[h2][mt][nt], a0, a1, a2, a3, bq[h2][nt][2 * q], bq[h2][nt][2 * q + 1]);
               }
             }
-        if constexpr (PS == 1) {
-          if ((s0 & spg_mask) == spg_mask) epilogue(C[0], s0, xst + pr * Ly::XB, sst, zst, sx);
-        } else {
-          // group ends inside the pair: one per segment when a group is one
-          // segment long, else at most one (the odd segment) with the sets summed
-          if (spg_mask == 0) {
-            epilogue(C[0], s0, xst + pr * Ly::XB, sst, zst, sx);
-            if (has1) epilogue(C[PS - 1], s0 + 1, xst + (pr + 1) * Ly::XB, sst, zst, sx);
-          } else if (((s0 + 1) & spg_mask) == spg_mask) {
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) C[0][mt][nt][e] += C[PS - 1][mt][nt][e];
-            epilogue(C[0], s0 + 1, xst + (pr + 1) * Ly::XB, sst, zst, sx);
+        for (int h2 = 0; h2 < PS; ++h2) {
+          const int sg = s0 + h2;
+          if (h2 > 0 && sg >= nseg) break;
+          if (spg_mask == 0) {   // one segment per group (the common case)
+            epilogue(C[h2], sg, xst + (pr + h2) * Ly::XB, sst, zst, sx);
+            continue;
           }
+          const bool gfirst = (sg & spg_mask) == 0, glast = (sg & spg_mask) == spg_mask;
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int v = gfirst ? C[h2][mt][nt][e] : C[h2][mt][nt][e] + carry[mt][nt][e];
+                if (glast) C[h2][mt][nt][e] = v;
+                else carry[mt][nt][e] = v;
+              }
+          if (glast) epilogue(C[h2], sg, xst + (pr + h2) * Ly::XB, sst, zst, sx);
         }
       }
       __syncwarp();
       if (j + kD - 1 < nstage) issue(j + kD - 1);
     }
     if (!ok) break;
-    gseg += (uint32_t)nstage;
-    if (tr && lane == 0) tr[3] = globaltimer_ns();
 
     // ---- results ---------------------------------------------------------------
     if constexpr (CMP) {
@@ -1253,7 +1253,6 @@ int run_tile_linear(const uint8_t* W, const float* S, const float* Z, const floa
   L.phctr = nullptr;
   L.flags = nullptr;
   L.prefetch = 0;
-  L.dbg = 0;
   const int need = (int)((L.total + c.wpc - 1) / c.wpc);
   if (c.grid > need) c.grid = need;
   cudaError_t e = launch_xblocks(T, c.LB, 1, L, stream, (q.nchunk + 7) / 8);
@@ -1490,7 +1489,6 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
   L.flags = reinterpret_cast<unsigned int*>(ws);
   L.phctr = reinterpret_cast<unsigned int*>(ws + align256((size_t)128 * c.grid));
   L.prefetch = env_int("SF_TILE_PREFETCH", 1);
-  L.dbg = env_int("SF_TILE_DBG", 0);
   L.epoch = nullptr;
   L.poison = poison;
   cudaError_t e = cudaMemcpy(table, h.data(), (size_t)ntasks * sizeof(TileTask), cudaMemcpyHostToDevice);
@@ -1553,28 +1551,6 @@ int sf_q4_step_run(void* handle, void* stream) { return sf_q4_step_launch(handle
 
 void sf_q4_step_destroy(void* handle) { delete static_cast<StepHandle*>(handle); }
 
-// Development aid, not part of the public header: record per-unit timestamps
-// of every later run of `handle` into `buf` (4 x u64 per unit; null stops).
-int sf_q4_step_set_trace(void* handle, unsigned long long* buf) {
-  if (!handle) return fail(SF_ERR_NULL, "null handle");
-  static_cast<StepHandle*>(handle)->L.trace = buf;
-  return SF_OK;
-}
-
-// Development aid: first unit and phase of task i (host copy of the table).
-int sf_q4_step_task_info(void* handle, int i, long long* ubase, int* phase) {
-  StepHandle* hd = static_cast<StepHandle*>(handle);
-  if (!hd || i < 0 || i >= hd->L.ntasks) return SF_ERR_SHAPE;
-  TileTask q;
-  cudaMemcpy(&q, hd->L.tasks + i, sizeof(q), cudaMemcpyDeviceToHost);
-  *ubase = q.ubase;
-  *phase = q.phase;
-  return SF_OK;
-}
-
-long long sf_q4_step_units(void* handle) {
-  return handle ? static_cast<StepHandle*>(handle)->L.total : 0;
-}
 
 }  // extern "C"
 
@@ -1681,7 +1657,6 @@ extern "C" int sf_q4_linear_static_scratch(const uint8_t* W, const float* scales
   L.phctr = nullptr;
   L.flags = nullptr;
   L.prefetch = 0;
-  L.dbg = 0;
   const int need = (int)((L.total + c.wpc - 1) / c.wpc);
   if (c.grid > need) c.grid = need;
   e = launch_xblocks(T, c.LB, 1, L, st, (q.nchunk + 7) / 8);
