@@ -121,13 +121,6 @@ size_t sf_q4_step_workspace_bytes(const sf_q4_task* tasks, int ntasks);
 int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size_t workspace_bytes,
                       void** handle_out);
 int sf_q4_step_run(void* handle, void* stream);
-/* sf_q4_step_run in parts, for measurement: part 1 = the preparation only
-   (clear the step's counters, convert the inputs of the first phase),
-   part 2 = the GEMV kernel only, part 0 = both (= sf_q4_step_run).  Part 2
-   is accepted only for a single-phase step (no task with wait_before), and is
-   a complete run when the previous run of this handle finished without error
-   and the inputs are unchanged since its part 1. */
-int sf_q4_step_launch(void* handle, void* stream, int part);
 void sf_q4_step_destroy(void* handle);
 
 /* sf_q4_linear for T <= 16 that allocates nothing.  No counterpart in the

@@ -46,7 +46,6 @@ SIGNATURES = {
     "sf_q4_step_workspace_bytes": [ctypes.POINTER(Q4Task), _I],
     "sf_q4_step_create": [ctypes.POINTER(Q4Task), _I, _P, _SZ, ctypes.POINTER(_P)],
     "sf_q4_step_run": [_P, _P],
-    "sf_q4_step_launch": [_P, _P, _I],
     "sf_q4_step_destroy": [_P],
     "sf_tp_handle_bytes": [],
     "sf_tp_comm_init": [_I, _I, _SZ, _SZ, ctypes.POINTER(_P), _P],

@@ -140,6 +140,7 @@ struct alignas(64) TileTask {
   // Phase of this task: a run of tasks that read X only after the previous
   // phase has written all its tiles.  Phase 0 reads inputs that exist at launch.
   int phase, ph_first, ph_tiles, ph_chunks, ph_last;
+  int ph_cbase;              // the phase's first entry in the launch's chunk map
   long long ph_ubase, ph_units;
   // Tensor-parallel exchange (row-parallel projections), see sf_q4_step_create_tp:
   //  kind 0: GEMV; push != 0: its fp32 tiles go to every rank's exchange
@@ -160,8 +161,10 @@ struct TileLaunch {
   unsigned int* flags;    // per CTA, one 128-byte line: [phases written, phases converted]
   long long total;        // units in the launch
   int ntasks;
-  int prefetch;           // pull a waiting unit's weights into L2 before the wait
-  unsigned long long* epoch;   // launch counter (tensor-parallel exchange), advanced by the pre-pass, or null
+  unsigned long long* epoch;   // last finished launch (tensor-parallel exchange epoch), or null
+  unsigned int* done;          // CTAs finished (step launches: the last one resets the counters), or null
+  const unsigned int* cmap;    // per phase, its conversion chunks in order: (task << 16) | chunk of the task
+  int nphase;                  // phases of the step (phctr has 4 words per phase)
   unsigned long long* poison;  // the communicator's sticky poison word (tensor-parallel steps), or null
 };
 
@@ -218,9 +221,6 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_
 }
 __device__ __forceinline__ void cpa4(uint32_t dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ uint4 lds128(uint32_t a) {
   uint4 v;
@@ -538,7 +538,8 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
   }
 
   const long long W_all = (long long)gridDim.x * (blockDim.x >> 5);
-  const unsigned long long ep = L.epoch ? launch_epoch(L) : 0ull;   // this launch's exchange epoch
+  // this launch's exchange epoch: one more than the last finished launch's
+  const unsigned long long ep = L.epoch ? launch_epoch(L) + 1 : 0ull;
   if (L.poison && *reinterpret_cast<volatile const unsigned long long*>(L.poison)) {
     // An earlier step gave up on a peer: compute nothing, and poison every
     // pushed tile's flag in every peer so that their reduce tasks fail at once.
@@ -553,6 +554,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     return;
   }
   uint32_t cslot = 0, cpar = 0;   // this warp's ring: next slot to consume and its phase parity
+  int seen_phase = -1;            // last phase whose inputs this warp has seen converted
   int ti = 0;
   bool ok = true;
 
@@ -571,35 +573,112 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     const int lg2spg = lg2gs - (31 - __clz(SEGK));   // segments per group = 1 << lg2spg
     const int spg_mask = (1 << lg2spg) - 1;
 
-    // ---- dependencies and activation blocks --------------------------------
-    if (p->phase > 0) {
-      const int ph = p->phase;
-      if (L.prefetch) {
-        // The weights do not depend on earlier tasks: start them towards L2
-        // now, so that the wait overlaps with HBM traffic.
-        const int rows = min(kUnitRows, N - r0);
-        if (ksplit == 1) {
-          if (lane == 0) prefetch_l2(p->W + (size_t)r0 * (K >> 1), (uint32_t)rows * (K >> 1));
-        } else if (lane < rows) {
-          prefetch_l2(p->W + (size_t)(r0 + lane) * (K >> 1) + (kb >> 1), (uint32_t)(ke - kb) >> 1);
+    // ---- operand streaming (set-up) ------------------------------------------
+    // Stage j holds k [kb + 256 j, kb + 256 j + 256): the weight tile, the
+    // activation blocks of its segments and the scale box of its groups.
+    // Ring position: `cslot` / `cpar` are the slot and phase parity of the
+    // next stage to consume, `islot` the slot of the next stage to issue.
+    const int nstage = (nseg + SPS - 1) / SPS;
+    const uint8_t* xsrc = p->xd + (size_t)(kb / SEGK) * Ly::XB;
+    const float* Sb = p->S;
+    const float* Zb = p->Z;
+    uint32_t islot = cslot;
+    // issue_w: the stage's barrier expectation (weights, scales AND activations)
+    // and its weight / scale copies; issue_x: its activation copy.  Weights do
+    // not depend on earlier tasks, so a unit that must wait for its inputs
+    // starts its first stages' weights before the wait.
+    auto slot_of = [&](int j) {   // ring slot of stage j of this unit
+      const uint32_t s2 = cslot + (uint32_t)j;
+      return s2 >= (uint32_t)kD ? s2 - kD : s2;
+    };
+    auto issue_w = [&](int j) {
+      const uint32_t slot = islot;
+      islot = islot + 1 == (uint32_t)kD ? 0u : islot + 1;
+      const uint32_t bar = bar0 + slot * 8;
+      const int nsub = min(SPS, nseg - j * SPS);
+      const int fg = (kb + j * 256) >> lg2gs;                   // first group of the stage
+      // scale box origin: TMA boxes start on SBW-group boundaries (units are
+      // cut in whole boxes, so the stage's groups stay inside); per-lane
+      // copies start at the stage's first group
+      const int sx = stma ? (fg & ~(Ly::SBW - 1)) : fg;
+      if (!stma) {
+#pragma unroll
+        for (int c = t; c < Ly::SBW; c += 4) {
+          const int grp = sx + c;
+          if (grp >= g0 && grp < gend) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int row = min(r0 + rloc[i], N - 1);
+              const uint32_t o = (uint32_t)(rloc[i] * Ly::SBW + c) * 4;
+              cpa4(sstage0 + slot * Ly::SBYTES + o, Sb + (size_t)row * G + grp);
+              if (ASYM) cpa4(zstage0 + slot * Ly::SBYTES + o, Zb + (size_t)row * G + grp);
+            }
+          }
+        }
+        // each lane's copies count as one more arrival on the stage's barrier;
+        // they are registered before lane 0's arrival below can end the phase
+        bar_arrive_cpasync(bar);
+        __syncwarp();
+      }
+      if (lane == 0) {
+        const uint32_t sbytes = stma ? (uint32_t)Ly::SBYTES * (ASYM ? 2 : 1) : 0u;
+        bar_expect_tx(bar, (uint32_t)Ly::ASTAGE + nsub * Ly::XB + sbytes);
+        tma_2d(astage0 + slot * Ly::ASTAGE, &p->tmW, (kb >> 1) + j * 128, r0, bar);
+        if (stma) {
+          tma_2d(sstage0 + slot * Ly::SBYTES, &p->tmS, sx, r0, bar);
+          if (ASYM) tma_2d(zstage0 + slot * Ly::SBYTES, &p->tmZ, sx, r0, bar);
         }
       }
+    };
+    auto issue_x = [&](int j, uint32_t slot) {
+      const int nsub = min(SPS, nseg - j * SPS);
+      if (lane == 0) {
+        bulk_copy(xstage0 + slot * Ly::XSTAGE, xsrc + (size_t)j * SPS * Ly::XB, nsub * Ly::XB, bar0 + slot * 8);
+      }
+    };
+    const int npro = min(kD - 1, nstage);   // stages issued before the main loop
+    // a wait that expired after issue_w: complete and wait out the copies in
+    // flight (bounded) so that none lands after the CTA has exited
+    auto drain = [&]() {
+      for (int j = 0; j < npro; ++j) issue_x(j, slot_of(j));
+      for (int j = 0; j < npro; ++j) {
+        const uint32_t sl = slot_of(j);
+        bar_wait(bar0 + sl * 8, cpar ^ (sl < cslot ? 1u : 0u), 0x10u);
+      }
+    };
+    const bool gemv = p->kind == 0;
+    if (gemv) {
+      __syncwarp();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      for (int j = 0; j < npro; ++j) issue_w(j);
+    }
+    // ---- dependencies and activation blocks --------------------------------
+    // A warp takes its units in increasing order and phases never go back, so
+    // only its first unit of a phase waits (and converts its share); the later
+    // ones find the phase's inputs ready.
+    if (!p->xpre && p->phase > seen_phase) {
+      const int ph = p->phase;
+      seen_phase = ph;
       const unsigned int* fl = L.flags + blockIdx.x * 32;
       int okw = 1;
       if (lane == 0) okw = spin_geq(fl, (unsigned)ph, 0x200u);   // previous phase written
       ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
-      if (!ok) break;
+      if (!ok) {
+        if (gemv) drain();
+        break;
+      }
       // The first units of the phase convert its inputs: unit i takes chunks
       // i, i + CS, ... over all tasks of the phase.  Every warp has at most
       // one such unit per phase and reaches it before any other unit of the
       // phase, so no converting warp waits on its own conversion.
+      {
       const long long CS = min(W_all, p->ph_units);
       const long long i = u - p->ph_ubase;
       if (i < CS && i < p->ph_chunks) {
-        int n = 0, tj = p->ph_first, cbase = 0;
+        int n = 0;
         for (long long c = i; c < p->ph_chunks; c += CS) {
-          while (c - cbase >= tile_task(L, tj)->nchunk) cbase += tile_task(L, tj++)->nchunk;
-          convert_chunk<T, LB>(tile_task(L, tj), (int)(c - cbase), lane);
+          const unsigned int e = __ldg(L.cmap + p->ph_cbase + c);
+          convert_chunk<T, LB>(tile_task(L, (int)(e >> 16)), (int)(e & 0xFFFFu), lane);
           ++n;
         }
         asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -616,7 +695,11 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
         asm volatile("fence.proxy.async.global;" ::: "memory");
       }
       ok = __shfl_sync(0xffffffffu, okx, 0) != 0;
-      if (!ok) break;
+      if (!ok) {
+        if (gemv) drain();
+        break;
+      }
+      }
     }
 
     if (p->kind == 1) {
@@ -666,62 +749,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       tile_written(L, p, lane);
       continue;
     }
-    // ---- operand streaming ---------------------------------------------------
-    // Stage j holds k [kb + 256 j, kb + 256 j + 256): the weight tile, the
-    // activation blocks of its segments and the scale box of its groups.
-    // Ring position: `cslot` / `cpar` are the slot and phase parity of the
-    // next stage to consume, `islot` the slot of the next stage to issue.
-    const int nstage = (nseg + SPS - 1) / SPS;
-    const uint8_t* xsrc = p->xd + (size_t)(kb / SEGK) * Ly::XB;
-    const float* Sb = p->S;
-    const float* Zb = p->Z;
-    uint32_t islot = cslot;
-    auto issue = [&](int j) {
-      const uint32_t slot = islot;
-      islot = islot + 1 == (uint32_t)kD ? 0u : islot + 1;
-      const uint32_t bar = bar0 + slot * 8;
-      const int nsub = min(SPS, nseg - j * SPS);
-      const int fg = (kb + j * 256) >> lg2gs;                   // first group of the stage
-      // scale box origin: TMA boxes start on SBW-group boundaries (units are
-      // cut in whole boxes, so the stage's groups stay inside); per-lane
-      // copies start at the stage's first group
-      const int sx = stma ? (fg & ~(Ly::SBW - 1)) : fg;
-      if (!stma) {
-#pragma unroll
-        for (int c = t; c < Ly::SBW; c += 4) {
-          const int grp = sx + c;
-          if (grp >= g0 && grp < gend) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int row = min(r0 + rloc[i], N - 1);
-              const uint32_t o = (uint32_t)(rloc[i] * Ly::SBW + c) * 4;
-              cpa4(sstage0 + slot * Ly::SBYTES + o, Sb + (size_t)row * G + grp);
-              if (ASYM) cpa4(zstage0 + slot * Ly::SBYTES + o, Zb + (size_t)row * G + grp);
-            }
-          }
-        }
-        // each lane's copies count as one more arrival on the stage's barrier;
-        // they are registered before lane 0's arrival below can end the phase
-        bar_arrive_cpasync(bar);
-        __syncwarp();
-      }
-      if (lane == 0) {
-        const uint32_t sbytes = stma ? (uint32_t)Ly::SBYTES * (ASYM ? 2 : 1) : 0u;
-        bar_expect_tx(bar, (uint32_t)Ly::ASTAGE + nsub * Ly::XB + sbytes);
-        tma_2d(astage0 + slot * Ly::ASTAGE, &p->tmW, (kb >> 1) + j * 128, r0, bar);
-        bulk_copy(xstage0 + slot * Ly::XSTAGE, xsrc + (size_t)j * SPS * Ly::XB, nsub * Ly::XB, bar);
-        if (stma) {
-          tma_2d(sstage0 + slot * Ly::SBYTES, &p->tmS, sx, r0, bar);
-          if (ASYM) tma_2d(zstage0 + slot * Ly::SBYTES, &p->tmZ, sx, r0, bar);
-        }
-      }
-    };
-
-    __syncwarp();
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-#pragma unroll
-    for (int j = 0; j < kD - 1; ++j)
-      if (j < nstage) issue(j);
+    for (int j = 0; j < npro; ++j) issue_x(j, slot_of(j));
 
     float acc[2][NG][2];
 #pragma unroll
@@ -836,7 +864,11 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
         }
       }
       __syncwarp();
-      if (j + kD - 1 < nstage) issue(j + kD - 1);
+      if (j + kD - 1 < nstage) {
+        const uint32_t sl = islot;
+        issue_w(j + kD - 1);
+        issue_x(j + kD - 1, sl);
+      }
     }
     if (!ok) break;
 
@@ -917,12 +949,34 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       }
     }
   }
+  // ---- end of a step launch: the last CTA to finish resets the cross-CTA
+  // counters and flag lines for the next launch on the stream, and advances
+  // the exchange epoch (so no clearing launch is needed between steps).
+  if (L.done) {
+    __syncthreads();
+    unsigned int old = 0;
+    if (threadIdx.x == 0) {
+      __threadfence();
+      old = atomicAdd(L.done, 1u);
+    }
+    if (__syncthreads_or(threadIdx.x == 0 && old == gridDim.x - 1)) {
+      __threadfence();
+      // flag lines use words 0 (phases written) and 1 (phases converted)
+      for (int i = threadIdx.x; i < 2 * (int)gridDim.x; i += blockDim.x) L.flags[(i >> 1) * 32 + (i & 1)] = 0u;
+      for (int i = threadIdx.x; i < 4 * L.nphase; i += blockDim.x) L.phctr[i] = 0u;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        if (L.epoch) *reinterpret_cast<volatile unsigned long long*>(L.epoch) = ep;
+        __threadfence();
+        *L.done = 0u;
+      }
+    }
+  }
 }
 
 // Activation blocks of the tasks whose input exists at launch: one CTA per task.
 template <int T, int LB>
 __global__ void __launch_bounds__(256) q4_xblocks_kernel(const __grid_constant__ TileLaunch L) {
-  if (L.epoch && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *L.epoch += 1;   // next exchange epoch
   const TileTask* p = tile_task(L, blockIdx.x);
   if (!p->xpre) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1252,7 +1306,6 @@ int run_tile_linear(const uint8_t* W, const float* S, const float* Z, const floa
   L.tasks = nullptr; L.ntasks = 1; L.total = (long long)q.ntile * q.ksplit;
   L.phctr = nullptr;
   L.flags = nullptr;
-  L.prefetch = 0;
   const int need = (int)((L.total + c.wpc - 1) / c.wpc);
   if (c.grid > need) c.grid = need;
   cudaError_t e = launch_xblocks(T, c.LB, 1, L, stream, (q.nchunk + 7) / 8);
@@ -1275,8 +1328,8 @@ namespace {
 // counters] (cleared before every run) [task table] [k-split partials]
 // [activation blocks].
 struct StepSizes {
-  size_t ctr, tiles, table, part, xblk;
-  size_t total() const { return ctr + tiles + table + part + xblk; }
+  size_t ctr, tiles, table, part, xblk, cmap;
+  size_t total() const { return ctr + tiles + table + part + xblk + cmap; }
 };
 
 // k-splits of a task list: each phase (a run of tasks that need not wait for
@@ -1306,18 +1359,20 @@ std::vector<int> plan_ksplit(const sf_q4_task* tasks, int n, int warps) {
 
 StepSizes step_sizes(const sf_q4_task* tasks, int n, const std::vector<int>& ksplit, int grid) {
   StepSizes z{};
-  z.ctr = align256((size_t)128 * grid) + align256((size_t)16 * n);
-  size_t tiles = 0, part = 0, xb = 0;
+  z.ctr = align256((size_t)128 * grid) + align256((size_t)16 * n + 16);   // flag lines, phase counters, done
+  size_t tiles = 0, part = 0, xb = 0, chunks = 0;
   for (int i = 0; i < n; ++i) {
     const sf_q4_task& a = tasks[i];
     const int ntile = (a.N + kUnitRows - 1) / kUnitRows;
     tiles += (size_t)ntile * 4;
     if (ksplit[i] > 1) part += align256((size_t)ksplit[i] * a.T * a.N * 4);
     xb += xblocks_bytes(a.T, a.K, a.group_size);
+    chunks += ((size_t)a.T * (a.K / 8) + 31) / 32;
   }
   z.tiles = align256(tiles);
   z.table = align256((size_t)n * sizeof(TileTask));
   z.part = part;
+  z.cmap = align256(chunks * 4);
   z.xblk = xb;
   return z;
 }
@@ -1328,9 +1383,7 @@ struct StepHandle {
   TileConfig cfg;
   TileLaunch L;
   void* workspace;
-  size_t clear_bytes;
-  bool coop, prepass;
-  int xny;                  // pre-pass CTAs per task (largest task's chunks / 8)
+  bool coop;
   bool tp;                  // has tensor-parallel exchange tasks (epoch at the workspace end)
 };
 
@@ -1407,7 +1460,7 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
   std::vector<TileTask> h(ntasks);
   unsigned long long* poison = nullptr;
   long long ub = 0;
-  int nph = 0, xny = 1;
+  int nph = 0;
   for (int i = 0; i < ntasks; ++i) {
     const sf_q4_task& a = tasks[i];
     TileTask& q = h[i];
@@ -1430,7 +1483,7 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
     // earlier ones).  Only phase-0 inputs exist before the launch.
     if (i == 0 || a.wait_before) ++nph;
     q.phase = nph - 1;
-    q.xpre = q.phase == 0 ? 1 : 0;
+    q.xpre = 0;   // every phase converts its inputs inside the launch
     const int role = roles ? roles[i] : SF_ROLE_GEMV;
     if (role != SF_ROLE_GEMV) {
       q.push = role == SF_ROLE_PUSH;
@@ -1451,7 +1504,6 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
         if (rc2 != SF_OK) return rc2;
       }
     }
-    if (q.xpre && (q.nchunk + 7) / 8 > xny) xny = (q.nchunk + 7) / 8;
     q.ubase = ub;
     ub += (long long)q.ntile * q.ksplit;
   }
@@ -1474,13 +1526,21 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
     }
     i = j;
   }
+  // chunk map: phase by phase, every task's conversion chunks in order
+  std::vector<unsigned int> cmap;
+  for (int i = 0; i < ntasks; ++i) {
+    if (i == 0 || h[i].phase != h[i - 1].phase) {
+      for (int k = i; k < ntasks && h[k].phase == h[i].phase; ++k) h[k].ph_cbase = (int)cmap.size();
+    }
+    if (h[i].nchunk > 0xFFFF || i > 0xFFFF)
+      return fail(SF_ERR_UNSUPPORTED, "task %d: too many tasks or conversion chunks for the step's chunk map", i);
+    for (int c = 0; c < h[i].nchunk; ++c) cmap.push_back(((unsigned int)i << 16) | (unsigned int)c);
+  }
+  uint8_t* cmap_d = ws + z.total() - z.cmap;
   StepHandle* hd = new StepHandle{};
   hd->cfg = c;
   hd->workspace = workspace;
-  hd->clear_bytes = z.ctr + z.tiles;
-  hd->coop = nph > 1 || has_tp;   // exchange waits need every CTA resident
-  hd->prepass = true;
-  hd->xny = xny;
+  hd->coop = true;   // the input-conversion and exchange waits need every CTA resident
   hd->tp = has_tp;
   TileLaunch& L = hd->L;
   L.tasks = reinterpret_cast<const TileTask*>(table);
@@ -1488,10 +1548,16 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
   L.total = ub;
   L.flags = reinterpret_cast<unsigned int*>(ws);
   L.phctr = reinterpret_cast<unsigned int*>(ws + align256((size_t)128 * c.grid));
-  L.prefetch = env_int("SF_TILE_PREFETCH", 1);
+  L.done = L.phctr + 4 * ntasks;
+  L.cmap = reinterpret_cast<const unsigned int*>(cmap_d);
+  L.nphase = nph;
   L.epoch = nullptr;
   L.poison = poison;
   cudaError_t e = cudaMemcpy(table, h.data(), (size_t)ntasks * sizeof(TileTask), cudaMemcpyHostToDevice);
+  // counters start at zero; every run leaves them so
+  if (e == cudaSuccess) e = cudaMemset(ws, 0, z.ctr + z.tiles);
+  if (e == cudaSuccess && !cmap.empty())
+    e = cudaMemcpy(cmap_d, cmap.data(), cmap.size() * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess && has_tp) {
     L.epoch = reinterpret_cast<unsigned long long*>(ws + z.total());
     e = cudaMemset(L.epoch, 0, kEpochBytes);
@@ -1518,36 +1584,16 @@ int sf_q4_step_create_tp(const sf_q4_task* tasks, const int* roles, int ntasks, 
   return step_create_impl(tasks, roles, ntasks, comm, workspace, workspace_bytes, handle_out);
 }
 
-int sf_q4_step_launch(void* handle, void* stream, int part) {
+int sf_q4_step_run(void* handle, void* stream) {
   if (!handle) return fail(SF_ERR_NULL, "null handle");
-  if (part < 0 || part > 2) return fail(SF_ERR_SHAPE, "part must be 0, 1 or 2");
   StepHandle* hd = static_cast<StepHandle*>(handle);
-  if (part == 2 && hd->coop)
-    return fail(SF_ERR_UNSUPPORTED,
-                "the GEMV kernel alone needs a single-phase step without exchange tasks (no wait_before)");
-  if (part == 1 && hd->tp)
-    return fail(SF_ERR_UNSUPPORTED,
-                "a step with exchange tasks runs whole (part 0): the pre-pass alone would advance its exchange "
-                "epoch without the exchange");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaSuccess;
-  if (part != 2) {
-    e = cudaMemsetAsync(hd->workspace, 0, hd->clear_bytes, st);
-    if (e != cudaSuccess) return cuda_fail(e, "clearing the step counters");
-  }
-  if (part != 2 && hd->prepass) {
-    e = launch_xblocks(hd->cfg.T, hd->cfg.LB, hd->L.ntasks, hd->L, st, hd->xny);
-    if (e != cudaSuccess) return cuda_fail(e, "activation pre-pass launch");
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-  }
-  if (part == 1) return SF_OK;
-  e = launch_tile(hd->cfg, hd->L, hd->coop, st);
+  // one launch: the kernel converts each phase's inputs itself and its last
+  // CTA leaves the counters cleared for the next run
+  cudaError_t e = launch_tile(hd->cfg, hd->L, hd->coop, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "q4 step launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return SF_OK;
 }
-
-int sf_q4_step_run(void* handle, void* stream) { return sf_q4_step_launch(handle, stream, 0); }
 
 void sf_q4_step_destroy(void* handle) { delete static_cast<StepHandle*>(handle); }
 
@@ -1656,7 +1702,6 @@ extern "C" int sf_q4_linear_static_scratch(const uint8_t* W, const float* scales
   L.tasks = nullptr; L.ntasks = 1; L.total = (long long)q.ntile * q.ksplit;
   L.phctr = nullptr;
   L.flags = nullptr;
-  L.prefetch = 0;
   const int need = (int)((L.total + c.wpc - 1) / c.wpc);
   if (c.grid > need) c.grid = need;
   e = launch_xblocks(T, c.LB, 1, L, st, (q.nchunk + 7) / 8);

@@ -126,26 +126,9 @@ class Q4StepRunner:
 
     @property
     def kernels_per_step(self) -> int:
-        """Kernels of this library one step launches: the activation pre-pass
-        and the GEMV kernel (persistent), or one GEMV launch per call."""
-        return 2 if self.persistent else len(self.calls)
-
-    def capture_kernel_only(self):
-        """A CUDA graph of the step's GEMV kernel alone (no counter clear, no
-        pre-pass), for timing that kernel.  Only for single-phase steps; valid
-        after one full run with unchanged inputs."""
-        if not self.persistent:
-            raise RuntimeError("kernel-only replay needs the persistent step")
-        lib = _lib.load()
-        with torch.cuda.device(self.device):
-            self.stream.wait_stream(torch.cuda.current_stream(self.device))
-            with torch.cuda.stream(self.stream):
-                _lib.check(lib.sf_q4_step_launch(self._handle, self.stream.cuda_stream, 2))
-            self.stream.synchronize()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=self.stream):
-                _lib.check(lib.sf_q4_step_launch(self._handle, self.stream.cuda_stream, 2))
-        return g
+        """Kernels of this library one step launches: one persistent launch,
+        or one GEMV launch per call (pre-pass + GEMV below the prefill size)."""
+        return 1 if self.persistent else 2 * len(self.calls)
 
     def algorithmic_bytes(self) -> int:
         """Bytes one step must move: packed weights, fp32 scales (and zeros),

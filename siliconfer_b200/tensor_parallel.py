@@ -379,11 +379,11 @@ class TPStepRunner:
                                                 None, part.numel(), part.shape[1], st.cuda_stream))
 
     def launches_per_step(self) -> int:
-        """Kernels of this library per step: 2 per step launch (activation
-        pre-pass + GEMV kernel), plus one peer all-reduce per row-parallel
+        """Kernels of this library per step: one per step handle (the
+        persistent GEMV launch), plus one peer all-reduce per row-parallel
         projection when mode is 'peer' and world > 1."""
         red = 2 * len(self.layers) if (self.world > 1 and self.mode == "peer") else 0
-        return 2 * len(self._handles) + red
+        return len(self._handles) + red
 
     def _launch_all(self, st):
         if self.mode == "fused":
