@@ -311,6 +311,8 @@ def run_ours(args, rank, world, local_rank):
         "build_s": round(build_s, 1),
     }
     if world == 1 and args.workload == "7b" and not args.no_prefill:
+        result["sweep"] = sweep_measure(layers, device, args)
+        result["small_configs"] = small_configs_measure(device)
         result["prefill"] = prefill_measure(device, runner.stream)
         result["kv_attention"] = kv_attention_measure(device, runner.stream)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -627,6 +629,105 @@ def _teardown(dist, comm, runners, *refs, exit_dist=True):
         dist.barrier()
         if exit_dist:
             dist.destroy_process_group()
+
+
+def _time_replays(replay, stream, n, flush=None):
+    """Device time of one replay (ms), CUDA events on `stream`.  With `flush`
+    (a buffer larger than L2) every replay is timed alone after the buffer
+    was overwritten, so each one starts with cold caches."""
+    import torch
+    if flush is None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(n):
+                replay()
+            e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / n
+    tot = 0.0
+    for _ in range(n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            flush.add_(1)
+            e0.record(stream)
+            replay()
+            e1.record(stream)
+        e1.synchronize()
+        tot += e0.elapsed_time(e1)
+    return tot / n
+
+
+def sweep_measure(layers, device, args):
+    """BASELINE config 3's batch sweep: the same 7B step at 4 and 16 tokens,
+    each one launch that reads every weight once (batch 1 is the headline)."""
+    import torch
+    from siliconfer_b200.runner import Q4StepRunner
+    peak, peak_kind = measured_peak()
+    out = []
+    for t in (4, 16):
+        r = Q4StepRunner(layers, tokens=t, x_dtype=torch.float16, y_dtype=torch.float32, device=device,
+                         waits=[False] * len(layers))
+        g = torch.Generator(device=device)
+        g.manual_seed(70 + t)
+        r.x.copy_(torch.randn(r.x.shape, generator=g, device=device).to(r.x.dtype))
+        r.capture()
+        with torch.cuda.stream(r.stream):
+            for _ in range(args.warmup):
+                r.graph.replay()
+            ms = _time_replays(r.graph.replay, r.stream, max(5, min(args.steps, 20)))
+        nb = r.algorithmic_bytes()
+        out.append({"batch": t, "us": round(ms * 1e3, 1), "gbs": round(nb / ms / 1e6, 1),
+                    "frac": round(nb / ms / 1e6 / peak, 4), "bytes": nb, "launches_per_step": r.kernels_per_step})
+        del r
+    return {"workload": "BASELINE config 3 (7B step, sym int4 g128, fp16 x) at batch 4 and 16; one launch of "
+                        "the decode kernel per step, every weight read once", "peak_gbs": peak,
+            "peak_kind": peak_kind, "timing": "CUDA events over back-to-back graph replays (weights 3.44 GB >> L2)",
+            "points": out}
+
+
+def small_configs_measure(device, iters=20):
+    """BASELINE configs 1 and 2 on Qwen2.5-0.5B shapes (hidden 896, inter 4864).
+
+    config 1: one layer, sym RTN int4 g128, batch 1, fp32 x -- 7.9 MB, a latency figure;
+    config 2: the 24-layer step, ASYMMETRIC int4 g128 with fp32 zeros (one 60-sigma outlier in
+    layer 0's down_proj), batch 1, fp32 x.  The weights are quantized on the device with the
+    reference's RTN (bit-exact); the HQQ grid choice (an offline quantizer) is not repeated here.
+    Both are timed one replay at a time after overwriting a 256 MB buffer (L2 flushed)."""
+    import torch
+    from siliconfer_b200.q4_linear import Q4Linear
+    from siliconfer_b200.quant import pack_weights_device
+    from siliconfer_b200.runner import Q4StepRunner
+    peak, _ = measured_peak()
+    flush = torch.zeros(64 << 20, dtype=torch.float32, device=device)   # 256 MB > L2
+    out = {}
+    for name, n_layers, sym in (("config1_0p5b_layer_sym", 1, True), ("config2_0p5b_24layers_asym", 24, False)):
+        gen = torch.Generator(device=device)
+        layers = []
+        for li in range(n_layers):
+            for pi, (pname, n, k) in enumerate(shapes("0.5b")):
+                gen.manual_seed(5000 + 100 * li + pi)
+                W = torch.randn((n, k), generator=gen, device=device) * 0.02
+                if not sym and li == 0 and pname == "down":
+                    W[17, 1234] = 60 * 0.02
+                trip = pack_weights_device(W, 128, sym=sym)
+                layers.append(Q4Linear(trip[0], trip[1], zeros=None if sym else trip[2], group_size=128,
+                                       device=device))
+        r = Q4StepRunner(layers, tokens=1, x_dtype=torch.float32, y_dtype=torch.float32, device=device,
+                         waits=[False] * len(layers))
+        r.x.normal_()
+        r.capture()
+        with torch.cuda.stream(r.stream):
+            for _ in range(3):
+                r.graph.replay()
+        ms = _time_replays(r.graph.replay, r.stream, iters, flush=flush)
+        nb = r.algorithmic_bytes()
+        out[name] = {"layers": n_layers, "layout": "sym" if sym else "asym (fp32 zeros)", "us": round(ms * 1e3, 2),
+                     "gbs": round(nb / ms / 1e6, 1), "frac": round(nb / ms / 1e6 / peak, 4), "bytes": nb,
+                     "launches_per_step": r.kernels_per_step}
+        del r, layers
+    out["timing"] = "each replay timed alone with CUDA events after a 256 MB buffer write (cold L2)"
+    return out
 
 
 def prefill_measure(device, stream, iters=20):

@@ -116,12 +116,33 @@ typedef struct {
   const void* X;        /* [T, K] of x_dtype */
   void* Y;              /* [T, N] of y_dtype */
   int N, K, T, group_size, x_dtype, y_dtype, wait_before;
+  int epilogue;         /* 0, or SF_EPI_SWIGLU (see sf_q4_linear_swiglu; N = gate + up rows) */
 } sf_q4_task;
+#define SF_EPI_SWIGLU 1
 size_t sf_q4_step_workspace_bytes(const sf_q4_task* tasks, int ntasks);
 int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size_t workspace_bytes,
                       void** handle_out);
 int sf_q4_step_run(void* handle, void* stream);
 void sf_q4_step_destroy(void* handle);
+
+/* ---- MLP gate/up with the SwiGLU activation fused ------------------------
+ * Replaces the gate/up half of siliconfer's MLP.__call__ (siliconfer/model/
+ * layers.py:144: down_proj(silu(gate_proj(x)) * up_proj(x))): both
+ * projections read x once, in one GEMV whose epilogue writes
+ *   Y[T, N] = silu(X @ Wg^T + bg) * (X @ Wu^T + bu),  silu(v) = v / (1 + e^-v),
+ * ready to be down_proj's input.  W, scales, zeros and bias hold the gate and
+ * up triples INTERLEAVED in blocks of 16 rows: rows 32i .. 32i+15 are gate rows
+ * 16i .. 16i+15, rows 32i+16 .. 32i+31 the same up rows (2N rows in all;
+ * N % 16 == 0).  Decode sizes only (T <= 16, T <= 8 at group size 32; shape
+ * rules of the decode kernel); other shapes return SF_ERR_UNSUPPORTED. */
+int sf_q4_linear_swiglu(const uint8_t* W, const float* scales, const float* zeros,
+                        const float* bias, const void* X, int x_dtype, void* Y, int y_dtype,
+                        int N, int K, int T, int group_size, void* stream);
+/* The same activation applied to an already computed product of the
+ * interleaved rows: in [T, 2N] fp32 (the sf_q4_linear output of those rows,
+ * bias not added), bias [2N] interleaved or NULL, out [T, N] of out_dtype. */
+int sf_swiglu_interleaved(const float* in, void* out, int out_dtype, int T, int N, const float* bias,
+                          void* stream);
 
 /* sf_q4_linear for T <= 16 that allocates nothing.  No counterpart in the
  * reference (its kernels need no device scratch).  sf_q4_linear keeps a

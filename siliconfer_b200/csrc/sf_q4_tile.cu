@@ -76,6 +76,7 @@ namespace {
 // above 8 tokens, still fit in shared memory).
 __host__ __device__ constexpr int tile_kd(int T) { return T > 4 ? 2 : 3; }
 constexpr int kUnitRows = 32;          // rows per unit (two m16 tiles)
+constexpr int kEpiSwiGLU = 1;          // TileTask::epi
 // At most 12 warps per CTA (168 registers per thread); more than 4 tokens
 // doubles the accumulators, and those launches hold at most 8 warps (their
 // stages are larger) with 255 registers per thread.
@@ -149,6 +150,7 @@ struct alignas(64) TileTask {
   //  kind 1: all-reduce of a pushed task: waits for flag[tile][*] >= epoch in
   //          this rank's region, sums the ranks in order (+ bias), writes Y.
   int kind, push, tp_rank, tp_world;
+  int epi;                             // kEpiSwiGLU: interleaved gate/up rows, Y = silu(gate) * up
   size_t xpar;                         // bytes of one parity half of a region's data
   uint8_t* xdata[8];                   // region data of every rank, as mapped here
   unsigned long long* xflag[8];        // region flags of every rank, as mapped here
@@ -297,6 +299,10 @@ __device__ __forceinline__ void st_y(void* y, size_t idx, float v, int dt) {
   else if (dt == SF_F16) reinterpret_cast<__half*>(y)[idx] = __float2half_rn(v);
   else reinterpret_cast<__nv_bfloat16*>(y)[idx] = __float2bfloat16_rn(v);
 }
+
+// SwiGLU activation of the gate: silu(x) = x / (1 + e^-x)
+// (siliconfer/model/layers.py:144, down_proj(silu(gate(x)) * up(x))).
+__device__ __forceinline__ float silu(float x) { return x / (1.f + expf(-x)); }
 
 // D (+)= A(u8, 16x32) * B(s8, 32x8), s32.  Not volatile: no side effects, so
 // the compiler may interleave independent chains.
@@ -887,6 +893,18 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       for (int tg = 0; tg < NG; ++tg) {
         const int tok = tg * 4 + ltok;
         if (dlead && tok < T) {
+          if (p->epi == kEpiSwiGLU) {
+            // rows 0-15 of the tile are gate rows, 16-31 the matching up rows
+            // (m tiles 0 and 1): output row 16 * tile + rloc
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int rg = r0 + rloc[h], ru = r0 + rloc[2 + h];
+              const float gv = acc[0][tg][h] + (p->bias ? __ldg(p->bias + rg) : 0.f);
+              const float uv = acc[1][tg][h] + (p->bias ? __ldg(p->bias + ru) : 0.f);
+              st_y(p->Y, (size_t)tok * (N >> 1) + (tile << 4) + rloc[h], silu(gv) * uv, p->ydt);
+            }
+            continue;
+          }
 #pragma unroll
           for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
@@ -926,7 +944,20 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
         __threadfence();
         if (lane == 0) p->tcnt[tile] = 0;   // ready for the next launch
         const int row = r0 + lane;
-        if (row < N) {
+        if (p->epi == kEpiSwiGLU) {
+          // N is a multiple of 32 here: every lane has a row.  Lane i < 16 holds
+          // gate row 16 * tile + i, lane i + 16 the matching up row.
+          const float bv = p->bias ? __ldg(p->bias + row) : 0.f;
+          for (int tok = 0; tok < T; ++tok) {
+            const float* src = p->part + (size_t)tok * N + row;
+            const size_t kstride = (size_t)T * N;
+            float a = 0.f;
+            for (int kc = 0; kc < ksplit; ++kc) a += __ldcg(src + (size_t)kc * kstride);
+            a += bv;
+            const float up = __shfl_down_sync(0xffffffffu, a, 16);
+            if (lane < 16) st_y(p->Y, (size_t)tok * (N >> 1) + (tile << 4) + lane, silu(a) * up, p->ydt);
+          }
+        } else if (row < N) {
           const float bv = p->bias ? __ldg(p->bias + row) : 0.f;
           for (int tok = 0; tok < T; ++tok) {
             // loads first (eight in flight), then the sum in k order
@@ -1277,13 +1308,15 @@ size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 // SF_ERR_UNSUPPORTED when the shape is not one this kernel takes.
 int run_tile_linear(const uint8_t* W, const float* S, const float* Z, const float* bias,
                     const void* X, int xdt, void* Y, int ydt, int N, int K, int T, int gs,
-                    cudaStream_t stream) {
+                    cudaStream_t stream, int epi) {
   if (T < 1 || T > kMaxGemvT || !shape_ok(N, K, gs)) return SF_ERR_UNSUPPORTED;
+  if (epi == kEpiSwiGLU && N % kUnitRows) return SF_ERR_UNSUPPORTED;
   TileConfig c;
   if (!make_config(T, Z != nullptr, gs, c)) return SF_ERR_UNSUPPORTED;
   TileLaunch L{};
   TileTask& q = L.single;
   q.W = W; q.S = S; q.Z = Z; q.bias = bias; q.X = X; q.Y = Y; q.xdt = xdt; q.ydt = ydt;
+  q.epi = epi;
   const int ntile = (N + kUnitRows - 1) / kUnitRows;
   const int warps = c.grid * c.wpc;
   int rc = fill_task(q, N, K, gs, T, (warps + ntile - 1) / ntile);
@@ -1441,6 +1474,10 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
                   i, a.N, a.K, a.group_size);
     if (a.x_dtype < 0 || a.x_dtype > 2 || a.y_dtype < 0 || a.y_dtype > 2)
       return fail(SF_ERR_DTYPE, "task %d: unknown dtype code", i);
+    if (a.epilogue != 0 && (a.epilogue != SF_EPI_SWIGLU || a.N % kUnitRows || role != SF_ROLE_GEMV))
+      return fail(SF_ERR_UNSUPPORTED,
+                  "task %d: epilogue %d needs SF_EPI_SWIGLU, N (gate + up rows) a multiple of 32 and no exchange "
+                  "role", i, a.epilogue);
     if ((reinterpret_cast<uintptr_t>(a.W) | reinterpret_cast<uintptr_t>(a.scales) |
          reinterpret_cast<uintptr_t>(a.zeros) | reinterpret_cast<uintptr_t>(a.X)) & 15)
       return fail(SF_ERR_ALIGN, "task %d: W, scales, zeros and X must be 16-byte aligned", i);
@@ -1467,6 +1504,7 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
     q = TileTask{};
     q.W = a.W; q.S = a.scales; q.Z = a.zeros; q.bias = a.bias; q.X = a.X; q.Y = a.Y;
     q.xdt = a.x_dtype; q.ydt = a.y_dtype;
+    q.epi = a.epilogue;
     int rc = fill_task(q, a.N, a.K, a.group_size, T, want[i]);
     if (rc != SF_OK) return rc;
     q.tcnt = reinterpret_cast<unsigned int*>(tiles);
@@ -1599,6 +1637,62 @@ void sf_q4_step_destroy(void* handle) { delete static_cast<StepHandle*>(handle);
 
 
 }  // extern "C"
+
+// ===========================================================================
+// SwiGLU on interleaved gate/up weights
+// ===========================================================================
+namespace sf {
+namespace {
+__global__ void swiglu_interleaved_kernel(const float* __restrict__ in, void* out, int ydt, int T, int n_out,
+                                          const float* __restrict__ bias) {
+  const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (i >= (long long)T * n_out) return;
+  const int t = (int)(i / n_out), o = (int)(i - (long long)t * n_out);
+  const int rg = (o >> 4) * 32 + (o & 15), ru = rg + 16;   // interleaved rows of the gate and up halves
+  const float* row = in + (size_t)t * 2 * n_out;
+  const float g = row[rg] + (bias ? bias[rg] : 0.f), u = row[ru] + (bias ? bias[ru] : 0.f);
+  st_y(out, (size_t)i, silu(g) * u, ydt);
+}
+}  // namespace
+}  // namespace sf
+
+extern "C" int sf_q4_linear_swiglu(const uint8_t* W, const float* scales, const float* zeros, const float* bias,
+                                   const void* X, int x_dtype, void* Y, int y_dtype, int N, int K, int T,
+                                   int group_size, void* stream) {
+  if (!W || !scales || !X || !Y) return fail(SF_ERR_NULL, "null pointer argument");
+  if (x_dtype < 0 || x_dtype > 2 || y_dtype < 0 || y_dtype > 2) return fail(SF_ERR_DTYPE, "unknown dtype code");
+  if (N < 0 || K <= 0 || T < 0) return fail(SF_ERR_SHAPE, "invalid N/K/T");
+  if (N % 16) return fail(SF_ERR_SHAPE, "SwiGLU output width N=%d must be a multiple of 16", N);
+  if (group_size <= 0 || group_size % 2 || K % group_size)
+    return fail(SF_ERR_SHAPE, "in_features must be divisible by an even group_size");
+  if (N == 0 || T == 0) return SF_OK;
+  if ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(zeros) |
+       reinterpret_cast<uintptr_t>(X)) & 15)
+    return fail(SF_ERR_ALIGN, "W, scales, zeros and X must be 16-byte aligned");
+  const int rc = run_tile_linear(W, scales, zeros, bias, X, x_dtype, Y, y_dtype, 2 * N, K, T, group_size,
+                                 static_cast<cudaStream_t>(stream), kEpiSwiGLU);
+  if (rc == SF_ERR_UNSUPPORTED)
+    return fail(SF_ERR_UNSUPPORTED,
+                "fused SwiGLU runs on the decode kernel: T <= %d (8 at group size 32), K %% 32 == 0 and a "
+                "power-of-two group_size in 32..256; use sf_q4_linear on the stacked rows and "
+                "sf_swiglu_interleaved", kMaxGemvT);
+  return rc;
+}
+
+extern "C" int sf_swiglu_interleaved(const float* in, void* out, int out_dtype, int T, int N, const float* bias,
+                                     void* stream) {
+  if (!in || !out) return fail(SF_ERR_NULL, "null pointer argument");
+  if (out_dtype < 0 || out_dtype > 2) return fail(SF_ERR_DTYPE, "unknown dtype code");
+  if (T < 0 || N < 0 || N % 16) return fail(SF_ERR_SHAPE, "N=%d must be a multiple of 16", N);
+  const long long n = (long long)T * N;
+  if (n == 0) return SF_OK;
+  swiglu_interleaved_kernel<<<(unsigned)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      in, out, out_dtype, T, N, bias);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "swiglu_interleaved_kernel launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return SF_OK;
+}
 
 // ===========================================================================
 // Decode GEMV without any allocation: the single-GEMV launch above, with its

@@ -83,3 +83,13 @@ def test_kv_attention_validation_without_gpu(args, code, msg):
     assert lib.sf_kv_attention_decode(*args) == code
     assert msg in lib.sf_last_error().decode()
     assert lib.sf_kv_attention_workspace_bytes(2, 8, 64, 4) == 2 * 8 * 4 * 66 * 4
+
+
+def test_swiglu_validation_without_gpu():
+    lib = _lib.load()
+    # N not a multiple of 16
+    assert lib.sf_q4_linear_swiglu(FAKE, FAKE, None, None, FAKE, 0, FAKE, 0, 24, 128, 1, 64, None) == 2
+    assert "multiple of 16" in lib.sf_last_error().decode()
+    assert lib.sf_q4_linear_swiglu(None, FAKE, None, None, FAKE, 0, FAKE, 0, 32, 128, 1, 64, None) == 1
+    assert lib.sf_swiglu_interleaved(FAKE, FAKE, 0, 2, 24, None, None) == 2
+    assert lib.sf_swiglu_interleaved(FAKE, FAKE, 0, 0, 32, None, None) == 0     # empty: nothing launched
