@@ -313,6 +313,7 @@ def run_ours(args, rank, world, local_rank):
     if world == 1 and args.workload == "7b" and not args.no_prefill:
         result["sweep"] = sweep_measure(layers, device, args)
         result["small_configs"] = small_configs_measure(device)
+        result["int2"] = int2_measure(device, args)
         result["prefill"] = prefill_measure(device, runner.stream)
         result["kv_attention"] = kv_attention_measure(device, runner.stream)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -728,6 +729,39 @@ def small_configs_measure(device, iters=20):
         del r, layers
     out["timing"] = "each replay timed alone with CUDA events after a 256 MB buffer write (cold L2)"
     return out
+
+
+def int2_measure(device, args):
+    """2-bit weights (the reference's pack_int2 format, which it cannot serve)
+    on the 7B step: 32 layers x 7 projections, symmetric, group 128, fp16 x,
+    batch 1, one launch.  The 2-bit codes and the scales are drawn at random
+    on the device (the kernel's speed does not depend on their values; its
+    results are checked against the oracle in the tests)."""
+    import torch
+    from siliconfer_b200.q4_linear import Q4Linear
+    from siliconfer_b200.runner import Q4StepRunner
+    peak, peak_kind = measured_peak()
+    gen = torch.Generator(device=device)
+    gen.manual_seed(2)
+    layers = []
+    for _ in range(HIDDEN["7b"][2]):
+        for _, n, k in shapes("7b"):
+            p = torch.randint(0, 256, (n, k // 4), generator=gen, device=device, dtype=torch.uint8)
+            sc = torch.rand((n, k // 128), generator=gen, device=device) * 0.01 + 0.005
+            layers.append(Q4Linear(p, sc, group_size=128, device=device, bits=2))
+    r = Q4StepRunner(layers, tokens=1, x_dtype=torch.float16, y_dtype=torch.float32, device=device,
+                     waits=[False] * len(layers))
+    r.x.normal_()
+    r.capture()
+    with torch.cuda.stream(r.stream):
+        for _ in range(args.warmup):
+            r.graph.replay()
+    ms = _time_replays(r.graph.replay, r.stream, max(5, min(args.steps, 20)))
+    nb = r.algorithmic_bytes()
+    return {"workload": "7B step, 2-bit symmetric weights (pack_int2 layout), group 128, fp16 x, batch 1",
+            "us": round(ms * 1e3, 1), "gbs": round(nb / ms / 1e6, 1), "frac": round(nb / ms / 1e6 / peak, 4),
+            "peak_kind": peak_kind, "bytes": nb, "launches_per_step": r.kernels_per_step,
+            "timing": "CUDA events over back-to-back graph replays (weights 1.8 GB >> L2)"}
 
 
 def prefill_measure(device, stream, iters=20):

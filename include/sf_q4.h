@@ -117,6 +117,8 @@ typedef struct {
   void* Y;              /* [T, N] of y_dtype */
   int N, K, T, group_size, x_dtype, y_dtype, wait_before;
   int epilogue;         /* 0, or SF_EPI_SWIGLU (see sf_q4_linear_swiglu; N = gate + up rows) */
+  int bits;             /* weight bit width: 0 or 4 (packed [N, K/2]), 2 (packed [N, K/4], see
+                           sf_q2_linear); every task of a step has the same */
 } sf_q4_task;
 #define SF_EPI_SWIGLU 1
 size_t sf_q4_step_workspace_bytes(const sf_q4_task* tasks, int ntasks);
@@ -124,6 +126,21 @@ int sf_q4_step_create(const sf_q4_task* tasks, int ntasks, void* workspace, size
                       void** handle_out);
 int sf_q4_step_run(void* handle, void* stream);
 void sf_q4_step_destroy(void* handle);
+
+/* ---- 2-bit weights ------------------------------------------------------
+ * The reference quantizes to 2 bits (siliconfer/quant/primitives.py:154-245,
+ * quantize_sym_int2 / quantize_asym_int2) and packs four values per byte
+ * (pack_int2, primitives.py:383-404: element i in bits 2i..2i+1), but its
+ * loader refuses to serve them (siliconfer/engine/q4_loader.py:142-154: no
+ * int2 kernel).  This is that kernel: W uint8 [N, K/4]; symmetric q in
+ * [-2, 1] (two's complement, zeros NULL) or asymmetric q in [0, 3] with fp32
+ * zeros; y = X @ dequant(W)^T (+ bias), dequant (q - z) * s as in
+ * dequantize_sym_int2 / dequantize_asym_int2 (primitives.py:184-245).
+ * K % 64 == 0 and group_size 128 or 256; any T (the decode kernel, 16
+ * tokens per launch). */
+int sf_q2_linear(const uint8_t* W, const float* scales, const float* zeros, const float* bias,
+                 const void* X, int x_dtype, void* Y, int y_dtype, int N, int K, int T,
+                 int group_size, void* stream);
 
 /* ---- MLP gate/up with the SwiGLU activation fused ------------------------
  * Replaces the gate/up half of siliconfer's MLP.__call__ (siliconfer/model/

@@ -299,3 +299,36 @@ def hqq_quantize_weight(W: np.ndarray, group_size: int = 128, p: float = 0.7,
     _, scale, zero = best
     q = np.clip(np.round(g / scale + zero), 0, qmax)
     return (scale * (q - zero)).reshape(n, k).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# 2-bit weights: the reference quantizes and packs them (primitives.py:154-245,
+# 383-425) but has no kernel for them, so the oracle is its dequant followed
+# by the product, the same arithmetic Q4Linear's gemm paths use for 4 bits.
+# ---------------------------------------------------------------------------
+def unpack_int2(packed: np.ndarray, signed: bool) -> np.ndarray:
+    """[N, K/4] uint8 -> [N, K] (unpack_int2, primitives.py:407-425, row by row)."""
+    p = np.asarray(packed, np.uint8)
+    out = np.empty((p.shape[0], p.shape[1] * 4), np.int32)
+    for i in range(4):
+        out[:, i::4] = (p >> (2 * i)) & 3
+    if signed:
+        out = np.where(out > 1, out - 4, out)
+    return out
+
+
+def dequantize_int2(packed, scales, zeros=None, group_size: int = 128) -> np.ndarray:
+    """(q - z) * s in fp32 (dequantize_sym_int2 / dequantize_asym_int2,
+    primitives.py:184-198, 234-245)."""
+    q = unpack_int2(packed, signed=zeros is None).astype(np.float32)
+    n, k = q.shape
+    g = q.reshape(n, k // group_size, group_size)
+    if zeros is not None:
+        g = g - np.asarray(zeros, np.float32)[..., None]
+    return (g * np.asarray(scales, np.float32)[..., None]).reshape(n, k).astype(np.float32)
+
+
+def gemm_int2(packed, scales, zeros, X, group_size: int = 128) -> np.ndarray:
+    """Y [T, N] = X [T, K] @ dequant(W)^T, fp64 accumulation of the fp32 products."""
+    W = dequantize_int2(packed, scales, zeros, group_size).astype(np.float64)
+    return (np.asarray(X, np.float64) @ W.T).astype(np.float32)

@@ -26,7 +26,7 @@ class Q4Task(ctypes.Structure):
     """Mirror of sf_q4_task (include/sf_q4.h)."""
     _fields_ = [("W", _P), ("scales", _P), ("zeros", _P), ("bias", _P), ("X", _P), ("Y", _P),
                 ("N", _I), ("K", _I), ("T", _I), ("group_size", _I), ("x_dtype", _I),
-                ("y_dtype", _I), ("wait_before", _I), ("epilogue", _I)]
+                ("y_dtype", _I), ("wait_before", _I), ("epilogue", _I), ("bits", _I)]
 
 # name -> argtypes (restype is int unless listed in _RESTYPES)
 SIGNATURES = {
@@ -41,6 +41,7 @@ SIGNATURES = {
     "sf_q4_linear": [_P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _P],
     "sf_q4_linear_static_scratch": [_P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P],
     "sf_q4_linear_swiglu": [_P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P],
+    "sf_q2_linear": [_P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P],
     "sf_swiglu_interleaved": [_P, _P, _I, _I, _I, _P, _P],
     "sf_q4_dequant": [_P, _P, _P, _P, _I, _I, _I, _I, _P],
     "sf_q4_quantize_pack": [_P, _P, _P, _P, _I, _I, _I, _P],

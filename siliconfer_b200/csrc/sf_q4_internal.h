@@ -77,9 +77,10 @@ int tp_region(void* comm, size_t src_bytes, size_t tiles, uint8_t** data, unsign
 // when the shape is not one it takes.
 // epi = 1 (SwiGLU): W holds interleaved gate/up rows (16 of each per 32), N
 // counts both, and Y [T, N/2] = silu(gate) * up.
+// bits = 2: W holds 2-bit weights, 4 per byte ([N, K/4]).
 int run_tile_linear(const uint8_t* W, const float* S, const float* Z, const float* bias,
                     const void* X, int xdt, void* Y, int ydt, int N, int K, int T, int gs,
-                    cudaStream_t stream, int epi = 0);
+                    cudaStream_t stream, int epi = 0, int bits = 4);
 
 // ---------------------------------------------------------------------------
 // Launch helper: optional programmatic dependent launch (PDL).

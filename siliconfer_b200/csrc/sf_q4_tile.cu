@@ -91,10 +91,11 @@ __host__ __device__ constexpr int xblock_bytes(int T, int LB) { return (T * (24 
 
 // Shared memory of a CTA: first the weight stages of every warp (1024-byte
 // aligned, as the 128-byte TMA swizzle needs), then each warp's other areas.
-// One stage = 32 rows x 128 bytes of W (256 k) = SPS k-segments of 8*LB k.
-template <int T, bool ASYM, int LB>
+// One stage = 32 rows x 128 bytes of W (256 k at 4 bits, 512 k at 2 bits) =
+// SPS k-segments of 8*LB k (LB: activation bytes per lane and digit).
+template <int T, bool ASYM, int LB, int BITS>
 struct TileLayout {
-  static constexpr int SPS = 128 / (4 * LB);            // k-segments per stage
+  static constexpr int SPS = 128 / (LB * BITS);         // k-segments per stage
   static constexpr int XB = xblock_bytes(T, LB);         // activation block of one segment
   static constexpr int ASTAGE = 32 * 128;                // weight tile of one stage
   static constexpr int SBW = LB == 4 ? 8 : 4;            // groups in one stage's scale box
@@ -166,6 +167,7 @@ struct TileLaunch {
   unsigned long long* epoch;   // last finished launch (tensor-parallel exchange epoch), or null
   unsigned int* done;          // CTAs finished (step launches: the last one resets the counters), or null
   const unsigned int* cmap;    // per phase, its conversion chunks in order: (task << 16) | chunk of the task
+  const long long* ubase;      // first unit of every task, compact (read through L1), or null: single task
   int nphase;                  // phases of the step (phctr has 4 words per phase)
   unsigned long long* poison;  // the communicator's sticky poison word (tensor-parallel steps), or null
 };
@@ -329,6 +331,12 @@ template <bool ASYM>
 __device__ __forceinline__ uint32_t nib_hi(uint32_t w) {
   return ((w >> 4) & 0x0F0F0F0Fu) ^ (ASYM ? 0u : 0x08080808u);
 }
+// 2-bit field f (0..3) of each byte as unsigned bytes; the symmetric layout's
+// two's-complement q in [-2, 1] becomes q + 2 (flip of the field's top bit).
+template <bool ASYM>
+__device__ __forceinline__ uint32_t fld2(uint32_t w, int f) {
+  return ((w >> (2 * f)) & 0x03030303u) ^ (ASYM ? 0u : 0x02020202u);
+}
 
 // Low bytes of d[0..7] in B-operand order: word 0 = k offsets {0,2,4,6},
 // word 1 = {1,3,5,7} (matching the low / high nibbles of the A operand).
@@ -342,9 +350,9 @@ __device__ __forceinline__ uint2 pack_digits(const int* d) {
 }
 
 // Fixed-point digit split of 8 activations of one lane; lanes in aligned
-// blocks of `lpg` form one quantization group.
-__device__ __forceinline__ void digits8(const float* v, int lpg, uint2* dig, float& gsc_out,
-                                        int& sum_out) {
+// blocks of `lpg` form one quantization group.  d[i][j]: digit i of input j.
+__device__ __forceinline__ void digits8_raw(const float* v, int lpg, int (&d)[3][8], float& gsc_out,
+                                            int& sum_out) {
   float m = 0.f;
   int bad = 0;
 #pragma unroll
@@ -362,7 +370,6 @@ __device__ __forceinline__ void digits8(const float* v, int lpg, uint2* dig, flo
   const int be = (int)(__float_as_uint(m) >> 23);
   const bool zero = bad || be < 22;
   const float scl = zero ? 0.f : __uint_as_float((uint32_t)(275 - be) << 23);   // 2^(148-be)
-  int d[3][8];
   int s = 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -376,9 +383,6 @@ __device__ __forceinline__ void digits8(const float* v, int lpg, uint2* dig, flo
     d[2][j] = (r1 - d1) >> 8;
   }
   for (int off = 1; off < lpg; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  dig[0] = pack_digits(d[0]);
-  dig[1] = pack_digits(d[1]);
-  dig[2] = pack_digits(d[2]);
   gsc_out = bad ? __int_as_float(0x7fc00000)
                 : (zero ? 0.f : __uint_as_float((uint32_t)(be - 21) << 23));   // 2^(be-148)
   sum_out = s;
@@ -386,7 +390,15 @@ __device__ __forceinline__ void digits8(const float* v, int lpg, uint2* dig, flo
 
 // Converts chunk `c` (32 consecutive octets of the [T][K] input) of a task
 // into its activation blocks.  Called by a whole warp.
-template <int T, int LB>
+//
+// Byte order of a lane's digits (each 8-byte run = one MMA k-step's two B
+// words), matching how the kernel unpacks the packed weights:
+//  * 4 bits: octet j (k 8j .. 8j+7) -> words {0,2,4,6}, {1,3,5,7} (the low and
+//    high nibbles of 4 packed bytes);
+//  * 2 bits: a 16-k block (octets 2q, 2q+1) -> 4 words, word r = k {r, r+4,
+//    r+8, r+12} (the 2-bit field r of 4 packed bytes); the two lanes of a
+//    block swap half-words and write 8 bytes each.
+template <int T, int LB, int BITS>
 __device__ __forceinline__ void convert_chunk(const TileTask* p, int c, int lane) {
   constexpr int SEGK = 8 * LB, XB = xblock_bytes(T, LB);
   const int K = p->K, lg2gs = p->lg2gs;
@@ -406,7 +418,30 @@ __device__ __forceinline__ void convert_chunk(const TileTask* p, int c, int lane
   uint2 dig[ND];
   float gsc;
   int s;
-  digits8(v, lpg, dig, gsc, s);
+  {
+    int d[3][8];
+    digits8_raw(v, lpg, d, gsc, s);
+    if constexpr (BITS == 4) {
+#pragma unroll
+      for (int i = 0; i < ND; ++i) dig[i] = pack_digits(d[i]);
+    } else {
+      const bool odd = (lane & 1) != 0;   // second octet of a 16-k block
+#pragma unroll
+      for (int i = 0; i < ND; ++i) {
+        uint32_t hw[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) hw[r] = (uint32_t)(d[i][r] & 255) | ((uint32_t)(d[i][4 + r] & 255) << 8);
+        // the even lane keeps words 0-1 and sends 2-3, the odd lane the reverse
+        const uint32_t mine0 = odd ? (hw[2] | hw[3] << 16) : (hw[0] | hw[1] << 16);
+        const uint32_t send = odd ? (hw[0] | hw[1] << 16) : (hw[2] | hw[3] << 16);
+        const uint32_t got = __shfl_xor_sync(0xffffffffu, send, 1);
+        // word r = [k r, r+4 from the even lane][k r+8, r+12 from the odd lane]
+        const uint32_t lo = odd ? got : mine0, hi = odd ? mine0 : got;
+        dig[i].x = (lo & 0xFFFFu) | (hi << 16);
+        dig[i].y = (lo >> 16) | (hi & 0xFFFF0000u);
+      }
+    }
+  }
   if (!ok) return;
   const int k0 = oo * 8;
   const int seg = k0 / SEGK, within = k0 - seg * SEGK;
@@ -475,15 +510,17 @@ __device__ __forceinline__ void tile_written(const TileLaunch& L, const TileTask
 // ---------------------------------------------------------------------------
 // The GEMV kernel
 // ---------------------------------------------------------------------------
-template <int T, bool ASYM, int LB>
+template <int T, bool ASYM, int LB, int BITS>
 __global__ void __launch_bounds__(tile_max_threads(T), 1)
     q4_tile_kernel(const __grid_constant__ TileLaunch L) {
-  using Ly = TileLayout<T, ASYM, LB>;
+  using Ly = TileLayout<T, ASYM, LB, BITS>;
   // CMP (T <= 2): one n tile, token t in columns 4t .. 4t + 3 (digits 0-2, empty);
   // else NG groups of 4 tokens, n tiles (2i, 2i + 1) = digits (0, 1) and 2 of group i
   constexpr bool CMP = T <= 2;
   constexpr int ND = 3, NG = CMP ? 1 : (T + 3) / 4, NT = CMP ? 1 : 2 * NG;
   constexpr int WPL = LB / 4, SEGK = 8 * LB, SPS = Ly::SPS, PS = tile_pair(T);
+  constexpr int LBA = LB * BITS / 4;             // packed weight bytes of a lane's row slice per segment
+  constexpr int KST = SPS * SEGK;                // k of one stage (128 bytes of every row)
   constexpr int GOFF = T * 8 * ND * LB;          // group scales / sums inside a segment's block
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -538,7 +575,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     rloc[i] = (i >> 1) * 16 + lane_row(g, LB) + 8 * (i & 1);
 #pragma unroll
     for (int sub = 0; sub < SPS; ++sub) {
-      const int b = sub * 4 * LB + t * LB;   // byte of the row this lane reads for segment `sub`
+      const int b = sub * 4 * LBA + t * LBA;   // byte of the row this lane reads for segment `sub`
       aoff[i][sub] = (uint32_t)(rloc[i] * 128 + ((((b >> 4) ^ (rloc[i] & 7)) << 4) | (b & 15)));
     }
   }
@@ -565,7 +602,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
   bool ok = true;
 
   for (long long u = (long long)warp * gridDim.x + blockIdx.x; u < L.total && ok; u += W_all) {
-    while (ti + 1 < L.ntasks && u >= tile_task(L, ti + 1)->ubase) ++ti;
+    while (ti + 1 < L.ntasks && u >= __ldg(L.ubase + ti + 1)) ++ti;
     const TileTask* p = tile_task(L, ti);
     const int N = p->N, K = p->K, G = p->G, lg2gs = p->lg2gs, ntile = p->ntile;
     const int ksplit = p->ksplit, kper = p->kper, stma = p->stma;
@@ -602,7 +639,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       islot = islot + 1 == (uint32_t)kD ? 0u : islot + 1;
       const uint32_t bar = bar0 + slot * 8;
       const int nsub = min(SPS, nseg - j * SPS);
-      const int fg = (kb + j * 256) >> lg2gs;                   // first group of the stage
+      const int fg = (kb + j * KST) >> lg2gs;                   // first group of the stage
       // scale box origin: TMA boxes start on SBW-group boundaries (units are
       // cut in whole boxes, so the stage's groups stay inside); per-lane
       // copies start at the stage's first group
@@ -629,7 +666,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       if (lane == 0) {
         const uint32_t sbytes = stma ? (uint32_t)Ly::SBYTES * (ASYM ? 2 : 1) : 0u;
         bar_expect_tx(bar, (uint32_t)Ly::ASTAGE + nsub * Ly::XB + sbytes);
-        tma_2d(astage0 + slot * Ly::ASTAGE, &p->tmW, (kb >> 1) + j * 128, r0, bar);
+        tma_2d(astage0 + slot * Ly::ASTAGE, &p->tmW, (kb * BITS >> 3) + j * 128, r0, bar);
         if (stma) {
           tma_2d(sstage0 + slot * Ly::SBYTES, &p->tmS, sx, r0, bar);
           if (ASYM) tma_2d(zstage0 + slot * Ly::SBYTES, &p->tmZ, sx, r0, bar);
@@ -684,7 +721,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
         int n = 0;
         for (long long c = i; c < p->ph_chunks; c += CS) {
           const unsigned int e = __ldg(L.cmap + p->ph_cbase + c);
-          convert_chunk<T, LB>(tile_task(L, (int)(e >> 16)), (int)(e & 0xFFFFu), lane);
+          convert_chunk<T, LB, BITS>(tile_task(L, (int)(e >> 16)), (int)(e & 0xFFFFu), lane);
           ++n;
         }
         asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -777,7 +814,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
         for (int h = 0; h < 2; ++h) {
           const int r = rloc[2 * mt + h];
           sc[mt][h] = __uint_as_float(lds32(sst + r * (Ly::SBW * 4) + soff));
-          zp[mt][h] = ASYM ? __uint_as_float(lds32(zst + r * (Ly::SBW * 4) + soff)) : 8.f;
+          zp[mt][h] = ASYM ? __uint_as_float(lds32(zst + r * (Ly::SBW * 4) + soff)) : (BITS == 4 ? 8.f : 2.f);
         }
 #pragma unroll
       for (int tg = 0; tg < NG; ++tg) {
@@ -812,7 +849,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
         cslot = 0;
         cpar ^= 1u;
       }
-      const int fgj = (kb + j * 256) >> lg2gs;
+      const int fgj = (kb + j * KST) >> lg2gs;
       const int sx = stma ? (fgj & ~(Ly::SBW - 1)) : fgj;
       // The stage's segments are taken in pairs (PS = 2) with one accumulator
       // set each, so that the two halves' loads, nibble splits and MMAs
@@ -823,13 +860,13 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       for (int pr = 0; pr < SPS; pr += PS) {
         const int s0 = j * SPS + pr;
         if (s0 >= nseg) break;
-        uint32_t w[PS][4][WPL];
+        uint32_t w[PS][4][LBA / 4];
         uint32_t bq[PS][NT][2 * WPL];
 #pragma unroll
         for (int h2 = 0; h2 < PS; ++h2) {
           const uint32_t xs0 = xst + (pr + h2) * Ly::XB;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) lds_n<LB>(ast + aoff[i][pr + h2], w[h2][i]);
+          for (int i = 0; i < 4; ++i) lds_n<LBA>(ast + aoff[i][pr + h2], w[h2][i]);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) lds_n<2 * LB>(bval[nt] ? xs0 + bslot[nt] : zblk, bq[h2][nt]);
         }
@@ -839,8 +876,20 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
           for (int h2 = 0; h2 < PS; ++h2)
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
-              const uint32_t a0 = nib_lo<ASYM>(w[h2][2 * mt][q]), a2 = nib_hi<ASYM>(w[h2][2 * mt][q]);
-              const uint32_t a1 = nib_lo<ASYM>(w[h2][2 * mt + 1][q]), a3 = nib_hi<ASYM>(w[h2][2 * mt + 1][q]);
+              uint32_t a0, a1, a2, a3;
+              if constexpr (BITS == 4) {
+                a0 = nib_lo<ASYM>(w[h2][2 * mt][q]);
+                a2 = nib_hi<ASYM>(w[h2][2 * mt][q]);
+                a1 = nib_lo<ASYM>(w[h2][2 * mt + 1][q]);
+                a3 = nib_hi<ASYM>(w[h2][2 * mt + 1][q]);
+              } else {
+                // 2-bit fields 2f, 2f + 1 of packed word q / 2 (16 weights)
+                const int f = 2 * (q & 1);
+                a0 = fld2<ASYM>(w[h2][2 * mt][q >> 1], f);
+                a2 = fld2<ASYM>(w[h2][2 * mt][q >> 1], f + 1);
+                a1 = fld2<ASYM>(w[h2][2 * mt + 1][q >> 1], f);
+                a3 = fld2<ASYM>(w[h2][2 * mt + 1][q >> 1], f + 1);
+              }
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt) {
                 if (q == 0) imma0(C[h2][mt][nt], a0, a1, a2, a3, bq[h2][nt][0], bq[h2][nt][1]);
@@ -1006,14 +1055,14 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
 }
 
 // Activation blocks of the tasks whose input exists at launch: one CTA per task.
-template <int T, int LB>
+template <int T, int LB, int BITS>
 __global__ void __launch_bounds__(256) q4_xblocks_kernel(const __grid_constant__ TileLaunch L) {
   const TileTask* p = tile_task(L, blockIdx.x);
   if (!p->xpre) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // blockIdx.y spreads one task's chunks over several CTAs
   const int wpb = blockDim.x >> 5;
-  for (int c = blockIdx.y * wpb + warp; c < p->nchunk; c += gridDim.y * wpb) convert_chunk<T, LB>(p, c, lane);
+  for (int c = blockIdx.y * wpb + warp; c < p->nchunk; c += gridDim.y * wpb) convert_chunk<T, LB, BITS>(p, c, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -1021,16 +1070,12 @@ __global__ void __launch_bounds__(256) q4_xblocks_kernel(const __grid_constant__
 // ---------------------------------------------------------------------------
 namespace {
 
-int env_int(const char* name, int dflt) {
-  const char* v = getenv(name);
-  return v && *v ? atoi(v) : dflt;
-}
 
 int lb_for(int gs) { return (gs % 128 == 0) ? 16 : (gs % 64 == 0 ? 8 : 4); }
 
-// Shared bytes per warp: TileLayout<T, ASYM, LB>::WARP.
-int warp_bytes(int T, bool asym, int LB) {
-  const int sps = 128 / (4 * LB), sbw = LB == 4 ? 8 : 4, kD = tile_kd(T);
+// Shared bytes per warp: TileLayout<T, ASYM, LB, BITS>::WARP.
+int warp_bytes(int T, bool asym, int LB, int bits) {
+  const int sps = 128 / (LB * bits), sbw = LB == 4 ? 8 : 4, kD = tile_kd(T);
   const int xstage = (sps * xblock_bytes(T, LB) + 127) & ~127;
   return kD * 32 * 128 + 128 + kD * xstage + kD * 32 * sbw * 4 * (asym ? 2 : 1);
 }
@@ -1041,25 +1086,29 @@ size_t xblocks_bytes(int T, int K, int gs) {
 }
 
 struct TileConfig {
-  int T, LB, wpc, grid;
+  int T, LB, bits, wpc, grid;
   bool asym;
   size_t smem;
 };
 
-bool shape_ok(int N, int K, int gs) {
-  return N >= 1 && K % 32 == 0 && gs >= 32 && gs <= 256 && (gs & (gs - 1)) == 0 && K % gs == 0;
+// Shapes of the decode kernel.  4 bits: K % 32, group size a power of two in
+// 32..256.  2 bits: K % 64 (16-byte rows for TMA), group size 128 or 256.
+bool shape_ok(int N, int K, int gs, int bits = 4) {
+  if (bits == 2) return N >= 1 && K % 64 == 0 && (gs == 128 || gs == 256) && K % gs == 0;
+  return bits == 4 && N >= 1 && K % 32 == 0 && gs >= 32 && gs <= 256 && (gs & (gs - 1)) == 0 && K % gs == 0;
 }
 
-bool make_config(int T, bool asym, int gs, TileConfig& c) {
+constexpr int kTileWarps = 12;   // warps per CTA at most (fewer when shared memory runs out)
+
+bool make_config(int T, bool asym, int gs, TileConfig& c, int bits = 4) {
   const DeviceInfo& di = device_info();
-  c.T = T; c.asym = asym; c.LB = lb_for(gs);
+  c.T = T; c.asym = asym; c.LB = lb_for(gs); c.bits = bits;
   if (T < 1 || T > kMaxGemvT || (T > 8 && c.LB == 4)) return false;   // 9-16 tokens need group size >= 64
-  const size_t per_warp = (size_t)warp_bytes(T, asym, c.LB);
-  size_t cap = (size_t)env_int("SF_TILE_SMEM_KB", 227) * 1024;
-  if (cap > (size_t)di.smem_optin) cap = (size_t)di.smem_optin;
+  if (bits == 2 && c.LB != 16) return false;
+  const size_t per_warp = (size_t)warp_bytes(T, asym, c.LB, bits);
+  const size_t cap = (size_t)di.smem_optin;
   int wpc = (int)(cap / per_warp);
-  const int want = env_int("SF_TILE_WARPS", 12);
-  if (wpc > want) wpc = want;
+  if (wpc > kTileWarps) wpc = kTileWarps;
   if (wpc > tile_max_threads(T) / 32) wpc = tile_max_threads(T) / 32;
   // whole multiples of the 4 schedulers: an odd warp would carry a 3-warp
   // scheduler and, since every warp gets the same share of units, slow all
@@ -1112,7 +1161,7 @@ int groups_per_unit(int G, long long want, bool stma, int gs) {
 }
 
 // Fills the shape fields and the tensor maps of a task (W, S, Z set).
-int fill_task(TileTask& q, int N, int K, int gs, int T, long long ksplit_want) {
+int fill_task(TileTask& q, int N, int K, int gs, int T, long long ksplit_want, int bits = 4) {
   const int LB = lb_for(gs);
   q.N = N; q.K = K; q.G = K / gs; q.lg2gs = __builtin_ctz((unsigned)gs);
   q.ntile = (N + kUnitRows - 1) / kUnitRows;
@@ -1123,7 +1172,8 @@ int fill_task(TileTask& q, int N, int K, int gs, int T, long long ksplit_want) {
   q.ksplit = (G + gper - 1) / gper;
   q.nchunk = (T * (K / 8) + 31) / 32;
   (void)LB;
-  if (!make_map(&q.tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, q.W, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+  const uint64_t row_bytes = (uint64_t)K * bits / 8;
+  if (!make_map(&q.tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, q.W, row_bytes, (uint64_t)N, row_bytes,
                 128, kUnitRows, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(SF_ERR_CUDA, "cuTensorMapEncodeTiled failed for the weights (N=%d K=%d)", N, K);
   if (q.stma) {
@@ -1138,10 +1188,10 @@ int fill_task(TileTask& q, int N, int K, int gs, int T, long long ksplit_want) {
   return SF_OK;
 }
 
-template <int T, bool ASYM, int LB>
+template <int T, bool ASYM, int LB, int BITS>
 cudaError_t launch_tile_t(const TileConfig& c, const TileLaunch& L, bool coop, cudaStream_t st) {
-  auto* fn = q4_tile_kernel<T, ASYM, LB>;
-  if (warp_bytes(T, ASYM, LB) != TileLayout<T, ASYM, LB>::WARP) return cudaErrorInvalidConfiguration;
+  auto* fn = q4_tile_kernel<T, ASYM, LB, BITS>;
+  if (warp_bytes(T, ASYM, LB, BITS) != TileLayout<T, ASYM, LB, BITS>::WARP) return cudaErrorInvalidConfiguration;
   static int configured[kMaxDevices] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1163,29 +1213,29 @@ cudaError_t launch_tile_t(const TileConfig& c, const TileLaunch& L, bool coop, c
   return cudaLaunchKernelEx(&cfg, fn, L);
 }
 
-template <bool ASYM, int LB>
+template <bool ASYM, int LB, int BITS>
 cudaError_t launch_tile_lb(const TileConfig& c, const TileLaunch& L, bool coop, cudaStream_t st) {
   switch (c.T) {
-    case 1: return launch_tile_t<1, ASYM, LB>(c, L, coop, st);
-    case 2: return launch_tile_t<2, ASYM, LB>(c, L, coop, st);
-    case 3: return launch_tile_t<3, ASYM, LB>(c, L, coop, st);
-    case 4: return launch_tile_t<4, ASYM, LB>(c, L, coop, st);
-    case 5: return launch_tile_t<5, ASYM, LB>(c, L, coop, st);
-    case 6: return launch_tile_t<6, ASYM, LB>(c, L, coop, st);
-    case 7: return launch_tile_t<7, ASYM, LB>(c, L, coop, st);
-    case 8: return launch_tile_t<8, ASYM, LB>(c, L, coop, st);
+    case 1: return launch_tile_t<1, ASYM, LB, BITS>(c, L, coop, st);
+    case 2: return launch_tile_t<2, ASYM, LB, BITS>(c, L, coop, st);
+    case 3: return launch_tile_t<3, ASYM, LB, BITS>(c, L, coop, st);
+    case 4: return launch_tile_t<4, ASYM, LB, BITS>(c, L, coop, st);
+    case 5: return launch_tile_t<5, ASYM, LB, BITS>(c, L, coop, st);
+    case 6: return launch_tile_t<6, ASYM, LB, BITS>(c, L, coop, st);
+    case 7: return launch_tile_t<7, ASYM, LB, BITS>(c, L, coop, st);
+    case 8: return launch_tile_t<8, ASYM, LB, BITS>(c, L, coop, st);
     default: break;
   }
   if constexpr (LB != 4) {   // 9-16 tokens: group sizes of 64 and more
     switch (c.T) {
-      case 9: return launch_tile_t<9, ASYM, LB>(c, L, coop, st);
-      case 10: return launch_tile_t<10, ASYM, LB>(c, L, coop, st);
-      case 11: return launch_tile_t<11, ASYM, LB>(c, L, coop, st);
-      case 12: return launch_tile_t<12, ASYM, LB>(c, L, coop, st);
-      case 13: return launch_tile_t<13, ASYM, LB>(c, L, coop, st);
-      case 14: return launch_tile_t<14, ASYM, LB>(c, L, coop, st);
-      case 15: return launch_tile_t<15, ASYM, LB>(c, L, coop, st);
-      case 16: return launch_tile_t<16, ASYM, LB>(c, L, coop, st);
+      case 9: return launch_tile_t<9, ASYM, LB, BITS>(c, L, coop, st);
+      case 10: return launch_tile_t<10, ASYM, LB, BITS>(c, L, coop, st);
+      case 11: return launch_tile_t<11, ASYM, LB, BITS>(c, L, coop, st);
+      case 12: return launch_tile_t<12, ASYM, LB, BITS>(c, L, coop, st);
+      case 13: return launch_tile_t<13, ASYM, LB, BITS>(c, L, coop, st);
+      case 14: return launch_tile_t<14, ASYM, LB, BITS>(c, L, coop, st);
+      case 15: return launch_tile_t<15, ASYM, LB, BITS>(c, L, coop, st);
+      case 16: return launch_tile_t<16, ASYM, LB, BITS>(c, L, coop, st);
       default: break;
     }
   }
@@ -1193,39 +1243,43 @@ cudaError_t launch_tile_lb(const TileConfig& c, const TileLaunch& L, bool coop, 
 }
 
 cudaError_t launch_tile(const TileConfig& c, const TileLaunch& L, bool coop, cudaStream_t st) {
-  if (c.asym) {
-    if (c.LB == 16) return launch_tile_lb<true, 16>(c, L, coop, st);
-    if (c.LB == 8) return launch_tile_lb<true, 8>(c, L, coop, st);
-    return launch_tile_lb<true, 4>(c, L, coop, st);
+  if (c.bits == 2) {   // 2-bit weights: group sizes 128 and 256 only
+    if (c.LB != 16) return cudaErrorInvalidValue;
+    return c.asym ? launch_tile_lb<true, 16, 2>(c, L, coop, st) : launch_tile_lb<false, 16, 2>(c, L, coop, st);
   }
-  if (c.LB == 16) return launch_tile_lb<false, 16>(c, L, coop, st);
-  if (c.LB == 8) return launch_tile_lb<false, 8>(c, L, coop, st);
-  return launch_tile_lb<false, 4>(c, L, coop, st);
+  if (c.asym) {
+    if (c.LB == 16) return launch_tile_lb<true, 16, 4>(c, L, coop, st);
+    if (c.LB == 8) return launch_tile_lb<true, 8, 4>(c, L, coop, st);
+    return launch_tile_lb<true, 4, 4>(c, L, coop, st);
+  }
+  if (c.LB == 16) return launch_tile_lb<false, 16, 4>(c, L, coop, st);
+  if (c.LB == 8) return launch_tile_lb<false, 8, 4>(c, L, coop, st);
+  return launch_tile_lb<false, 4, 4>(c, L, coop, st);
 }
 
-template <int LB>
+template <int LB, int BITS>
 cudaError_t launch_xblocks_lb(int T, int ntasks, const TileLaunch& L, cudaStream_t st, int ny) {
   const dim3 grid((unsigned)ntasks, (unsigned)(ny < 1 ? 1 : ny));
   switch (T) {
-    case 1: q4_xblocks_kernel<1, LB><<<grid, 256, 0, st>>>(L); break;
-    case 2: q4_xblocks_kernel<2, LB><<<grid, 256, 0, st>>>(L); break;
-    case 3: q4_xblocks_kernel<3, LB><<<grid, 256, 0, st>>>(L); break;
-    case 4: q4_xblocks_kernel<4, LB><<<grid, 256, 0, st>>>(L); break;
-    case 5: q4_xblocks_kernel<5, LB><<<grid, 256, 0, st>>>(L); break;
-    case 6: q4_xblocks_kernel<6, LB><<<grid, 256, 0, st>>>(L); break;
-    case 7: q4_xblocks_kernel<7, LB><<<grid, 256, 0, st>>>(L); break;
-    case 8: q4_xblocks_kernel<8, LB><<<grid, 256, 0, st>>>(L); break;
+    case 1: q4_xblocks_kernel<1, LB, BITS><<<grid, 256, 0, st>>>(L); break;
+    case 2: q4_xblocks_kernel<2, LB, BITS><<<grid, 256, 0, st>>>(L); break;
+    case 3: q4_xblocks_kernel<3, LB, BITS><<<grid, 256, 0, st>>>(L); break;
+    case 4: q4_xblocks_kernel<4, LB, BITS><<<grid, 256, 0, st>>>(L); break;
+    case 5: q4_xblocks_kernel<5, LB, BITS><<<grid, 256, 0, st>>>(L); break;
+    case 6: q4_xblocks_kernel<6, LB, BITS><<<grid, 256, 0, st>>>(L); break;
+    case 7: q4_xblocks_kernel<7, LB, BITS><<<grid, 256, 0, st>>>(L); break;
+    case 8: q4_xblocks_kernel<8, LB, BITS><<<grid, 256, 0, st>>>(L); break;
     default:
       if constexpr (LB != 4) {
         switch (T) {
-          case 9: q4_xblocks_kernel<9, LB><<<grid, 256, 0, st>>>(L); break;
-          case 10: q4_xblocks_kernel<10, LB><<<grid, 256, 0, st>>>(L); break;
-          case 11: q4_xblocks_kernel<11, LB><<<grid, 256, 0, st>>>(L); break;
-          case 12: q4_xblocks_kernel<12, LB><<<grid, 256, 0, st>>>(L); break;
-          case 13: q4_xblocks_kernel<13, LB><<<grid, 256, 0, st>>>(L); break;
-          case 14: q4_xblocks_kernel<14, LB><<<grid, 256, 0, st>>>(L); break;
-          case 15: q4_xblocks_kernel<15, LB><<<grid, 256, 0, st>>>(L); break;
-          case 16: q4_xblocks_kernel<16, LB><<<grid, 256, 0, st>>>(L); break;
+          case 9: q4_xblocks_kernel<9, LB, BITS><<<grid, 256, 0, st>>>(L); break;
+          case 10: q4_xblocks_kernel<10, LB, BITS><<<grid, 256, 0, st>>>(L); break;
+          case 11: q4_xblocks_kernel<11, LB, BITS><<<grid, 256, 0, st>>>(L); break;
+          case 12: q4_xblocks_kernel<12, LB, BITS><<<grid, 256, 0, st>>>(L); break;
+          case 13: q4_xblocks_kernel<13, LB, BITS><<<grid, 256, 0, st>>>(L); break;
+          case 14: q4_xblocks_kernel<14, LB, BITS><<<grid, 256, 0, st>>>(L); break;
+          case 15: q4_xblocks_kernel<15, LB, BITS><<<grid, 256, 0, st>>>(L); break;
+          case 16: q4_xblocks_kernel<16, LB, BITS><<<grid, 256, 0, st>>>(L); break;
           default: return cudaErrorInvalidValue;
         }
       } else {
@@ -1237,11 +1291,12 @@ cudaError_t launch_xblocks_lb(int T, int ntasks, const TileLaunch& L, cudaStream
 
 // ny: CTAs per task (each converts every ny-th run of 8 chunks); chunks per
 // task = T*K/256, so ny = ceil(chunks / 8) gives every warp one chunk.
-cudaError_t launch_xblocks(int T, int LB, int ntasks, const TileLaunch& L, cudaStream_t st, int ny) {
+cudaError_t launch_xblocks(int T, int LB, int ntasks, const TileLaunch& L, cudaStream_t st, int ny, int bits = 4) {
   if (ny > 64) ny = 64;
-  if (LB == 16) return launch_xblocks_lb<16>(T, ntasks, L, st, ny);
-  if (LB == 8) return launch_xblocks_lb<8>(T, ntasks, L, st, ny);
-  return launch_xblocks_lb<4>(T, ntasks, L, st, ny);
+  if (bits == 2) return LB == 16 ? launch_xblocks_lb<16, 2>(T, ntasks, L, st, ny) : cudaErrorInvalidValue;
+  if (LB == 16) return launch_xblocks_lb<16, 4>(T, ntasks, L, st, ny);
+  if (LB == 8) return launch_xblocks_lb<8, 4>(T, ntasks, L, st, ny);
+  return launch_xblocks_lb<4, 4>(T, ntasks, L, st, ny);
 }
 
 // Library-owned scratch of the single-GEMV entry, one pair of buffers per
@@ -1308,18 +1363,18 @@ size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 // SF_ERR_UNSUPPORTED when the shape is not one this kernel takes.
 int run_tile_linear(const uint8_t* W, const float* S, const float* Z, const float* bias,
                     const void* X, int xdt, void* Y, int ydt, int N, int K, int T, int gs,
-                    cudaStream_t stream, int epi) {
-  if (T < 1 || T > kMaxGemvT || !shape_ok(N, K, gs)) return SF_ERR_UNSUPPORTED;
+                    cudaStream_t stream, int epi, int bits) {
+  if (T < 1 || T > kMaxGemvT || !shape_ok(N, K, gs, bits)) return SF_ERR_UNSUPPORTED;
   if (epi == kEpiSwiGLU && N % kUnitRows) return SF_ERR_UNSUPPORTED;
   TileConfig c;
-  if (!make_config(T, Z != nullptr, gs, c)) return SF_ERR_UNSUPPORTED;
+  if (!make_config(T, Z != nullptr, gs, c, bits)) return SF_ERR_UNSUPPORTED;
   TileLaunch L{};
   TileTask& q = L.single;
   q.W = W; q.S = S; q.Z = Z; q.bias = bias; q.X = X; q.Y = Y; q.xdt = xdt; q.ydt = ydt;
   q.epi = epi;
   const int ntile = (N + kUnitRows - 1) / kUnitRows;
   const int warps = c.grid * c.wpc;
-  int rc = fill_task(q, N, K, gs, T, (warps + ntile - 1) / ntile);
+  int rc = fill_task(q, N, K, gs, T, (warps + ntile - 1) / ntile, bits);
   if (rc != SF_OK) return rc;
   const size_t cbytes = align256((size_t)q.ntile * 4);
   const size_t pbytes = q.ksplit > 1 ? align256((size_t)q.ksplit * T * N * 4) : 0;
@@ -1341,7 +1396,7 @@ int run_tile_linear(const uint8_t* W, const float* S, const float* Z, const floa
   L.flags = nullptr;
   const int need = (int)((L.total + c.wpc - 1) / c.wpc);
   if (c.grid > need) c.grid = need;
-  cudaError_t e = launch_xblocks(T, c.LB, 1, L, stream, (q.nchunk + 7) / 8);
+  cudaError_t e = launch_xblocks(T, c.LB, 1, L, stream, (q.nchunk + 7) / 8, bits);
   if (e != cudaSuccess) return cuda_fail(e, "activation pre-pass launch");
   e = launch_tile(c, L, false, stream);
   if (e != cudaSuccess) return cuda_fail(e, "q4_tile_kernel launch");
@@ -1369,7 +1424,7 @@ struct StepSizes {
 // one another) is cut into about `units_per_warp` units per warp of the grid.
 std::vector<int> plan_ksplit(const sf_q4_task* tasks, int n, int warps) {
   std::vector<int> ks(n, 1);
-  const int upw = env_int("SF_TILE_UNITS_PER_WARP", 1);
+  const int upw = 1;   // units per warp a phase is cut into
   int i = 0;
   while (i < n) {
     int j = i + 1;
@@ -1405,7 +1460,7 @@ StepSizes step_sizes(const sf_q4_task* tasks, int n, const std::vector<int>& ksp
   z.tiles = align256(tiles);
   z.table = align256((size_t)n * sizeof(TileTask));
   z.part = part;
-  z.cmap = align256(chunks * 4);
+  z.cmap = align256(chunks * 4) + align256((size_t)8 * n);   // chunk map, then the compact unit starts
   z.xblk = xb;
   return z;
 }
@@ -1420,8 +1475,10 @@ struct StepHandle {
   bool tp;                  // has tensor-parallel exchange tasks (epoch at the workspace end)
 };
 
+int task_bits(const sf_q4_task& a) { return a.bits == 0 ? 4 : a.bits; }
+
 bool step_config(const sf_q4_task* tasks, TileConfig& c) {
-  return make_config(tasks[0].T, tasks[0].zeros != nullptr, tasks[0].group_size, c);
+  return make_config(tasks[0].T, tasks[0].zeros != nullptr, tasks[0].group_size, c, task_bits(tasks[0]));
 }
 }  // namespace
 
@@ -1430,7 +1487,8 @@ extern "C" {
 size_t sf_q4_step_workspace_bytes(const sf_q4_task* tasks, int ntasks) {
   if (!tasks || ntasks < 1) return 0;
   for (int i = 0; i < ntasks; ++i)
-    if (tasks[i].T < 1 || tasks[i].T > kMaxGemvT || !shape_ok(tasks[i].N, tasks[i].K, tasks[i].group_size))
+    if (tasks[i].T < 1 || tasks[i].T > kMaxGemvT ||
+        !shape_ok(tasks[i].N, tasks[i].K, tasks[i].group_size, task_bits(tasks[i])))
       return 0;
   TileConfig c;
   if (!step_config(tasks, c)) return 0;
@@ -1467,9 +1525,9 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
     if (!a.W || !a.scales || !a.X || (!a.Y && role != SF_ROLE_PUSH))
       return fail(SF_ERR_NULL, "task %d: null pointer", i);
     if (a.T != T || (a.zeros != nullptr) != asym || a.group_size <= 0 ||
-        lb_for(a.group_size) != lb_for(tasks[0].group_size))
-      return fail(SF_ERR_UNSUPPORTED, "task %d: all tasks need the same T, layout and group class", i);
-    if (!shape_ok(a.N, a.K, a.group_size))
+        lb_for(a.group_size) != lb_for(tasks[0].group_size) || task_bits(a) != task_bits(tasks[0]))
+      return fail(SF_ERR_UNSUPPORTED, "task %d: all tasks need the same T, layout, bit width and group class", i);
+    if (!shape_ok(a.N, a.K, a.group_size, task_bits(a)))
       return fail(SF_ERR_UNSUPPORTED, "task %d: shape N=%d K=%d gs=%d not supported by the step kernel",
                   i, a.N, a.K, a.group_size);
     if (a.x_dtype < 0 || a.x_dtype > 2 || a.y_dtype < 0 || a.y_dtype > 2)
@@ -1505,7 +1563,7 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
     q.W = a.W; q.S = a.scales; q.Z = a.zeros; q.bias = a.bias; q.X = a.X; q.Y = a.Y;
     q.xdt = a.x_dtype; q.ydt = a.y_dtype;
     q.epi = a.epilogue;
-    int rc = fill_task(q, a.N, a.K, a.group_size, T, want[i]);
+    int rc = fill_task(q, a.N, a.K, a.group_size, T, want[i], task_bits(a));
     if (rc != SF_OK) return rc;
     q.tcnt = reinterpret_cast<unsigned int*>(tiles);
     tiles += (size_t)q.ntile * 4;
@@ -1575,6 +1633,9 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
     for (int c = 0; c < h[i].nchunk; ++c) cmap.push_back(((unsigned int)i << 16) | (unsigned int)c);
   }
   uint8_t* cmap_d = ws + z.total() - z.cmap;
+  long long* ubase_d = reinterpret_cast<long long*>(cmap_d + align256(cmap.size() * 4));
+  std::vector<long long> ubase(ntasks);
+  for (int i = 0; i < ntasks; ++i) ubase[i] = h[i].ubase;
   StepHandle* hd = new StepHandle{};
   hd->cfg = c;
   hd->workspace = workspace;
@@ -1588,6 +1649,7 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
   L.phctr = reinterpret_cast<unsigned int*>(ws + align256((size_t)128 * c.grid));
   L.done = L.phctr + 4 * ntasks;
   L.cmap = reinterpret_cast<const unsigned int*>(cmap_d);
+  L.ubase = ubase_d;
   L.nphase = nph;
   L.epoch = nullptr;
   L.poison = poison;
@@ -1596,6 +1658,7 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
   if (e == cudaSuccess) e = cudaMemset(ws, 0, z.ctr + z.tiles);
   if (e == cudaSuccess && !cmap.empty())
     e = cudaMemcpy(cmap_d, cmap.data(), cmap.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(ubase_d, ubase.data(), (size_t)ntasks * 8, cudaMemcpyHostToDevice);
   if (e == cudaSuccess && has_tp) {
     L.epoch = reinterpret_cast<unsigned long long*>(ws + z.total());
     e = cudaMemset(L.epoch, 0, kEpochBytes);
@@ -1691,6 +1754,36 @@ extern "C" int sf_swiglu_interleaved(const float* in, void* out, int out_dtype, 
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "swiglu_interleaved_kernel launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
+  return SF_OK;
+}
+
+// 2-bit weights (siliconfer/quant/primitives.py:383-404 pack_int2: 4 values per
+// byte, element i in bits 2i..2i+1; symmetric q in [-2, 1] two's complement,
+// asymmetric q in [0, 3] with fp32 zeros).  Decode sizes on the same kernel
+// (T <= 16 per launch, larger T in chunks of 16); group size 128 or 256.
+extern "C" int sf_q2_linear(const uint8_t* W, const float* scales, const float* zeros, const float* bias,
+                            const void* X, int x_dtype, void* Y, int y_dtype, int N, int K, int T, int group_size,
+                            void* stream) {
+  if (!W || !scales || !X || !Y) return fail(SF_ERR_NULL, "null pointer argument");
+  if (x_dtype < 0 || x_dtype > 2 || y_dtype < 0 || y_dtype > 2) return fail(SF_ERR_DTYPE, "unknown dtype code");
+  if (N < 0 || K <= 0 || T < 0) return fail(SF_ERR_SHAPE, "invalid N/K/T");
+  if (group_size <= 0 || K % group_size) return fail(SF_ERR_SHAPE, "in_features must be divisible by group_size");
+  if (K % 4) return fail(SF_ERR_SHAPE, "in_features must be divisible by 4 for int2 packing");
+  if (N == 0 || T == 0) return SF_OK;
+  if (!shape_ok(N, K, group_size, 2))
+    return fail(SF_ERR_UNSUPPORTED, "int2 GEMV takes K %% 64 == 0 and group_size 128 or 256 (got K=%d gs=%d)", K,
+                group_size);
+  if ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(zeros) |
+       reinterpret_cast<uintptr_t>(X)) & 15)
+    return fail(SF_ERR_ALIGN, "W, scales, zeros and X must be 16-byte aligned");
+  const size_t xe = x_dtype == SF_F32 ? 4 : 2, ye = y_dtype == SF_F32 ? 4 : 2;
+  for (int t0 = 0; t0 < T; t0 += kMaxGemvT) {
+    const int tc = T - t0 < kMaxGemvT ? T - t0 : kMaxGemvT;
+    const int rc = run_tile_linear(W, scales, zeros, bias, static_cast<const uint8_t*>(X) + (size_t)t0 * K * xe,
+                                   x_dtype, static_cast<uint8_t*>(Y) + (size_t)t0 * N * ye, y_dtype, N, K, tc,
+                                   group_size, static_cast<cudaStream_t>(stream), 0, 2);
+    if (rc != SF_OK) return rc == SF_ERR_UNSUPPORTED ? fail(rc, "int2 GEMV: no launch configuration") : rc;
+  }
   return SF_OK;
 }
 

@@ -68,12 +68,12 @@ def _shape(a):
     return tuple(a.shape)
 
 
-def _check_weights(W, scales, group_size, zeros=None):
+def _check_weights(W, scales, group_size, zeros=None, bits: int = 4):
     if len(_shape(W)) != 2:
-        raise RuntimeError("W must be 2-D [out, in/2]")
+        raise RuntimeError("W must be 2-D [out, in/2]" if bits == 4 else "W must be 2-D [out, in/4]")
     if len(_shape(scales)) != 2:
         raise RuntimeError("scales must be 2-D [out, n_groups]")
-    out_f, in_f = _shape(W)[0], _shape(W)[1] * 2
+    out_f, in_f = _shape(W)[0], _shape(W)[1] * (8 // bits)
     if group_size <= 0:
         raise RuntimeError("group_size must be positive")
     n_groups = in_f // group_size
@@ -85,11 +85,12 @@ def _check_weights(W, scales, group_size, zeros=None):
 
 
 def linear(packed, scales, zeros, X, group_size: int = 128, bias=None,
-           out_dtype=None, pdl: bool = False):
+           out_dtype=None, pdl: bool = False, bits: int = 4):
     """Y[T, N] = X[T, K] @ dequant(W)^T (+ bias) on the GPU.
 
     All tensor arguments must already be CUDA tensors on one device; X may be
     fp32, fp16 or bf16; Y is fp32 unless ``out_dtype`` says otherwise.
+    ``bits=2``: ``packed`` holds four 2-bit weights per byte (sf_q2_linear).
     """
     _require_cuda()
     T, K = X.shape
@@ -97,6 +98,12 @@ def linear(packed, scales, zeros, X, group_size: int = 128, bias=None,
     out_dtype = out_dtype or torch.float32
     Y = torch.empty((T, N), dtype=out_dtype, device=X.device)
     lib = _lib.load()
+    if bits == 2:
+        _lib.check(lib.sf_q2_linear(
+            packed.data_ptr(), scales.data_ptr(), None if zeros is None else zeros.data_ptr(),
+            None if bias is None else bias.data_ptr(), X.data_ptr(), _dtype_code(X),
+            Y.data_ptr(), _dtype_code(Y), N, K, T, group_size, torch.cuda.current_stream(X.device).cuda_stream))
+        return Y
     _lib.check(lib.sf_q4_linear(
         packed.data_ptr(), scales.data_ptr(), None if zeros is None else zeros.data_ptr(),
         None if bias is None else bias.data_ptr(), X.data_ptr(), _dtype_code(X),

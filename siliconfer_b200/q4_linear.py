@@ -11,6 +11,10 @@ Restates siliconfer/model/q4_linear.py:12-68 as a ``torch.nn.Module``:
 * ``forward(x[..., K]) -> y[..., N]``, bias added after the product
   (q4_linear.py:63-66).
 
+``bits=2`` serves the reference's 2-bit packing (pack_int2,
+siliconfer/quant/primitives.py:383-404: ``packed`` is [N, K/4]), which the
+reference quantizes but cannot serve (siliconfer/engine/q4_loader.py:142-154).
+
 Differences that follow from the hardware: the triple is uploaded to the GPU
 once at construction (device buffers ``packed_d``, ``scales_d``, ``zeros_d``);
 activations stay on the GPU (no per-call host sync or copy, unlike
@@ -35,16 +39,19 @@ def _host_array(a, dtype):
 
 class Q4Linear(torch.nn.Module):
     def __init__(self, packed, scales, zeros=None, bias=None, group_size: int = 128,
-                 device=None, out_dtype=None):
+                 device=None, out_dtype=None, bits: int = 4):
         super().__init__()
+        if bits not in (2, 4):
+            raise RuntimeError("bits must be 4 or 2")
         self._packed = packed
         self._scales = scales
         self._zeros = zeros
+        self.bits = int(bits)
         self.group_size = int(group_size)
         self.out_features = int(packed.shape[0])
-        self.in_features = int(packed.shape[1]) * 2
+        self.in_features = int(packed.shape[1]) * (8 // self.bits)
         self.out_dtype = out_dtype
-        K._check_weights(packed, scales, self.group_size, zeros)
+        K._check_weights(packed, scales, self.group_size, zeros, bits=self.bits)
         if self.in_features % self.group_size:
             raise RuntimeError("in_features must be divisible by group_size")
         if device is None:
@@ -81,11 +88,11 @@ class Q4Linear(torch.nn.Module):
             xt = xt.float()
         xt = xt.contiguous()
         y = K.linear(self.packed_d, self.scales_d, self.zeros_d, xt, self.group_size,
-                     bias=self.bias_d, out_dtype=self.out_dtype, pdl=self.pdl)
+                     bias=self.bias_d, out_dtype=self.out_dtype, pdl=self.pdl, bits=self.bits)
         y = y.reshape(*orig[:-1], self.out_features)
         return y.cpu().numpy() if host else y
 
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "
-                f"group_size={self.group_size}, {'asym' if self.is_asym else 'sym'}, "
+                f"group_size={self.group_size}, bits={self.bits}, {'asym' if self.is_asym else 'sym'}, "
                 f"bias={self.bias is not None}")

@@ -64,6 +64,49 @@ def pack_weights_asym(W: np.ndarray, group_size: int = 128):
     return _pack(q), s, z
 
 
+# ---------------------------------------------------------------------------
+# 2-bit weights (siliconfer/quant/primitives.py:154-245, 383-404)
+# ---------------------------------------------------------------------------
+def quantize_sym_int2(w: np.ndarray, group_size: int = 128):
+    """int2 in [-2, 1] and fp32 scale = absmax / 1 per group (primitives.py:154-181)."""
+    g = _grouped(np.asarray(w, np.float32), group_size)
+    scale = (np.abs(g).max(axis=-1, keepdims=True) / np.float32(1)).astype(np.float32)
+    div = np.where(scale == 0.0, np.float32(1.0), scale)
+    q = np.round(g / div).clip(-2, 1).astype(np.int8)
+    return q.reshape(w.shape), scale[..., 0]
+
+
+def quantize_asym_int2(w: np.ndarray, group_size: int = 128):
+    """uint2 in [0, 3], fp32 scale = (max - min) / 3, integer-valued fp32 zero
+    (primitives.py:203-231)."""
+    g = _grouped(np.asarray(w, np.float32), group_size)
+    lo, hi = g.min(axis=-1, keepdims=True), g.max(axis=-1, keepdims=True)
+    scale = ((hi - lo) / np.float32(3)).astype(np.float32)
+    div = np.where(scale == 0.0, np.float32(1.0), scale)
+    zero = np.round(-lo / div).clip(0, 3).astype(np.float32)
+    q = (np.round(g / div) + zero).clip(0, 3).astype(np.uint8)
+    return q.reshape(w.shape), scale[..., 0], zero[..., 0]
+
+
+def pack_int2(q: np.ndarray) -> np.ndarray:
+    """Four 2-bit values per byte, element i in bits 2i..2i+1 (primitives.py:383-404);
+    rows are packed independently ([N, K] -> [N, K/4])."""
+    v = (np.asarray(q).astype(np.int32) & 3).astype(np.uint8)
+    return (v[:, 0::4] | (v[:, 1::4] << 2) | (v[:, 2::4] << 4) | (v[:, 3::4] << 6)).astype(np.uint8)
+
+
+def pack_weights_int2_sym(W: np.ndarray, group_size: int = 128):
+    """-> (packed uint8 [out, in/4], scales fp32 [out, in/group_size])."""
+    q, s = quantize_sym_int2(np.asarray(W, np.float32), group_size)
+    return pack_int2(q), s
+
+
+def pack_weights_int2_asym(W: np.ndarray, group_size: int = 128):
+    """-> (packed uint8 [out, in/4], scales fp32, zeros fp32 [out, in/group_size])."""
+    q, s, z = quantize_asym_int2(np.asarray(W, np.float32), group_size)
+    return pack_int2(q), s, z
+
+
 def pack_weights_device(W, group_size: int = 128, sym: bool = True):
     """RTN quantize + pack an fp32 CUDA tensor [N, K] on its device.
 

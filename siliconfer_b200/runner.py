@@ -88,7 +88,7 @@ class Q4StepRunner:
                 None if m.bias_d is None else m.bias_d.data_ptr(),
                 self.x.data_ptr() + c.x_off * xs, self.y.data_ptr() + c.y_off * ys,
                 m.out_features, m.in_features, self.tokens, m.group_size, xc, yc,
-                1 if self.waits[i] else 0)
+                1 if self.waits[i] else 0, 0, getattr(m, "bits", 4))
         nbytes = int(lib.sf_q4_step_workspace_bytes(arr, n))
         self._workspace = torch.zeros(nbytes + 256, dtype=torch.uint8, device=self.device)
         base = self._workspace.data_ptr()
@@ -138,7 +138,7 @@ class Q4StepRunner:
         for c in self.calls:
             m = c.layer
             g = m.in_features // m.group_size
-            tot += m.out_features * m.in_features // 2 + m.out_features * g * 4
+            tot += m.out_features * m.in_features * getattr(m, "bits", 4) // 8 + m.out_features * g * 4
             if m.is_asym:
                 tot += m.out_features * g * 4
             if m.bias_d is not None:
@@ -160,6 +160,14 @@ class Q4StepRunner:
         st = stream.cuda_stream
         for c in self.calls:
             m = c.layer
+            fn = lib.sf_q2_linear if getattr(m, "bits", 4) == 2 else None
+            if fn is not None:
+                _lib.check(fn(m.packed_d.data_ptr(), m.scales_d.data_ptr(),
+                              None if m.zeros_d is None else m.zeros_d.data_ptr(),
+                              None if m.bias_d is None else m.bias_d.data_ptr(),
+                              xb + c.x_off * xs, xc, yb + c.y_off * ys, yc,
+                              m.out_features, m.in_features, self.tokens, m.group_size, st))
+                continue
             rc = lib.sf_q4_linear(
                 m.packed_d.data_ptr(), m.scales_d.data_ptr(),
                 None if m.zeros_d is None else m.zeros_d.data_ptr(),

@@ -42,6 +42,10 @@ def layer_seed(config: int, layer: int, proj: str) -> int:
 
 QWEN_LAYERS = 24   # config 2: the full Qwen2.5-0.5B decode step
 
+# 2-bit cases: name -> (seed, out_f, in_f, group_size, std)
+INT2_CASES = {"int2_sym": (71, 96, 512, 128, 0.02), "int2_asym": (72, 96, 512, 128, 0.02),
+              "int2_sym_unit": (73, 64, 256, 128, 1.0), "int2_asym_g256": (74, 40, 1024, 256, 0.02)}
+
 
 def bf16_round(a: np.ndarray) -> np.ndarray:
     """fp32 values rounded to the nearest bfloat16 (ties to even), as fp32."""

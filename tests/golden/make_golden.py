@@ -10,7 +10,9 @@ module level).  Every output below comes from the reference's own functions:
 ``siliconfer.kernels.neon.{pack_weights_sym, pack_weights_asym, gemv_sym,
 gemm_sym, gemm_asym, _numpy_gemv_asym}``, ``siliconfer.quant.primitives.
 {quantize_sym, quantize_asym, dequantize_sym, dequantize_asym, unpack_int4,
-fake_quantize}`` and ``siliconfer.quant.hqq.hqq_quantize_weight``.
+fake_quantize, quantize_sym_int2, quantize_asym_int2, pack_int2, unpack_int2,
+dequantize_sym_int2, dequantize_asym_int2}`` and
+``siliconfer.quant.hqq.hqq_quantize_weight``.
 """
 from __future__ import annotations
 
@@ -165,6 +167,23 @@ def main() -> None:
             meta["hashes"][f"c2L/{layer}/{proj}/packed"] = C.sha(p)
             x = C.acts(C.layer_seed(2, layer, proj) + 7, 1, k)
             out[f"c2L/{layer}/{proj}/y"] = K.gemm_asym(p, s, z, x, 128)
+
+    # --- 2-bit packing (quantized and packed by the reference, served here) ----
+    # The reference has no int2 product; "y" is its own dequant times x.
+    for name, (seed, n, k, gs, std) in C.INT2_CASES.items():
+        w = C.weights(seed, n, k, std)
+        x = C.acts(seed + 7, 3, k)
+        if name.startswith("int2_asym"):
+            q, s, z = P.quantize_asym_int2(w, gs)
+            dq = P.dequantize_asym_int2(P.unpack_int2(P.pack_int2(q), w.size, signed=False).reshape(w.shape), s, z, gs)
+            out[f"{name}/zeros"] = z
+        else:
+            q, s = P.quantize_sym_int2(w, gs)
+            dq = P.dequantize_sym_int2(P.unpack_int2(P.pack_int2(q), w.size, signed=True).reshape(w.shape), s, gs)
+        out[f"{name}/packed"] = P.pack_int2(q).reshape(n, k // 4)
+        out[f"{name}/scales"] = s
+        out[f"{name}/dequant"] = dq.astype(np.float32)
+        out[f"{name}/y"] = (x.astype(np.float64) @ dq.astype(np.float64).T).astype(np.float32)
 
     np.savez_compressed(HERE / "golden.npz", **out)
     (HERE / "golden_meta.json").write_text(json.dumps(meta, indent=1, sort_keys=True))

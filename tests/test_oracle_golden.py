@@ -104,3 +104,25 @@ def test_oracle_config2_step_layers(golden):
             assert C.sha(p) == meta["hashes"][f"c2L/{layer}/{proj}/packed"]
             x = C.acts(C.layer_seed(2, layer, proj) + 7, 1, k)
             assert O.normwise_rel_err(O.gemm(p, s, z, x), g[f"c2L/{layer}/{proj}/y"]) < 1e-6
+
+
+@pytest.mark.parametrize("name", list(C.INT2_CASES))
+def test_int2_packers_and_oracle_match_reference(name, golden):
+    """2-bit quantize/pack (siliconfer/quant/primitives.py:154-245, 383-425):
+    the product packers and the oracle's unpack/dequant are bit-exact with the
+    reference; the oracle product equals the reference dequant times x."""
+    from siliconfer_b200 import quant as Q
+    g, _ = golden
+    seed, n, k, gs, std = C.INT2_CASES[name]
+    w = C.weights(seed, n, k, std)
+    x = C.acts(seed + 7, 3, k)
+    asym = name.startswith("int2_asym")
+    if asym:
+        p, s, z = Q.pack_weights_int2_asym(w, gs)
+        assert np.array_equal(z, g[f"{name}/zeros"])
+    else:
+        (p, s), z = Q.pack_weights_int2_sym(w, gs), None
+    assert np.array_equal(p, g[f"{name}/packed"])
+    assert np.array_equal(s, g[f"{name}/scales"])
+    assert np.array_equal(O.dequantize_int2(p, s, z, gs), g[f"{name}/dequant"])
+    assert O.normwise_rel_err(O.gemm_int2(p, s, z, x, gs), g[f"{name}/y"]) < 1e-6
