@@ -42,6 +42,12 @@ def layer_seed(config: int, layer: int, proj: str) -> int:
 
 QWEN_LAYERS = 24   # config 2: the full Qwen2.5-0.5B decode step
 
+# int8 KV attention cases of the reference's own tests
+# (tests/test_metal_attention.py): name -> (seed, B, H, Hkv, D, T)
+KV_CASES = {"kv_mha_T128": (0, 1, 4, 4, 8, 128), "kv_gqa_T512": (3, 1, 14, 2, 64, 512),
+            "kv_batch": (9, 3, 4, 2, 16, 32), "kv_tiles_T100": (11, 1, 14, 2, 64, 100),
+            "kv_gqa_T2048": (17, 1, 14, 2, 64, 2048)}
+
 # 2-bit cases: name -> (seed, out_f, in_f, group_size, std)
 INT2_CASES = {"int2_sym": (71, 96, 512, 128, 0.02), "int2_asym": (72, 96, 512, 128, 0.02),
               "int2_sym_unit": (73, 64, 256, 128, 1.0), "int2_asym_g256": (74, 40, 1024, 256, 0.02)}

@@ -42,6 +42,34 @@ def _install_mlx_standin() -> None:
         sys.modules[name] = m
 
 
+def _load_with_numpy_mx(path: pathlib.Path, name: str):
+    """Loads one reference module whose mlx.core calls are plain array
+    functions (max/abs/where/ones_like/round/clip/astype) with numpy standing
+    in for mlx.core, so that the reference's own code computes the vectors."""
+    import importlib.util
+    shim = types.ModuleType("mlx.core")
+    for fn in ("max", "abs", "where", "ones_like", "round", "clip", "float32", "float16", "int8"):
+        setattr(shim, fn, getattr(np, fn))
+    shim.array = np.ndarray
+    shim.Dtype = type(np.float32)
+    saved = {k: sys.modules.get(k) for k in ("mlx", "mlx.core")}
+    sys.modules["mlx.core"] = shim
+    pkg = types.ModuleType("mlx")
+    pkg.core = shim
+    sys.modules["mlx"] = pkg
+    try:
+        spec = importlib.util.spec_from_file_location(name, path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                sys.modules.pop(k, None)
+            else:
+                sys.modules[k] = v
+    return mod
+
+
 def main() -> None:
     ref = os.environ.get("SILICONFER_REF")
     if not ref:
@@ -184,6 +212,23 @@ def main() -> None:
         out[f"{name}/scales"] = s
         out[f"{name}/dequant"] = dq.astype(np.float32)
         out[f"{name}/y"] = (x.astype(np.float64) @ dq.astype(np.float64).T).astype(np.float32)
+
+    # --- int8 KV cache: the reference's quantize_kv (model/kv_cache.py:49-63)
+    # on the inputs of its own attention tests (tests/test_metal_attention.py:
+    # _random_inputs with their seeds and shapes)
+    kvmod = _load_with_numpy_mx(pathlib.Path(ref) / "siliconfer" / "model" / "kv_cache.py", "ref_kv_cache")
+    for name, (seed, B, H, Hkv, D, T) in C.KV_CASES.items():
+        rng = np.random.default_rng(seed)
+        q = rng.normal(0, 1, (B, H, D)).astype(np.float32)
+        k = rng.normal(0, 1, (B, Hkv, T, D)).astype(np.float32)
+        v = rng.normal(0, 1, (B, Hkv, T, D)).astype(np.float32)
+        kc, ks = kvmod.quantize_kv(k)
+        vc, vs = kvmod.quantize_kv(v)
+        out[f"{name}/q"] = q
+        out[f"{name}/k_codes"] = np.asarray(kc, np.int8)
+        out[f"{name}/k_scales"] = np.asarray(ks, np.float32)[..., 0]
+        out[f"{name}/v_codes"] = np.asarray(vc, np.int8)
+        out[f"{name}/v_scales"] = np.asarray(vs, np.float32)[..., 0]
 
     np.savez_compressed(HERE / "golden.npz", **out)
     (HERE / "golden_meta.json").write_text(json.dumps(meta, indent=1, sort_keys=True))

@@ -79,3 +79,53 @@ def test_gpu_tilings_and_dtypes(cuda, n_tiles):
         r = O.kv_attention_fp64(qq.float().cpu().numpy(), kc.cpu().numpy(), ks.cpu().numpy(),
                                 vc.cpu().numpy(), vs.cpu().numpy()) if qdt != torch.float32 else ref
         assert np.max(np.abs(out.float().cpu().numpy() - r)) / np.max(np.abs(r)) < tol
+
+
+# ---- pinned to the reference: its own quantize_kv on its own test inputs -----
+import cases as C   # noqa: E402
+
+
+def _kv_golden(g, name):
+    return tuple(g[f"{name}/{f}"] for f in ("q", "k_codes", "k_scales", "v_codes", "v_scales"))
+
+
+@pytest.mark.parametrize("name", list(C.KV_CASES))
+def test_quantize_kv_matches_reference(golden, name):
+    """The int8 codes and scales the reference's quantize_kv (kv_cache.py:49-63)
+    computed on the inputs of its attention tests: bit-exact."""
+    g, _ = golden
+    seed, B, H, Hkv, D, T = C.KV_CASES[name]
+    rng = np.random.default_rng(seed)
+    rng.normal(0, 1, (B, H, D))
+    k = rng.normal(0, 1, (B, Hkv, T, D)).astype(np.float32)
+    v = rng.normal(0, 1, (B, Hkv, T, D)).astype(np.float32)
+    _, kc, ks, vc, vs = _kv_golden(g, name)
+    for x, c_ref, s_ref in ((k, kc, ks), (v, vc, vs)):
+        c, s = O.quantize_kv(x)
+        assert np.array_equal(c, c_ref) and np.array_equal(s.view(np.uint32), s_ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("name", list(C.KV_CASES))
+def test_oracle_attention_on_reference_cases(golden, name):
+    """The reference test's criterion (tests/test_metal_attention.py: max
+    |out - ref| < 1e-4 against dequant + softmax attention), with the tile
+    count its heuristic picks (q4_attention.py:183-197)."""
+    g, _ = golden
+    q, kc, ks, vc, vs = _kv_golden(g, name)
+    T = kc.shape[2]
+    n_tiles = 1 if T <= 16 else min(256, -(-T // 16))
+    got = O.kv_attention_decode(q, kc, ks, vc, vs, n_tiles=n_tiles)
+    assert np.max(np.abs(got - O.kv_attention_fp64(q, kc, ks, vc, vs))) < 1e-4
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", [n for n, c in C.KV_CASES.items() if c[4] in (64, 128, 256)])
+def test_gpu_on_reference_cases(cuda, golden, name):
+    """The CUDA kernel on the reference-quantized caches, at the reference
+    test's own tolerance (max abs difference < 1e-4)."""
+    from siliconfer_b200.kv_attention import fused_quantized_attention_decode
+    g, _ = golden
+    q, kc, ks, vc, vs = _kv_golden(g, name)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    out = fused_quantized_attention_decode(dev(q), dev(kc), dev(ks), dev(vc), dev(vs)).cpu().numpy()
+    assert np.max(np.abs(out - O.kv_attention_fp64(q, kc, ks, vc, vs))) < 1e-4
