@@ -314,6 +314,7 @@ def run_ours(args, rank, world, local_rank):
         result["sweep"] = sweep_measure(layers, device, args)
         result["small_configs"] = small_configs_measure(device)
         result["int2"] = int2_measure(device, args)
+        result["per_call"] = per_call_measure(device)
         result["prefill"] = prefill_measure(device, runner.stream)
         result["kv_attention"] = kv_attention_measure(device, runner.stream)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -729,6 +730,49 @@ def small_configs_measure(device, iters=20):
         del r, layers
     out["timing"] = "each replay timed alone with CUDA events after a 256 MB buffer write (cold L2)"
     return out
+
+
+def per_call_measure(device, n=200):
+    """The reference-shaped call: one Q4Linear forward per projection
+    (siliconfer/model/q4_linear.py:49-68), on 7B q_proj (4096 x 4096, sym g128),
+    batch 1.  `torch_*`: fp16 activation already on the GPU, output left on
+    it (the module API: ctypes call, output allocation, pre-pass + GEMV
+    launches); device time per call from CUDA events over n back-to-back
+    calls, host time per call from the wall clock of the same loop.
+    `numpy_us`: numpy fp32 in, numpy fp32 out (H2D copy, kernels, D2H copy,
+    synchronisation), wall clock per call, like the reference's call."""
+    import torch
+    from siliconfer_b200.q4_linear import Q4Linear
+    from siliconfer_b200.quant import pack_weights_device
+    g = torch.Generator(device=device)
+    g.manual_seed(11)
+    p, sc = pack_weights_device(torch.randn((4096, 4096), generator=g, device=device) * 0.02, 128)
+    m = Q4Linear(p, sc, group_size=128, device=device)
+    x = torch.randn((1, 4096), generator=g, device=device).half()
+    for _ in range(20):
+        m(x)
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    for _ in range(n):
+        m(x)
+    e1.record()
+    host_us = (time.perf_counter() - t0) / n * 1e6
+    e1.synchronize()
+    dev_us = e0.elapsed_time(e1) / n * 1e3
+    xn = x.float().cpu().numpy()
+    for _ in range(10):
+        m(xn)
+    t0 = time.perf_counter()
+    for _ in range(n // 4):
+        m(xn)
+    np_us = (time.perf_counter() - t0) / (n // 4) * 1e6
+    nb = 4096 * 2048 + 4096 * 32 * 4 + 4096 * 2 + 4096 * 4
+    return {"workload": "Q4Linear.forward on 7B q_proj (4096x4096, sym int4 g128), batch 1",
+            "torch_device_us": round(dev_us, 2), "torch_host_us": round(host_us, 2),
+            "torch_gbs": round(nb / dev_us / 1e3, 1), "numpy_us": round(np_us, 2),
+            "kernels_per_call": 2}
 
 
 def int2_measure(device, args):
