@@ -13,7 +13,7 @@
 //
 // Two kernels share this file: a tensor-core kernel for head_dim 64/128 and
 // GQA groups up to 16 (the default, described before kv_attn_tc_kernel), and
-// the CUDA-core kernel below (head_dim 256, or SF_ATTN_SIMT=1).
+// the CUDA-core kernel below (head_dim 256).
 // B200 layout of the work (CUDA-core kernel):
 //  * one CTA per (T split, batch, kv head) serves every query head of that kv
 //    head (GQA group), so each K/V byte is read once per group, not once per
@@ -45,8 +45,6 @@ extern std::atomic<long long> g_launches;
 namespace {
 
 constexpr int kAttnWarps = 4;
-constexpr int kMaxD = 256;
-constexpr int kMaxGroup = 8;
 
 struct AttnArgs {
   const void* q;          // [B, H, D] of q_dtype
@@ -577,7 +575,7 @@ int sf_kv_attention_decode(const void* q, int q_dtype, const int8_t* k_codes, co
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid((unsigned)n_split, (unsigned)(B * Hkv));
   cudaError_t e;
-  if (D <= 128 && G <= 16 && !getenv("SF_ATTN_SIMT")) {
+  if (D <= 128 && G <= 16) {
     e = D == 64 ? launch_tc_d<64>(a, grid, st) : launch_tc_d<128>(a, grid, st);
   } else {
     e = D == 64 ? launch_split_d<64>(a, grid, st)

@@ -11,21 +11,24 @@
 // even), and X is bf16 (converted from fp32/fp16 by a pre-pass), so outputs
 // agree with the fp32 reference to the bf16 tolerance.
 //
-// Kernel structure (one persistent CTA per SM, 14 warps):
-//  * warp 4  (producer): per k-block of 64, one TMA tile copy of each
-//    128-token slice of X (128-byte swizzle, the tcgen05 K-major layout) and
-//    one TMA tile copy of the packed weight bytes [BN rows x 32 bytes];
-//  * warps 6-13 (dequant): turn the packed bytes into bf16 weights
-//    (q - z) * s in fp32, rounded to bf16, written into shared memory in the
-//    same 128-byte swizzled K-major layout, then fence to the async proxy;
-//  * warp 5  (MMA): allocates TMEM, one elected thread issues
-//    tcgen05.mma.kind::f16 (M = 128 tokens, N = BN weight rows, K = 16) for
-//    each of the MT token slices, and releases each stage with
+// Kernel structure (one persistent CTA per SM, 18 warps):
+//  * warp 4 (producer): per k-block of 64, one TMA tile copy of the BT-token
+//    slice of X (128-byte swizzle, the tcgen05 K-major layout) and one TMA
+//    tile copy of the packed weight bytes [128 rows x 32 bytes];
+//  * warps 6-17 (dequant, three per TMEM lane quarter, each taking every
+//    third k-block): turn the packed bytes into bf16 weights RNE((q - z) * s)
+//    and write them straight into TMEM with tcgen05.st, where they are the
+//    MMA's A operand (M = 128 weight rows);
+//  * warp 5 (MMA): allocates TMEM; one elected thread issues
+//    tcgen05.mma.cta_group::1.kind::f16 (A = weights from TMEM, B = X from
+//    shared memory, N = BT tokens, K = 16) and releases stages with
 //    tcgen05.commit;
-//  * warps 0-3 (epilogue): tcgen05.ld the fp32 accumulators (warp w reads
-//    TMEM lanes 32w..32w+31 = tokens), add the bias, convert, store Y.
-//  The accumulators are double-buffered in TMEM when MT*BN <= 256 columns,
-//  so a tile's epilogue overlaps the next tile's main loop.
+//  * warps 0-3 (epilogue): tcgen05.ld the fp32 accumulators (lanes = weight
+//    rows, columns = tokens), add the bias, convert, and store Y through a
+//    [token][row] staging tile in shared memory with one TMA bulk store per
+//    32-token chunk (two staging tiles alternate).
+//  BT = 256 tokens (one accumulator buffer) or 128 (two, so that a tile's
+//  epilogue overlaps the next tile's main loop), chosen by tile rounds per SM.
 //  Every wait is bounded; on expiry the kernel records a bit in the device
 //  error word, raises a block-wide abort flag, drains its own copies and
 //  MMAs (bounded), frees its TMEM and returns.
@@ -45,9 +48,6 @@
 #include "sf_q4.h"
 #include "sf_q4_internal.h"
 
-#ifndef SF_TC_DQ_LANES
-#define SF_TC_DQ_LANES 3
-#endif
 
 namespace sf {
 SF_DEFINE_ERROR_READER(take_dev_error_tc)
@@ -56,9 +56,8 @@ extern std::atomic<long long> g_launches;
 namespace {
 
 constexpr int kBK = 64;                 // k per stage: 64 bf16 = one 128-byte swizzle row
-constexpr int kSliceBytes = 128 * 128;  // one 128-token slice of X per stage
 constexpr int kEpiWarps = 4, kProdWarp = 4, kMmaWarp = 5, kDqWarp0 = 6;
-constexpr int kDqLanes = SF_TC_DQ_LANES;   // dequant warps per TMEM lane quarter, one per in-flight k-block
+constexpr int kDqLanes = 3;   // dequant warps per TMEM lane quarter, one per in-flight k-block
 constexpr int kDqWarps = 4 * kDqLanes;
 constexpr int kThreads = 32 * (kDqWarp0 + kDqWarps);
 constexpr int kSmemLimit = 232448;      // 227 KB opt-in per block
@@ -76,7 +75,6 @@ struct TcParams {
   int T, N, K, G, gs, lg2gs, ydt;
   int mtiles, ntiles, kblocks, stages;
   int tma_store;  // epilogue writes Y with TMA stores (Y 16-byte aligned, N * elem % 16 == 0)
-  int dbg;  // development switches (SF_TC_DBG): 1 = no dequant work, 2 = no MMAs, 4 = no Y stores
 };
 
 // ---------------------------------------------------------------------------
@@ -148,15 +146,6 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
@@ -409,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t acol = tmem + L::A_COL + 32 * s;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
-            if (!(p.dbg & 2)) mma_bf16_ts(dcol, acol + 8 * kk, sw128_desc(st + kk * 32), idesc, (kb | kk) != 0);
+            mma_bf16_ts(dcol, acol + 8 * kk, sw128_desc(st + kk * 32), idesc, (kb | kk) != 0);
           issued = 1;
           mma_commit(empty0 + 8 * s);
         }
@@ -458,11 +447,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         ld2(srow, kb + kDqLanes, sn);
         if (ASYM) ld2(zrow, kb + kDqLanes, zn);
         if (!bar_wait(full0 + 8 * s, ph, kErrDq, abort_flag)) { ok = false; break; }
-        if (p.dbg & 1) {
-          __syncwarp();
-          if (lane == 0) bar_arrive(dq0 + 8 * s);
-          continue;
-        }
         tc_fence_after();
         const uint32_t st = base + s * L::STAGE;
         // packed row r: 32 bytes in the 32-byte swizzle (16-byte chunk c at c ^ ((r >> 2) & 1))
@@ -518,7 +502,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c0 = 0; c0 < BT; c0 += 32, ++chunk) {
         float v[32];
         tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * BT + c0), v);
-        if (p.dbg & 4) continue;
         if (p.tma_store) {
           const uint32_t ob = out0 + (uint32_t)(chunk & 1) * L::OUT;
           // the store that last read this staging tile (two chunks ago) has finished reading it
@@ -575,315 +558,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kMmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::TMEM_COLS)
-                 : "memory");
-  }
-}
-
-// ---------------------------------------------------------------------------
-// CTA-pair kernel: one cluster of two CTAs computes Y[t0 : t0+BT, n0 : n0+256].
-// CTA r (r = rank in the pair) dequantizes weight rows n0 + 128 r .. + 127 into
-// its own TMEM and loads tokens t0 + r*BT/2 .. of X into its own shared memory;
-// the leader (r = 0) issues tcgen05.mma.cta_group::2 (M = 256 rows across the
-// pair, N = BT tokens, each CTA providing half of B) and signals both CTAs'
-// barriers with multicast commits.  Per SM this halves the X bytes per MAC
-// against the single-CTA kernel.  No load uses cluster multicast.
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// Address of the same shared-memory location in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t map_cta(uint32_t saddr, uint32_t rank) {
-  uint32_t d;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
-  return d;
-}
-__device__ __forceinline__ void bar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// TMA tile load whose completion is counted on the pair leader's barrier.
-__device__ __forceinline__ void tma_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y,
-                                            uint32_t leader_bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-      "l"(map), "r"(x), "r"(y), "r"(leader_bar)
-      : "memory");
-}
-__device__ __forceinline__ void mma_bf16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
-                                                 uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrives on the barrier at `bar` in both CTAs of the pair once the leader's
-// earlier MMAs have completed.
-__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          bar),
-      "h"((unsigned short)3)
-      : "memory");
-}
-
-// Per CTA: X half [BT/2 tokens x 64 k] (128-byte swizzle) + packed weights of
-// its 128 rows; TMEM: accumulators (BT columns, two buffers when BT <= 128),
-// then one 32-column weight slot per stage.
-template <int BT>
-struct Tc2Layout {
-  static constexpr uint32_t X = (BT / 2) * 128;
-  static constexpr uint32_t P = 128 * 32;
-  static constexpr uint32_t STAGE = X + P;
-  static constexpr int NBUF = BT <= 128 ? 2 : 1;
-  static constexpr uint32_t A_COL = NBUF * BT;
-  static constexpr int S_TMEM = (512 - A_COL) / 32;
-  static constexpr int S_SMEM = (kSmemLimit - 1024 - 512) / STAGE;
-  static constexpr int S = (S_TMEM < S_SMEM ? S_TMEM : S_SMEM) > 8 ? 8 : (S_TMEM < S_SMEM ? S_TMEM : S_SMEM);
-  static constexpr uint32_t TMEM_COLS = 512;
-  static_assert(STAGE % 1024 == 0, "stage must keep 1024-byte alignment");
-  static_assert(A_COL + 32 * S <= TMEM_COLS, "TMEM plan exceeds 512 columns");
-  static constexpr size_t SMEM = 1024 + (size_t)S * STAGE + 512;
-};
-
-template <int BT, bool ASYM>
-__global__ void __launch_bounds__(kThreads, 1)
-    q4_gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_constant__ CUtensorMap mapW,
-                       const TcParams p) {
-  using L = Tc2Layout<BT>;
-  constexpr int S = L::S;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t base = (raw + 1023u) & ~1023u;
-  // control block: xfull[8] wfull[8] dq[8] empty[8] accf[2] acce[2] drain, TMEM address, abort flag.
-  // The offset is the same in both CTAs (same smem size and alignment).
-  const uint32_t ctl = base + (uint32_t)S * L::STAGE;
-  const uint32_t xfull0 = ctl, wfull0 = ctl + 64, dq0 = ctl + 128, empty0 = ctl + 192;
-  const uint32_t accf0 = ctl + 256, acce0 = ctl + 272, drain = ctl + 288;
-  uint8_t* ctl_gen = smem_raw + (ctl - raw);
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(ctl_gen + 296);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(ctl_gen + 300);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_rank();
-  const bool leader = rank == 0;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      bar_init(xfull0 + 8 * s, 1);          // leader: its expect_tx; both halves complete_tx here
-      bar_init(wfull0 + 8 * s, 1);          // own packed weights
-      bar_init(dq0 + 8 * s, 8);             // leader: one warp per lane quarter of each CTA
-      bar_init(empty0 + 8 * s, 1);          // multicast commit
-    }
-    for (int b = 0; b < 2; ++b) {
-      bar_init(accf0 + 8 * b, 1);           // multicast commit
-      bar_init(acce0 + 8 * b, 2 * kEpiWarps);   // leader: epilogue warps of both CTAs
-    }
-    bar_init(drain, 1);
-    *abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  if (warp == kProdWarp && lane == 0) {
-    prefetch_map(&mapX);
-    prefetch_map(&mapW);
-  }
-  if (warp == kMmaWarp) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32((const void*)tmem_slot)),
-                 "r"(L::TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-  }
-  tc_fence_before();
-  cluster_sync();   // barriers of both CTAs initialized, TMEM allocated
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  // the leader's copies of the shared barriers, as seen from this CTA
-  const uint32_t L_xfull0 = map_cta(xfull0, 0), L_dq0 = map_cta(dq0, 0), L_acce0 = map_cta(acce0, 0);
-
-  const int ntiles_total = p.mtiles * p.ntiles;
-  const int KB = p.kblocks;
-  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-
-  if (warp == kProdWarp) {
-    if (lane == 0) {
-      uint32_t it = 0;
-      bool ok = true;
-      for (int tile = pair; tile < ntiles_total && ok; tile += npairs) {
-        const int m0 = (tile % p.mtiles) * BT + (int)rank * (BT / 2);
-        const int n0 = (tile / p.mtiles) * 256 + (int)rank * 128;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
-          const uint32_t s = it % S, ph = (it / S) & 1;
-          if (!bar_wait(empty0 + 8 * s, ph ^ 1, kErrProd, abort_flag)) { ok = false; break; }
-          const uint32_t st = base + s * L::STAGE;
-          if (leader) bar_expect_tx(xfull0 + 8 * s, 2 * L::X);
-          tma_2d_pair(st, &mapX, kb * kBK, m0, L_xfull0 + 8 * s);
-          bar_expect_tx(wfull0 + 8 * s, L::P);
-          tma_2d(st + L::X, &mapW, kb * (kBK / 2), n0, wfull0 + 8 * s);
-        }
-      }
-      // Drain: this CTA's packed-weight copies (local barrier) must have landed
-      // before exit; the X halves are covered by the leader's MMA waits or the
-      // pair barrier at the end.
-      const uint32_t pending = it < (uint32_t)S ? it : (uint32_t)S;
-      for (uint32_t j = it - pending; j < it; ++j) {
-        const uint32_t s = j % S, ph = (j / S) & 1;
-        if (!bar_try(wfull0 + 8 * s, ph)) {
-          const long long t0 = clock64();
-          while (!bar_try(wfull0 + 8 * s, ph))
-            if (clock64() - t0 > kWaitCycles) { atomicOr(&g_dev_error, kErrDrain); break; }
-        }
-        if (leader && !bar_try(xfull0 + 8 * s, ph)) {
-          const long long t0 = clock64();
-          while (!bar_try(xfull0 + 8 * s, ph))
-            if (clock64() - t0 > kWaitCycles) { atomicOr(&g_dev_error, kErrDrain); break; }
-        }
-      }
-    }
-  } else if (warp == kMmaWarp) {
-    if (lane == 0 && leader) {
-      const uint32_t idesc = idesc_bf16(256, BT);
-      uint32_t it = 0, issued = 0;
-      int local = 0;
-      bool ok = true;
-      for (int tile = pair; tile < ntiles_total && ok; tile += npairs, ++local) {
-        const int b = L::NBUF == 2 ? (local & 1) : 0;
-        const uint32_t use = L::NBUF == 2 ? (uint32_t)(local >> 1) : (uint32_t)local;
-        if (!bar_wait(acce0 + 8 * b, (use & 1) ^ 1, kErrMma, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t dcol = tmem + (uint32_t)(b * BT);
-        for (int kb = 0; kb < KB; ++kb, ++it) {
-          const uint32_t s = it % S, ph = (it / S) & 1;
-          if (!bar_wait(xfull0 + 8 * s, ph, kErrMma, abort_flag) ||
-              !bar_wait(dq0 + 8 * s, ph, kErrMma, abort_flag)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t st = base + s * L::STAGE;
-          const uint32_t acol = tmem + L::A_COL + 32 * s;
-#pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            if (!(p.dbg & 2)) mma_bf16_ts_pair(dcol, acol + 8 * kk, sw128_desc(st + kk * 32), idesc, (kb | kk) != 0);
-          issued = 1;
-          mma_commit_pair(empty0 + 8 * s);
-        }
-        if (ok) mma_commit_pair(accf0 + 8 * b);
-      }
-      if (issued) {
-        mma_commit_pair(drain);
-        if (!bar_try(drain, 0)) {
-          const long long t0 = clock64();
-          while (!bar_try(drain, 0))
-            if (clock64() - t0 > kWaitCycles) { atomicOr(&g_dev_error, kErrDrain); break; }
-        }
-      }
-    }
-  } else if (warp >= kDqWarp0) {
-    // dequant: this CTA's 128 weight rows into its own TMEM slot (see the
-    // single-CTA kernel); completion is counted on the leader's barrier
-    const int q = warp & 3, j = (warp - kDqWarp0) >> 2;
-    const int r = 32 * q + lane;
-    uint32_t it0 = 0;
-    bool ok = true;
-    for (int tile = pair; tile < ntiles_total && ok; tile += npairs, it0 += KB) {
-      const int n = (tile / p.mtiles) * 256 + (int)rank * 128 + r;
-      const bool in = n < p.N;
-      const float* srow = p.S + (size_t)(in ? n : 0) * p.G;
-      const float* zrow = ASYM ? p.Z + (size_t)(in ? n : 0) * p.G : nullptr;
-      const int kb0 = (int)(((uint32_t)j + kDqLanes - it0 % kDqLanes) % kDqLanes);
-      auto ld2 = [&](const float* row, int kb, float (&v)[2]) {
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
-          v[hh] = (in && kb < KB) ? __ldg(row + ((kb * kBK + 32 * hh) >> p.lg2gs)) : 0.f;
-      };
-      float sn[2], zn[2] = {8.f, 8.f};
-      ld2(srow, kb0, sn);
-      if (ASYM) ld2(zrow, kb0, zn);
-      for (int kb = kb0; kb < KB; kb += kDqLanes) {
-        const uint32_t it = it0 + kb;
-        const uint32_t s = it % S, ph = (it / S) & 1;
-        const float sc[2] = {sn[0], sn[1]}, zc[2] = {zn[0], zn[1]};
-        ld2(srow, kb + kDqLanes, sn);
-        if (ASYM) ld2(zrow, kb + kDqLanes, zn);
-        if (!bar_wait(wfull0 + 8 * s, ph, kErrDq, abort_flag)) { ok = false; break; }
-        if (!(p.dbg & 1)) {
-          tc_fence_after();
-          const uint32_t st = base + s * L::STAGE;
-          uint32_t w8[8];
-          const uint32_t prow = st + L::X + r * 32, sw = (uint32_t)((r >> 2) & 1) << 4;
-          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                       : "=r"(w8[0]), "=r"(w8[1]), "=r"(w8[2]), "=r"(w8[3]) : "r"(prow + sw));
-          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                       : "=r"(w8[4]), "=r"(w8[5]), "=r"(w8[6]), "=r"(w8[7]) : "r"(prow + (sw ^ 16)));
-          uint32_t o[32];
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const float z = ASYM ? zc[hh] : 8.f;
-            const bool zint = !ASYM || (z == rintf(z) && fabsf(z) < 4194304.f);
-            const uint64_t s2 = f2(sc[hh], sc[hh]), negzc2 = f2(-(8388608.f + z), -(8388608.f + z)),
-                           negz2 = f2(-z, -z);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              uint32_t oc[4];
-              if (zint) dequant8<true>(w8[4 * hh + c], !ASYM, negzc2, negz2, s2, oc);
-              else dequant8<false>(w8[4 * hh + c], !ASYM, negzc2, negz2, s2, oc);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) o[16 * hh + 4 * c + e] = oc[e];
-            }
-          }
-          tmem_st32(tmem + ((uint32_t)(32 * q) << 16) + L::A_COL + 32 * s, o);
-          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) bar_arrive_cluster(L_dq0 + 8 * s);
-      }
-    }
-  } else {
-    // epilogue: this CTA's 128 weight rows x BT tokens
-    const int q = warp;
-    int local = 0;
-    for (int tile = pair; tile < ntiles_total; tile += npairs, ++local) {
-      const int m0 = (tile % p.mtiles) * BT, n = (tile / p.mtiles) * 256 + (int)rank * 128 + 32 * q + lane;
-      const int b = L::NBUF == 2 ? (local & 1) : 0;
-      const uint32_t use = L::NBUF == 2 ? (uint32_t)(local >> 1) : (uint32_t)local;
-      if (!bar_wait(accf0 + 8 * b, use & 1, kErrEpi, abort_flag)) break;
-      tc_fence_after();
-      const bool nin = n < p.N;
-      const float bv = (p.bias && nin) ? __ldg(p.bias + n) : 0.f;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BT; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * BT + c0), v);
-        if (nin && !(p.dbg & 4)) {
-          const int t0 = m0 + c0;
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            if (t0 + jj < p.T) {
-              const size_t o = (size_t)(t0 + jj) * p.N + n;
-              const float y = v[jj] + bv;
-              if (p.ydt == SF_F32) static_cast<float*>(p.Y)[o] = y;
-              else if (p.ydt == SF_BF16) static_cast<__nv_bfloat16*>(p.Y)[o] = __float2bfloat16_rn(y);
-              else static_cast<__half*>(p.Y)[o] = __float2half_rn(y);
-            }
-          }
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) bar_arrive_cluster(L_acce0 + 8 * b);
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();   // no CTA leaves while its peer may still touch its shared memory or TMEM
-  if (warp == kMmaWarp) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::TMEM_COLS)
                  : "memory");
   }
 }
@@ -995,49 +669,12 @@ int launch_tc(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& m
   return SF_OK;
 }
 
-// Token-tile width of the pair kernel (256 weight rows per pair tile).
-int choose_bt_pair(int T, int N, int sms) {
-  const long long nt = (N + 255) / 256, pairs = sms / 2;
-  const long long r128 = ((T + 127) / 128 * nt + pairs - 1) / pairs;
-  const long long r256 = ((T + 255) / 256 * nt + pairs - 1) / pairs;
-  const double c128 = (double)r128 * 128 * 1.3, c256 = (double)r256 * 256 * 1.05;
-  return (T > 128 && c256 <= c128) ? 256 : 128;
-}
-
-template <int BT, bool ASYM>
-int launch_tc2(const CUtensorMap& mx, const CUtensorMap& mw, TcParams& p, int sms, cudaStream_t st) {
-  using L = Tc2Layout<BT>;
-  p.stages = L::S;
-  auto* fn = q4_gemm_tc2_kernel<BT, ASYM>;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::SMEM);
-  if (e != cudaSuccess) return cuda_fail(e, "q4_gemm_tc2_kernel smem attribute");
-  const int tiles = p.mtiles * p.ntiles;
-  const int pairs = tiles < sms / 2 ? tiles : sms / 2;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(2 * pairs));
-  cfg.blockDim = dim3((unsigned)kThreads);
-  cfg.dynamicSmemBytes = L::SMEM;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, fn, mx, mw, p);
-  if (e != cudaSuccess) return cuda_fail(e, "q4_gemm_tc2_kernel launch");
-  g_launches.fetch_add(1, std::memory_order_relaxed);
-  return SF_OK;
-}
-
 }  // namespace
 
 int run_tc_gemm(const uint8_t* W, const float* S, const float* Z, const float* bias, const void* X, int xdt,
                 void* Y, int ydt, int N, int K, int T, int gs, int flags, cudaStream_t stream) {
   (void)flags;
-  if (getenv("SF_TC_DISABLE")) return SF_ERR_UNSUPPORTED;
-  if (T < kTcMinT && !getenv("SF_TC_FORCE")) return SF_ERR_UNSUPPORTED;
+  if (T < kTcMinT) return SF_ERR_UNSUPPORTED;
   // Shapes this kernel takes: whole 64-k blocks, a group size that keeps each
   // 32-k half inside one group, 16-byte aligned weights and activations.
   if (K % kBK || gs % 32 || (gs & (gs - 1)) || ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(X)) & 15))
@@ -1060,11 +697,10 @@ int run_tc_gemm(const uint8_t* W, const float* S, const float* Z, const float* b
     xb = buf;
   }
 
-  const bool pair_kernel = getenv("SF_TC_PAIR") != nullptr;
-  const int BT = pair_kernel ? choose_bt_pair(T, N, di.sms) : choose_bt(T, N, di.sms);
+  const int BT = choose_bt(T, N, di.sms);
   CUtensorMap mx, mw;
   if (!make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xb, (uint64_t)K, (uint64_t)T, (uint64_t)K * 2, kBK,
-                (uint32_t)(pair_kernel ? BT / 2 : BT), CU_TENSOR_MAP_SWIZZLE_128B))
+                (uint32_t)BT, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(SF_ERR_CUDA, "cuTensorMapEncodeTiled failed for the prefill activations (T=%d K=%d)", T, K);
   if (!make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, kBK / 2,
                 128, CU_TENSOR_MAP_SWIZZLE_32B))
@@ -1074,18 +710,12 @@ int run_tc_gemm(const uint8_t* W, const float* S, const float* Z, const float* b
   p.S = S; p.Z = Z; p.bias = bias; p.Y = Y;
   p.T = T; p.N = N; p.K = K; p.G = K / gs; p.gs = gs; p.lg2gs = __builtin_ctz((unsigned)gs); p.ydt = ydt;
   p.mtiles = (T + BT - 1) / BT;
-  p.ntiles = pair_kernel ? (N + 255) / 256 : (N + 127) / 128;
+  p.ntiles = (N + 127) / 128;
   p.kblocks = K / kBK;
-  if (const char* d = getenv("SF_TC_DBG")) p.dbg = atoi(d);
   const bool asym = Z != nullptr;
-  if (pair_kernel) {
-    if (BT == 256)
-      return asym ? launch_tc2<256, true>(mx, mw, p, di.sms, stream) : launch_tc2<256, false>(mx, mw, p, di.sms, stream);
-    return asym ? launch_tc2<128, true>(mx, mw, p, di.sms, stream) : launch_tc2<128, false>(mx, mw, p, di.sms, stream);
-  }
   CUtensorMap my;
   const int ye = ydt == SF_F32 ? 4 : 2;
-  p.tma_store = !getenv("SF_TC_NO_TMA_STORE") && (reinterpret_cast<uintptr_t>(Y) & 15) == 0 &&
+  p.tma_store = (reinterpret_cast<uintptr_t>(Y) & 15) == 0 &&
                 ((size_t)N * ye) % 16 == 0 &&
                 make_map(&my, ydt == SF_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                               : (ydt == SF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16),
