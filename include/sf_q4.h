@@ -80,8 +80,10 @@ int sf_q4_gemm_asym(const uint8_t* W, const float* scales, const float* zeros,
  * Replaces Q4Linear.__call__'s kernel dispatch (siliconfer/model/q4_linear.py:
  * 57-66): zeros != NULL selects the asymmetric kernel, bias (fp32 [N], may be
  * NULL) is added after the product.  T <= 16 (T <= 8 at group size 32) runs
- * the decode GEMV kernel in one pass over W; T >= 48 runs the prefill GEMM;
- * in between, the decode kernel runs on chunks of 16 tokens.  flags: bit 0 = allow programmatic
+ * the decode GEMV kernel in one pass over W (above 8 tokens on a two-digit
+ * activation grid: rounding at most 2^-15 of each group's max |x|); T >= 48
+ * runs the prefill GEMM; in between, the decode kernel runs on chunks of 8
+ * tokens.  flags: bit 0 = allow programmatic
  * dependent launch (the kernel may start streaming weights before the
  * previous kernel on `stream` has finished; x is read only after it has). */
 int sf_q4_linear(const uint8_t* W, const float* scales, const float* zeros,
@@ -136,8 +138,8 @@ void sf_q4_step_destroy(void* handle);
  * [-2, 1] (two's complement, zeros NULL) or asymmetric q in [0, 3] with fp32
  * zeros; y = X @ dequant(W)^T (+ bias), dequant (q - z) * s as in
  * dequantize_sym_int2 / dequantize_asym_int2 (primitives.py:184-245).
- * K % 64 == 0 and group_size 128 or 256; any T (the decode kernel, 16
- * tokens per launch). */
+ * K % 64 == 0 and group_size 128 or 256; any T (the decode kernel: one
+ * launch up to 16 tokens, chunks of 8 above). */
 int sf_q2_linear(const uint8_t* W, const float* scales, const float* zeros, const float* bias,
                  const void* X, int x_dtype, void* Y, int y_dtype, int N, int K, int T,
                  int group_size, void* stream);

@@ -253,8 +253,11 @@ int run_linear(const uint8_t* W, const float* S, const float* Z, const float* bi
   if (!force_generic && aligned) {
     // Decode GEMV as independent warp units; T above kMaxGemvT that the GEMM
     // path declined is cut into chunks of kMaxGemvT tokens (weights re-read).
+    // Up to 16 tokens: one launch (9-16 tokens need group size >= 64 and use
+    // the two-digit activation grid).  17-47 tokens: chunks of 8 on the
+    // three-digit grid, which keeps the reference's elementwise tolerances.
     int rc = SF_OK;
-    const int tmax = gs % 64 == 0 ? kMaxGemvT : 8;   // 9-16 tokens need group size >= 64
+    const int tmax = (T <= kMaxGemvT && gs % 64 == 0) ? kMaxGemvT : 8;
     for (int t0 = 0; t0 < T && rc == SF_OK; t0 += tmax) {
       const int tc = T - t0 < tmax ? T - t0 : tmax;
       rc = run_tile_linear(W, S, Z, bias, static_cast<const uint8_t*>(X) + (size_t)t0 * K * xe, xdt,

@@ -13,8 +13,10 @@
 //  * activations: per (token, group) x_fix = rint(x * 2^(22-E)), E the binary
 //    exponent of the group's max |x| (the grid step is 2^-22 of the group
 //    max), split into three signed int8 digits (x_fix = d0 + 256 d1 + 65536 d2).
-//    (Two digits would halve the MMAs from 3 tokens on, but their 2^-15
-//    rounding misses the reference's own elementwise test tolerances.)
+//    Above 8 tokens two digits on a 2^(14-E) grid (rounding at most 2^-15 of
+//    the group max, normwise about 1e-5 of y): they halve the MMAs.  Up to 8
+//    tokens three are kept: two digits would miss the reference's own
+//    elementwise test tolerances on its unit cases (1 and 4 tokens).
 //  * mma.sync m16n8k32 u8 x s8 -> s32 sums u*d exactly.  Up to 2 tokens a
 //    token's digits are adjacent B columns of one n tile (4 per token, the
 //    fourth empty), so a lane's accumulator pair holds digits (0, 1) or
@@ -87,7 +89,8 @@ __host__ __device__ constexpr int tile_pair(int T) { return T <= 8 ? 2 : 1; }
 
 // Bytes of one segment's activation block: [T][3 digits][4 lanes][2*LB] digit
 // bytes, then [T] x (group scale 2^(E-22), sum of x_fix) as two fp32.
-__host__ __device__ constexpr int xblock_bytes(int T, int LB) { return (T * (24 * LB + 8) + 15) & ~15; }
+__host__ __device__ constexpr int tile_nd(int T) { return T > 8 ? 2 : 3; }   // activation digits
+__host__ __device__ constexpr int xblock_bytes(int T, int LB) { return (T * (8 * tile_nd(T) * LB + 8) + 15) & ~15; }
 
 // Shared memory of a CTA: first the weight stages of every warp (1024-byte
 // aligned, as the 128-byte TMA swizzle needs), then each warp's other areas.
@@ -351,6 +354,7 @@ __device__ __forceinline__ uint2 pack_digits(const int* d) {
 
 // Fixed-point digit split of 8 activations of one lane; lanes in aligned
 // blocks of `lpg` form one quantization group.  d[i][j]: digit i of input j.
+template <int ND>
 __device__ __forceinline__ void digits8_raw(const float* v, int lpg, int (&d)[3][8], float& gsc_out,
                                             int& sum_out) {
   float m = 0.f;
@@ -365,11 +369,13 @@ __device__ __forceinline__ void digits8_raw(const float* v, int lpg, int (&d)[3]
     bad |= __shfl_xor_sync(0xffffffffu, bad, off);
   }
   // biased binary exponent `be` of the group max m: m < 2^(be-126), so
-  // x * 2^(148-be) stays within +-2^22 and splits into three int8 digits.
-  // Groups whose max is below 2^-105 are zero.
+  // x * 2^(126+F-be) stays within +-2^F: three int8 digits for F = 22, two for
+  // F = 14 (d1 = (x_fix - d0) / 256 lies in [-64, 64]).  Groups whose max is
+  // below 2^-105 are zero.
+  constexpr int F = ND == 3 ? 22 : 14;
   const int be = (int)(__float_as_uint(m) >> 23);
   const bool zero = bad || be < 22;
-  const float scl = zero ? 0.f : __uint_as_float((uint32_t)(275 - be) << 23);   // 2^(148-be)
+  const float scl = zero ? 0.f : __uint_as_float((uint32_t)(253 + F - be) << 23);   // 2^(126+F-be)
   int s = 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -377,14 +383,19 @@ __device__ __forceinline__ void digits8_raw(const float* v, int lpg, int (&d)[3]
     s += xf;
     const int d0 = (xf << 24) >> 24;
     const int r1 = (xf - d0) >> 8;
-    const int d1 = (r1 << 24) >> 24;
     d[0][j] = d0;
-    d[1][j] = d1;
-    d[2][j] = (r1 - d1) >> 8;
+    if constexpr (ND == 3) {
+      const int d1 = (r1 << 24) >> 24;
+      d[1][j] = d1;
+      d[2][j] = (r1 - d1) >> 8;
+    } else {
+      d[1][j] = r1;
+      d[2][j] = 0;
+    }
   }
   for (int off = 1; off < lpg; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
   gsc_out = bad ? __int_as_float(0x7fc00000)
-                : (zero ? 0.f : __uint_as_float((uint32_t)(be - 21) << 23));   // 2^(be-148)
+                : (zero ? 0.f : __uint_as_float((uint32_t)(be + 1 - F) << 23));   // 2^(be-126-F)
   sum_out = s;
 }
 
@@ -414,13 +425,13 @@ __device__ __forceinline__ void convert_chunk(const TileTask* p, int c, int lane
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] = 0.f;
   }
-  constexpr int ND = 3;
+  constexpr int ND = tile_nd(T);
   uint2 dig[ND];
   float gsc;
   int s;
   {
     int d[3][8];
-    digits8_raw(v, lpg, d, gsc, s);
+    digits8_raw<ND>(v, lpg, d, gsc, s);
     if constexpr (BITS == 4) {
 #pragma unroll
       for (int i = 0; i < ND; ++i) dig[i] = pack_digits(d[i]);
@@ -515,9 +526,10 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     q4_tile_kernel(const __grid_constant__ TileLaunch L) {
   using Ly = TileLayout<T, ASYM, LB, BITS>;
   // CMP (T <= 2): one n tile, token t in columns 4t .. 4t + 3 (digits 0-2, empty);
-  // else NG groups of 4 tokens, n tiles (2i, 2i + 1) = digits (0, 1) and 2 of group i
+  // 3..8 tokens: NG groups of 4 tokens, n tiles (2i, 2i + 1) = digits (0, 1) and 2
+  // of group i; 9..16 tokens: two digits, n tile i = digits (0, 1) of group i
   constexpr bool CMP = T <= 2;
-  constexpr int ND = 3, NG = CMP ? 1 : (T + 3) / 4, NT = CMP ? 1 : 2 * NG;
+  constexpr int ND = tile_nd(T), NG = CMP ? 1 : (T + 3) / 4, NT = CMP ? 1 : (ND == 3 ? 2 * NG : NG);
   constexpr int WPL = LB / 4, SEGK = 8 * LB, SPS = Ly::SPS, PS = tile_pair(T);
   constexpr int LBA = LB * BITS / 4;             // packed weight bytes of a lane's row slice per segment
   constexpr int KST = SPS * SEGK;                // k of one stage (128 bytes of every row)
@@ -557,9 +569,12 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     if (CMP) {
       tok = g >> 2;
       dg = g & 3;
-    } else {
+    } else if (ND == 3) {
       tok = (nt >> 1) * 4 + (g >> 1);
       dg = (nt & 1) ? ((g & 1) ? 3 : 2) : (g & 1);
+    } else {
+      tok = nt * 4 + (g >> 1);
+      dg = g & 1;
     }
     bval[nt] = tok < T && dg < ND;
     bslot[nt] = bval[nt] ? ((tok * ND + dg) * 4 + t) * 2 * LB : 0;
@@ -827,6 +842,8 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
             float v;
             if (CMP) {
               v = lmul * (float)(Cs[mt][0][2 * h] + 256 * Cs[mt][0][2 * h + 1]);
+            } else if (ND == 2) {
+              v = (float)(Cs[mt][tg][2 * h] + 256 * Cs[mt][tg][2 * h + 1]);
             } else {
               const int i01 = Cs[mt][2 * tg][2 * h] + 256 * Cs[mt][2 * tg][2 * h + 1];
               v = fmaf(65536.f, (float)Cs[mt][2 * tg + 1][2 * h], (float)i01);
@@ -1777,8 +1794,9 @@ extern "C" int sf_q2_linear(const uint8_t* W, const float* scales, const float* 
        reinterpret_cast<uintptr_t>(X)) & 15)
     return fail(SF_ERR_ALIGN, "W, scales, zeros and X must be 16-byte aligned");
   const size_t xe = x_dtype == SF_F32 ? 4 : 2, ye = y_dtype == SF_F32 ? 4 : 2;
-  for (int t0 = 0; t0 < T; t0 += kMaxGemvT) {
-    const int tc = T - t0 < kMaxGemvT ? T - t0 : kMaxGemvT;
+  const int tmax = T <= kMaxGemvT ? kMaxGemvT : 8;   // as sf_q4_linear: chunks of 8 above 16 tokens
+  for (int t0 = 0; t0 < T; t0 += tmax) {
+    const int tc = T - t0 < tmax ? T - t0 : tmax;
     const int rc = run_tile_linear(W, scales, zeros, bias, static_cast<const uint8_t*>(X) + (size_t)t0 * K * xe,
                                    x_dtype, static_cast<uint8_t*>(Y) + (size_t)t0 * N * ye, y_dtype, N, K, tc,
                                    group_size, static_cast<cudaStream_t>(stream), 0, 2);
