@@ -431,6 +431,9 @@ def tp_measure(args, rank, world, local_rank, dist):
                                      device=device),
     }
     if world > 1:
+        # the same fused launch without the exchange (partials kept local): what the GEMVs alone cost
+        runners["fused_no_exchange"] = TPStepRunner(groups, tokens=1, x_dtype=torch.bfloat16, mode="fused",
+                                                    device=device, exchange=False)
         runners["peer"] = TPStepRunner(groups, tokens=1, x_dtype=torch.bfloat16, mode="peer", comm=comm,
                                        device=device)
         runners["nccl"] = TPStepRunner(groups, tokens=1, x_dtype=torch.bfloat16, mode="nccl", device=device)
@@ -539,6 +542,7 @@ def tp_measure(args, rank, world, local_rank, dist):
         "fused_us": round(ms * 1e3, 1),
         "fused_ordered_us": round(times["fused_ordered"] * 1e3, 1),
         "fused_batch8_us": round(times["fused_batch8"] * 1e3, 1),
+        "fused_no_exchange_us": round(times["fused_no_exchange"] * 1e3, 1) if "fused_no_exchange" in times else None,
         "peer_us": round(times["peer"] * 1e3, 1) if "peer" in times else None,
         "nccl_us": round(times["nccl"] * 1e3, 1) if "nccl" in times else None,
         "gbs_per_gpu": round(per_gpu, 1),

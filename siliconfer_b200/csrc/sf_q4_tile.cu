@@ -79,6 +79,7 @@ namespace {
 __host__ __device__ constexpr int tile_kd(int T) { return T > 4 ? 2 : 3; }
 constexpr int kUnitRows = 32;          // rows per unit (two m16 tiles)
 constexpr int kEpiSwiGLU = 1;          // TileTask::epi
+constexpr int kRedTiles = 4;           // 32-row tiles summed by one unit of an all-reduce task
 // At most 12 warps per CTA (168 registers per thread); more than 4 tokens
 // doubles the accumulators, and those launches hold at most 8 warps (their
 // stages are larger) with 255 registers per thread.
@@ -495,12 +496,12 @@ __device__ __forceinline__ void push_val(const TileTask* p, unsigned long long e
   for (int q = 0; q < p->tp_world; ++q) __stcg(reinterpret_cast<float*>(p->xdata[q] + off), v);
 }
 // The warp's pushes of one tile are complete: flag it in every rank (whole warp).
+// The warp barrier orders every lane's pushes before the flag lanes' stores,
+// and a system-scope release makes them visible to a peer that acquires the
+// flag (release is cumulative over the stores ordered before it).
 __device__ __forceinline__ void push_flag(const TileTask* p, unsigned long long ep, int tile, int lane) {
   __syncwarp();
-  if (lane < p->tp_world) {
-    __threadfence_system();
-    st_release_sys_u64(p->xflag[lane] + (size_t)tile * p->tp_world + p->tp_rank, ep);
-  }
+  if (lane < p->tp_world) st_release_sys_u64(p->xflag[lane] + (size_t)tile * p->tp_world + p->tp_rank, ep);
   __syncwarp();
 }
 
@@ -761,11 +762,15 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
     }
 
     if (p->kind == 1) {
-      // ---- all-reduce of a pushed task: tile = lu (one unit per 32-row tile) ----
-      const unsigned long long* fl = p->xflag[p->tp_rank] + (size_t)lu * p->tp_world;
+      // ---- all-reduce of a pushed task: unit lu sums kRedTiles 32-row tiles ----
+      // lane l polls the flag of tile 4 lu + l / world from rank l % world
+      const int W_ = p->tp_world, ntl = (N + kUnitRows - 1) / kUnitRows;
+      const int t32 = lu * kRedTiles + lane / W_, src_rank = lane % W_;
+      const bool poll = lane < kRedTiles * W_ && t32 < ntl;
       int okf = 1;
-      if (lane < p->tp_world) {
-        unsigned long long v = ld_acquire_sys_u64(fl + lane);
+      if (poll) {
+        const unsigned long long* fl = p->xflag[p->tp_rank] + (size_t)t32 * W_ + src_rank;
+        unsigned long long v = ld_acquire_sys_u64(fl);
         const long long t0 = clock64();
         while (v < ep) {
           if (clock64() - t0 > kWaitCycles) {
@@ -774,7 +779,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
             break;
           }
           __nanosleep(32);
-          v = ld_acquire_sys_u64(fl + lane);
+          v = ld_acquire_sys_u64(fl);
         }
         if (v == kFlagPoison) {   // that rank gave up on an earlier step
           atomicOr(&g_dev_error, kErrPoisoned);
@@ -785,23 +790,29 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       __syncwarp();
       ok = __all_sync(0xffffffffu, okf) != 0;
       if (!ok) {
-        // the ranks are out of step for good: poison the communicator and this
-        // tile's flag in every peer, so that no peer sums a stale region
+        // the ranks are out of step for good: poison the communicator and these
+        // tiles' flags in every peer, so that no peer sums a stale region
         if (lane == 0 && L.poison) *reinterpret_cast<volatile unsigned long long*>(L.poison) = 1ull;
-        if (lane < p->tp_world) {
+        if (poll) {
           __threadfence_system();
-          st_release_sys_u64(p->xflag[lane] + (size_t)lu * p->tp_world + p->tp_rank, kFlagPoison);
+          st_release_sys_u64(p->xflag[src_rank] + (size_t)t32 * W_ + p->tp_rank, kFlagPoison);
         }
         break;
       }
-      const int row = lu * kUnitRows + lane;
-      if (row < N) {
+      const float* src = reinterpret_cast<const float*>(p->xdata[p->tp_rank] + (size_t)(ep & 1) * p->xpar);
+#pragma unroll 1
+      for (int i = 0; i < kRedTiles; ++i) {
+        const int row = (lu * kRedTiles + i) * kUnitRows + lane;
+        if (row >= N) break;
         const float bv = p->bias ? __ldg(p->bias + row) : 0.f;
-        const float* src = reinterpret_cast<const float*>(p->xdata[p->tp_rank] + (size_t)(ep & 1) * p->xpar);
         for (int tok = 0; tok < T; ++tok) {
-          float a = 0.f;
-          for (int q = 0; q < p->tp_world; ++q) a += __ldcv(src + ((size_t)q * T + tok) * N + row);
-          st_y(p->Y, (size_t)tok * N + row, a + bv, p->ydt);
+          float v[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) v[q] = q < W_ ? __ldcv(src + ((size_t)q * T + tok) * N + row) : 0.f;
+          float a2 = 0.f;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) a2 += v[q];   // rank order: every rank gets the same bits
+          st_y(p->Y, (size_t)tok * N + row, a2 + bv, p->ydt);
         }
       }
       tile_written(L, p, lane);
@@ -1601,9 +1612,10 @@ int step_create_impl(const sf_q4_task* tasks, const int* roles, int ntasks, void
     if (role != SF_ROLE_GEMV) {
       q.push = role == SF_ROLE_PUSH;
       q.kind = role >= SF_ROLE_REDUCE ? 1 : 0;
-      if (q.kind == 1) {   // sums an earlier pushed task: no weights, one unit per tile
+      if (q.kind == 1) {   // sums an earlier pushed task: no weights, one unit per kRedTiles tiles
         const TileTask& sq = h[role - SF_ROLE_REDUCE];
         q.ksplit = 1;
+        q.ntile = (q.ntile + kRedTiles - 1) / kRedTiles;
         q.xpre = 0;
         q.nchunk = 0;
         q.xpar = sq.xpar;

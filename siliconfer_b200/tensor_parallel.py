@@ -215,7 +215,8 @@ class TPStepRunner:
     LAYER_WAITS = (True, False, False, True, True, False, True)
 
     def __init__(self, layers, tokens: int = 1, x_dtype=None, mode: str = "peer",
-                 comm: PeerComm | None = None, group=None, device=None, ordered: bool = False):
+                 comm: PeerComm | None = None, group=None, device=None, ordered: bool = False,
+                 exchange: bool = True):
         import torch
         import torch.distributed as dist
         self.torch = torch
@@ -227,7 +228,12 @@ class TPStepRunner:
             raise ValueError("ordered=True needs mode='fused' (the unfused modes run in order already)")
         self.ordered = bool(ordered)
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
-        if self.world > 1 and mode in ("peer", "fused") and comm is None:
+        # exchange=False (fused mode, measurement only): the row-parallel shards'
+        # partial products are written locally and not summed across ranks
+        self.exchange = bool(exchange) and self.world > 1
+        if not exchange and mode != "fused":
+            raise ValueError("exchange=False needs mode='fused'")
+        if self.world > 1 and (mode == "peer" or (mode == "fused" and self.exchange)) and comm is None:
             raise ValueError(f"mode={mode!r} needs a PeerComm")
         self.device = torch.device(device) if device is not None else self.layers[0][0].packed_d.device
         self.lib = _lib.load()
@@ -291,7 +297,7 @@ class TPStepRunner:
                     roles.append(0)
                     continue
                 out = self.red[li, 0 if i == 3 else 1]
-                if self.world == 1:
+                if not self.exchange:
                     tasks.append(_lib.Q4Task(*base, None, xp, out.data_ptr(), m.out_features, m.in_features,
                                              self.tokens, m.group_size, _dtype_code(self.x), _lib.SF_F32, wait))
                     roles.append(0)
@@ -323,9 +329,9 @@ class TPStepRunner:
         ws = torch.zeros(nbytes + 256, dtype=torch.uint8, device=self.device)
         self._ws.append(ws)
         h = _lib.ctypes.c_void_p()
-        comm = self.comm.comm if (self.comm is not None and self.world > 1) else None
+        comm = self.comm.comm if (self.comm is not None and self.exchange) else None
         with torch.cuda.device(self.device):
-            if self.world > 1:
+            if self.exchange:
                 _lib.check(self.lib.sf_q4_step_create_tp(arr, rl, n, comm, (ws.data_ptr() + 255) & ~255, nbytes,
                                                          _lib.ctypes.byref(h)))
             else:
@@ -398,7 +404,7 @@ class TPStepRunner:
         """Line the ranks up before a run whose kernels wait on peers: the
         exchange waits are bounded (about 2 s), so a rank that is still
         building its shards would otherwise make the others' waits expire."""
-        if self.world > 1 and self.mode in ("peer", "fused"):
+        if self.world > 1 and (self.mode == "peer" or (self.mode == "fused" and self.exchange)):
             import torch.distributed as dist
             self.torch.cuda.synchronize(self.device)
             dist.barrier(group=self.group)
