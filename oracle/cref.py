@@ -21,9 +21,23 @@ _P = ctypes.c_void_p
 _I = ctypes.c_int
 
 
+def reference_root() -> str | None:
+    """Root of the siliconfer reference tree: $SILICONFER_REF, else the
+    ``reference_path`` that BASELINE.json records; None when neither exists."""
+    ref = os.environ.get("SILICONFER_REF")
+    if not ref:
+        meta = _HERE.parent / "BASELINE.json"
+        if meta.exists():
+            import json
+            ref = json.loads(meta.read_text()).get("reference_path")
+    return ref if ref and pathlib.Path(ref).is_dir() else None
+
+
 def build() -> None:
-    """Compile the checkers (make -C oracle); reference sources are optional."""
-    subprocess.run(["make", "-s", "-C", str(_HERE)], check=True)
+    """Compile the checkers (make -C oracle); the reference's own kernels only
+    when its source tree is present (see reference_root)."""
+    ref = reference_root()
+    subprocess.run(["make", "-s", "-C", str(_HERE)] + ([f"REF={ref}"] if ref else []), check=True)
 
 
 def _load(path: pathlib.Path):

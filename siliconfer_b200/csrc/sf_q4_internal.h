@@ -28,8 +28,6 @@ struct GemvParams {
   const void* X;
   void* Y;
   int N, K, G, gs, xdt, ydt;
-  int KS, RG, R, nst;
-  uint32_t stage_bytes, s_off, z_off, stage_base;
 };
 
 

@@ -730,7 +730,6 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       // i, i + CS, ... over all tasks of the phase.  Every warp has at most
       // one such unit per phase and reaches it before any other unit of the
       // phase, so no converting warp waits on its own conversion.
-      {
       const long long CS = min(W_all, p->ph_units);
       const long long i = u - p->ph_ubase;
       if (i < CS && i < p->ph_chunks) {
@@ -749,7 +748,7 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
         if (old + n == (unsigned)p->ph_chunks) publish(L.flags, 1, (unsigned)ph + 1, lane);
       }
       int okx = 1;
-      if (lane == 0) {
+      if (lane == 0 && p->ph_chunks > 0) {   // (a phase with nothing to convert has no such flag)
         okx = spin_geq(fl + 1, (unsigned)ph + 1, 0x400u);            // this phase's inputs converted
         asm volatile("fence.proxy.async.global;" ::: "memory");
       }
@@ -757,7 +756,6 @@ __global__ void __launch_bounds__(tile_max_threads(T), 1)
       if (!ok) {
         if (gemv) drain();
         break;
-      }
       }
     }
 
