@@ -148,6 +148,18 @@ def build_layers(workload, device, tp_rank=0, tp_size=1, seed=1234, n_layers=0):
     return layers
 
 
+def workload_config(args, world, n_layers, layout):
+    """The `config` object of both arms' lines (the same workload)."""
+    return {"workload": f"BASELINE config 3: {args.workload}-shaped decode step, "
+                        f"{n_layers} layers x 7 projections, each reading its own pre-supplied input",
+            "batch": args.batch, "group_size": 128, "layout": layout,
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "l2": "weights 3.44 GB per step >> 126 MB L2 (no flush needed)"
+            if args.workload == "7b" else "weights >> L2 (no flush needed)",
+            "layer_order": "decode_step_us_layer_order: same step with q/k/v -> o -> "
+                           "gate/up -> down -> next layer dependencies inside the launch"}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     from siliconfer_b200 import _lib
@@ -285,15 +297,7 @@ def run_ours(args, rank, world, local_rank):
         "dtype": "int4 weights (u8 nibbles) x fp16 activations, exact int32 products, fp32 accumulate",
         "data": "synthetic: seeded N(0,0.02) weights, RTN int4 sym g128 (device pack, bit-exact "
                 "with the reference packer); fp16 N(0,1) activations",
-        "config": {"workload": f"BASELINE config 3: {args.workload}-shaped decode step, "
-                               f"{len(layers) // 7} layers x 7 projections, each reading "
-                               f"its own pre-supplied input",
-                   "batch": args.batch, "group_size": 128, "layout": layout,
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": "weights 3.44 GB per step >> 126 MB L2 (no flush needed)"
-                   if args.workload == "7b" else "weights >> L2 (no flush needed)",
-                   "layer_order": "decode_step_us_layer_order: same step with q/k/v -> o -> "
-                                  "gate/up -> down -> next layer dependencies inside the launch"},
+        "config": workload_config(args, world, len(layers) // 7, layout),
         "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(kernel_gbs / peak, 4),
                      "peak_kind": peak_kind,
@@ -1000,8 +1004,7 @@ def run_reference(args, rank, world):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int4 weights x fp32 activations (fp16-representable), fp32 accumulate",
         "data": "synthetic: seeded N(0,0.02) weights, RTN int4 sym g128",
-        "config": {"workload": f"BASELINE config 3: {args.workload}-shaped decode step",
-                   "batch": args.batch, "group_size": 128, "layout": "sym"},
+        "config": workload_config(args, world, HIDDEN[args.workload][2], "sym"),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
                          "sample": f"{n_sample} of {full_layers} layers per step "
                                    f"(ms_per_step extrapolated to all layers); {desc}"},
