@@ -91,6 +91,28 @@ def load():
     return lib
 
 
+_ext = None
+
+
+def ext():
+    """The torch binding (_sf_ext, built from csrc/sf_torch_ext.cpp next to
+    libsf_q4.so).  It calls the same C entry points as the ctypes handle
+    above, on torch's current stream; RuntimeError if it is missing."""
+    global _ext
+    if _ext is None:
+        load()
+        from . import build as _build
+        if _build.ext_stale():
+            try:
+                _build.build_ext()
+            except Exception as exc:
+                if not _build.ext_path().exists():
+                    raise RuntimeError(f"{_build.ext_path()} is missing and could not be built: {exc}") from exc
+        from . import _sf_ext
+        _ext = _sf_ext
+    return _ext
+
+
 def check(rc: int) -> None:
     if rc != SF_OK:
         lib = load()

@@ -41,6 +41,8 @@ def build(force: bool = False, verbose: bool = False) -> pathlib.Path:
     per file), then links the shared library."""
     from concurrent.futures import ThreadPoolExecutor
     if not force and not needs_build():
+        if ext_stale():
+            build_ext(verbose)
         return LIB
     srcs = [p for p in SOURCES if p.exists()]
     objdir = PKG / "_build"
@@ -59,10 +61,46 @@ def build(force: bool = False, verbose: bool = False) -> pathlib.Path:
         return str(obj)
 
     with ThreadPoolExecutor(max_workers=max(1, min(len(srcs), os.cpu_count() or 1))) as ex:
-        objs = list(ex.map(compile_one, srcs))
-    subprocess.run([nvcc(), *ARCH, "-shared", "-o", str(LIB) + ".tmp", *objs], check=True)
+        futs = list(ex.map(compile_one, srcs))
+    subprocess.run([nvcc(), *ARCH, "-shared", "-o", str(LIB) + ".tmp", *futs], check=True)
     os.replace(str(LIB) + ".tmp", LIB)
+    build_ext(verbose)
     return LIB
+
+
+def ext_stale() -> bool:
+    out, src = ext_path(), PKG / "csrc" / "sf_torch_ext.cpp"
+    if not out.exists():
+        return True
+    t = out.stat().st_mtime
+    return any(p.stat().st_mtime > t for p in (src, LIB, ROOT / "include" / "sf_q4.h") if p.exists())
+
+
+def ext_path() -> pathlib.Path:
+    import sysconfig
+    return PKG / ("_sf_ext" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_ext(verbose: bool = False) -> pathlib.Path:
+    """The thin torch binding (csrc/sf_torch_ext.cpp), compiled in-tree with
+    torch's headers and linked against libsf_q4.so (found next to it)."""
+    import sysconfig
+    import torch
+    from torch.utils import cpp_extension as ce
+    src = PKG / "csrc" / "sf_torch_ext.cpp"
+    out = ext_path()
+    incs = ce.include_paths(device_type="cuda")
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-DTORCH_EXTENSION_NAME=_sf_ext",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+           *[f"-I{p}" for p in incs], f"-I{sysconfig.get_paths()['include']}", f"-I{ROOT / 'include'}",
+           str(src), "-o", str(out) + ".tmp",
+           *[f"-L{p}" for p in ce.library_paths()], "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu",
+           "-ltorch_cuda", "-ltorch_python", f"-L{PKG}", "-l:libsf_q4.so", "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True)
+    os.replace(str(out) + ".tmp", out)
+    return out
 
 
 if __name__ == "__main__":

@@ -89,27 +89,14 @@ def linear(packed, scales, zeros, X, group_size: int = 128, bias=None,
     """Y[T, N] = X[T, K] @ dequant(W)^T (+ bias) on the GPU.
 
     All tensor arguments must already be CUDA tensors on one device; X may be
-    fp32, fp16 or bf16; Y is fp32 unless ``out_dtype`` says otherwise.
+    fp32, fp16 or bf16; Y is fp32 unless ``out_dtype`` says otherwise.  The
+    call goes through the torch binding (_sf_ext), which allocates Y and runs
+    sf_q4_linear / sf_q2_linear on torch's current stream.
     ``bits=2``: ``packed`` holds four 2-bit weights per byte (sf_q2_linear).
     """
     _require_cuda()
-    T, K = X.shape
-    N = packed.shape[0]
-    out_dtype = out_dtype or torch.float32
-    Y = torch.empty((T, N), dtype=out_dtype, device=X.device)
-    lib = _lib.load()
-    if bits == 2:
-        _lib.check(lib.sf_q2_linear(
-            packed.data_ptr(), scales.data_ptr(), None if zeros is None else zeros.data_ptr(),
-            None if bias is None else bias.data_ptr(), X.data_ptr(), _dtype_code(X),
-            Y.data_ptr(), _dtype_code(Y), N, K, T, group_size, torch.cuda.current_stream(X.device).cuda_stream))
-        return Y
-    _lib.check(lib.sf_q4_linear(
-        packed.data_ptr(), scales.data_ptr(), None if zeros is None else zeros.data_ptr(),
-        None if bias is None else bias.data_ptr(), X.data_ptr(), _dtype_code(X),
-        Y.data_ptr(), _dtype_code(Y), N, K, T, group_size,
-        _lib.SF_FLAG_PDL if pdl else 0, torch.cuda.current_stream(X.device).cuda_stream))
-    return Y
+    return _lib.ext().linear(packed, scales, zeros, bias, X, group_size,
+                             out_dtype or torch.float32, bits, pdl)
 
 
 def _run(packed, scales, zeros, X, group_size, scalar=False):
@@ -128,11 +115,11 @@ def _run(packed, scales, zeros, X, group_size, scalar=False):
             Xd = Xd.float()
     T, K = Xd.shape
     N = Wd.shape[0]
-    Y = torch.empty((T, N), dtype=torch.float32, device=dev)
-    lib = _lib.load()
-    stream = torch.cuda.current_stream(dev).cuda_stream
     with torch.cuda.device(dev):
         if scalar:
+            Y = torch.empty((T, N), dtype=torch.float32, device=dev)
+            lib = _lib.load()
+            stream = torch.cuda.current_stream(dev).cuda_stream
             if Xd.dtype != torch.float32:
                 Xd = Xd.float()
             for t in range(T):
@@ -140,10 +127,7 @@ def _run(packed, scales, zeros, X, group_size, scalar=False):
                                                  Xd[t].data_ptr(), Y[t].data_ptr(),
                                                  N, K, group_size, stream))
         else:
-            _lib.check(lib.sf_q4_linear(
-                Wd.data_ptr(), Sd.data_ptr(), None if Zd is None else Zd.data_ptr(), None,
-                Xd.data_ptr(), _dtype_code(Xd), Y.data_ptr(), _lib.SF_F32, N, K, T,
-                group_size, 0, stream))
+            Y = _lib.ext().linear(Wd, Sd, Zd, None, Xd, group_size, torch.float32)
     if host:
         return Y.cpu().numpy()
     return Y

@@ -93,3 +93,18 @@ def test_swiglu_validation_without_gpu():
     assert lib.sf_q4_linear_swiglu(None, FAKE, None, None, FAKE, 0, FAKE, 0, 32, 128, 1, 64, None) == 1
     assert lib.sf_swiglu_interleaved(FAKE, FAKE, 0, 2, 24, None, None) == 2
     assert lib.sf_swiglu_interleaved(FAKE, FAKE, 0, 0, 32, None, None) == 0     # empty: nothing launched
+
+
+def test_torch_binding_loads_and_checks_devices():
+    """The torch binding imports next to libsf_q4.so, exposes both entry
+    points, and rejects host tensors before any launch."""
+    torch = pytest.importorskip("torch")
+    ext = _lib.ext()
+    assert callable(ext.linear) and callable(ext.linear_swiglu)
+    W = torch.zeros((32, 64), dtype=torch.uint8)
+    S = torch.ones((32, 1), dtype=torch.float32)
+    X = torch.zeros((1, 128), dtype=torch.float32)
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        ext.linear(W, S, None, None, X, 128, torch.float32)
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        ext.linear_swiglu(W, S, None, None, X, 128, torch.float32)
