@@ -55,6 +55,7 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstddef>
 #include <cstdint>
@@ -1446,26 +1447,64 @@ struct StepSizes {
   size_t total() const { return ctr + tiles + table + part + xblk + cmap; }
 };
 
-// k-splits of a task list: each phase (a run of tasks that need not wait for
-// one another) is cut into about `units_per_warp` units per warp of the grid.
+// k-splits of a task list.  Each phase (a run of tasks that need not wait for
+// one another) ends when its busiest warp does.  Warps take the launch's units
+// round robin (unit u goes to warp u mod W), so for every candidate split the
+// phase's units are dealt out exactly that way and the split whose busiest
+// warp has the least work wins; a unit's work is its groups plus kUnitCost
+// (its pipeline fill and k-split partials, in groups of streaming time).  This
+// keeps a small phase from being cut into slightly more units than the grid
+// has warps, which would leave a few warps a second unit and take twice as long.
+constexpr int kUnitCost = 4;
 std::vector<int> plan_ksplit(const sf_q4_task* tasks, int n, int warps) {
   std::vector<int> ks(n, 1);
-  const int upw = 1;   // units per warp a phase is cut into
+  auto stma_of = [&](int k) {
+    const int G = tasks[k].K / tasks[k].group_size;
+    return G % 4 == 0 &&
+           ((reinterpret_cast<uintptr_t>(tasks[k].scales) | reinterpret_cast<uintptr_t>(tasks[k].zeros)) & 15) == 0;
+  };
+  auto gper_for = [&](int k, int B) {
+    const int G = tasks[k].K / tasks[k].group_size;
+    return groups_per_unit(G, (G + B - 1) / B, stma_of(k), tasks[k].group_size);
+  };
+  std::vector<long long> load(warps);
+  long long ubase = 0;   // the phase's first unit in the launch
   int i = 0;
   while (i < n) {
     int j = i + 1;
     while (j < n && !tasks[j].wait_before) ++j;
-    long long tiles = 0;
-    for (int k = i; k < j; ++k) tiles += (tasks[k].N + kUnitRows - 1) / kUnitRows;
-    const long long want = tiles > 0 ? ((long long)warps * upw + tiles - 1) / tiles : 1;
+    int gmax = 1;
+    for (int k = i; k < j; ++k) gmax = std::max(gmax, tasks[k].K / tasks[k].group_size);
+    long long best_cost = -1, best_units = 0;
+    int best_b = gmax, last_sig = -1;
+    for (int B = gmax; B >= 1; --B) {
+      int sig = 0;   // skip a candidate that cuts every task as the previous one did
+      for (int k = i; k < j; ++k) sig = sig * 31 + gper_for(k, B);
+      if (sig == last_sig) continue;
+      last_sig = sig;
+      std::fill(load.begin(), load.end(), 0);
+      long long u = ubase;
+      for (int k = i; k < j; ++k) {
+        const int G = tasks[k].K / tasks[k].group_size, gper = gper_for(k, B);
+        const int kspl = (G + gper - 1) / gper, ntile = (tasks[k].N + kUnitRows - 1) / kUnitRows;
+        for (int s2 = 0; s2 < kspl; ++s2) {   // units of one k-range are consecutive (tile fastest)
+          const int len = std::min(gper, G - s2 * gper) + kUnitCost;
+          for (int t2 = 0; t2 < ntile; ++t2) load[(size_t)(u++ % warps)] += len;
+        }
+      }
+      const long long units = u - ubase;
+      const long long cost = *std::max_element(load.begin(), load.end());
+      if (best_cost < 0 || cost < best_cost || (cost == best_cost && units < best_units)) {
+        best_cost = cost;
+        best_units = units;
+        best_b = B;
+      }
+    }
     for (int k = i; k < j; ++k) {
-      const int G = tasks[k].K / tasks[k].group_size;
-      const bool stma = G % 4 == 0 &&
-                        ((reinterpret_cast<uintptr_t>(tasks[k].scales) |
-                          reinterpret_cast<uintptr_t>(tasks[k].zeros)) & 15) == 0;
-      const int gper = groups_per_unit(G, want, stma, tasks[k].group_size);
+      const int G = tasks[k].K / tasks[k].group_size, gper = gper_for(k, best_b);
       ks[k] = (G + gper - 1) / gper;
     }
+    ubase += best_units;
     i = j;
   }
   return ks;
