@@ -893,7 +893,7 @@ def kv_attention_measure(device, stream, iters=20):
         out.append({"B": B, "H": H, "Hkv": Hkv, "T": T, "D": D, "us": round(us, 1),
                     "gbs": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / peak, 4)})
         del kc, ks, vc, vs, q
-    return {"kernel": "kv_attn_split_kernel + kv_attn_merge_kernel (int8 KV, fp32 online softmax)",
+    return {"kernel": "kv_attn_tc_kernel + kv_attn_merge_kernel (int8 KV, mma.sync, fp32 online softmax; kv_attn_split_kernel only for head_dim 256)",
             "bound": "hbm", "peak_gbs": peak, "timing": "CUDA events around 20 back-to-back calls",
             "shapes": out}
 

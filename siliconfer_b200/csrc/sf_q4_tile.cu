@@ -1,4 +1,4 @@
-// sf_q4_tile.cu -- decode GEMV (T <= 8 tokens) as independent warp work units
+// sf_q4_tile.cu -- decode GEMV (T <= 16 tokens) as independent warp work units
 // on the sm_100a tensor cores, exact integer arithmetic.
 //
 // Reference semantics (siliconfer/kernels/neon/q4_gemv.cpp:37-140, 145-238;
@@ -43,12 +43,13 @@
 //  * A unit that covers part of K writes fp32 partial sums; the last unit of
 //    a 32-row tile to finish (per-tile arrival counter) adds the partials in
 //    k order -- deterministic -- and writes Y.
-//  * Dependencies (a task that reads what earlier tasks wrote) are per-task
-//    completion counters: a warp starting a unit of such a task first pulls
-//    the unit's weights towards L2 (they do not depend on anything), then
-//    waits until every tile of the tasks it depends on has been written.  All
-//    warps are resident (cooperative launch) and take units in increasing
-//    order, so a wait never blocks a unit it depends on.  Waits are bounded.
+//  * Dependencies (a task that reads what earlier tasks wrote) are phases: a
+//    warp starting a unit of a later phase first issues its first stages'
+//    weight copies (they do not depend on anything), then waits until every
+//    tile of the previous phase has been written (per-CTA flag lines) and the
+//    phase's inputs converted.  All warps are resident (cooperative launch)
+//    and take units in increasing order, so a wait never blocks a unit it
+//    depends on.  Waits are bounded.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
