@@ -827,10 +827,10 @@ def prefill_measure(device, stream, iters=20):
     import torch
     from siliconfer_b200 import quant as Q
     from siliconfer_b200.kernels import cuda as K
-    peak = None
+    peak, kind = 1590.0, "fallback bf16 burst (no MEASURED_PEAKS.json)"
     pk = ROOT / "MEASURED_PEAKS.json"
     if pk.exists():
-        peak = float(json.loads(pk.read_text())["bf16_tflops"])
+        peak, kind = float(json.loads(pk.read_text())["bf16_tflops"]), "measured bf16 burst"
     out = []
     g = torch.Generator(device=device)
     for m in (512, 2048):
@@ -862,7 +862,7 @@ def prefill_measure(device, stream, iters=20):
             del graph, p, s, z, X
     return {"workload": "BASELINE config 4: gemm_asym prefill, 7B shapes, asym int4 g128, bf16 X",
             "kernel": "q4_gemm_tc_kernel (tcgen05, dequant to bf16 in TMEM)", "peak_tflops": peak,
-            "peak_kind": "measured bf16 burst" if peak else None, "shapes": out}
+            "peak_kind": kind, "shapes": out}
 
 
 def kv_attention_measure(device, stream, iters=20):
