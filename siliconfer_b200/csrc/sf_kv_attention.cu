@@ -224,21 +224,27 @@ __global__ void __launch_bounds__(256) kv_attn_merge_kernel(const AttnArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Tensor-core variant (head_dim 64 or 128, GQA group <= 16): one warp takes 32
-// tokens at a time.
-//  * S = Q K^T on mma.sync m16n8k16 (fp16 in, fp32 accumulate): the G query
-//    rows of the group, padded to 16, are the A operand, split into an fp16
-//    high and low part (two MMAs) so that q keeps about 22 bits; the int8
-//    keys are the B operand, converted exactly (0x6400 | (v + 128) - 1152).
-//    Inside each 16-wide block of head_dim, the order is permuted the same
-//    way in Q and K (logical k 2t, 2t+1, 2t+8, 2t+9 = physical 4t .. 4t+3),
-//    which leaves q.k unchanged and lets each lane fetch its key bytes with
-//    one 32-bit load;
-//  * the scores are scaled per token by k_scale, online softmax per row;
-//  * O += P V with P' = p * v_scale * 2^10 (split high/low, the power of two
-//    keeps P' clear of fp16 subnormals and is divided out at the end) as the
-//    A operand straight from the score accumulators, and the int8 values
-//    staged as fp16 in shared memory and read with ldmatrix.trans.
+// Tensor-core variant (head_dim 64 or 128, GQA group <= 8): one warp takes 32
+// tokens at a time, with the products transposed so that the tokens, not the
+// few query heads of a group, fill the MMA's 16 rows:
+//  * S^T = K Q^T on mma.sync m16n8k16 (fp16 in, fp32 accumulate): the int8
+//    keys are the A operand (16 tokens x 16 of head_dim), converted exactly
+//    (0x6400 | (v + 128) - 1152); the group's query heads, padded to 8, are
+//    the B operand, split into an fp16 high and low part (two MMAs) so that q
+//    keeps about 22 bits.  Inside each 16-wide block of head_dim the order is
+//    permuted the same way in Q and K (logical k 2t, 2t+1, 2t+8, 2t+9 =
+//    physical 4t .. 4t+3), which leaves q.k unchanged and lets each lane
+//    fetch its key bytes with one 32-bit load;
+//  * the scores are scaled per token by k_scale; a lane holds heads 2t, 2t+1
+//    of its tokens and keeps their online-softmax state;
+//  * O^T += V^T P'^T with P' = p * v_scale * 2^10 (split high/low, the power
+//    of two keeps P' clear of fp16 subnormals and is divided out at the end):
+//    the values, staged as fp16 in shared memory, are the A operand through
+//    ldmatrix.trans, and P' goes through a small shared tile to become the B
+//    operand (also ldmatrix.trans).  The accumulators hold O^T[d][head] with
+//    the same heads 2t, 2t+1 per lane as the softmax state.
+// Per 32 tokens and head_dim 128 this is 32 + 32 MMAs (the untransposed form,
+// with at most 8 of 16 rows in use, needs 64 + 64).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -267,14 +273,15 @@ __device__ __forceinline__ void split_h2(float x0, float x1, uint32_t& hi, uint3
 // Per-warp shared memory of the tensor-core kernel: two stages of raw int8
 // K and V rows (32 tokens, row pitch D + 16: the 32-bit key-fragment reads of
 // 8 rows land on 8 different bank groups), then the block's values as fp16
-// (row pitch 2D + 16: conflict-free ldmatrix).
+// (row pitch 2D + 16: conflict-free ldmatrix), then the P'^T tiles.
 template <int D>
 struct TcAttnLayout {
   static constexpr int RP = D + 16;                 // raw row pitch
   static constexpr int RAW = 32 * RP;               // one K or V block
   static constexpr int STAGE = 2 * RAW;             // K then V
   static constexpr int PITCH = 2 * D + 16;          // fp16 value rows
-  static constexpr int WARP = 2 * STAGE + 32 * PITCH;
+  static constexpr int PT = 32 * 16;                // P'^T high (then low): [32 tokens][8 heads] fp16
+  static constexpr int WARP = 2 * STAGE + 32 * PITCH + 2 * PT;
   static constexpr int SMEM = 4 * WARP;             // kAttnWarps = 4
 };
 
@@ -286,8 +293,8 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool v
 template <int D>
 __global__ void __launch_bounds__(32 * kAttnWarps, 2) kv_attn_tc_kernel(const AttnArgs a) {
   using Ly = TcAttnLayout<D>;
-  constexpr int KS = D / 16;            // k-steps of S
-  constexpr int DT = D / 8;             // d tiles of O
+  constexpr int KS = D / 16;            // k-steps of S^T (over head_dim)
+  constexpr int DM = D / 16;            // 16-row d tiles of O^T
   constexpr int CH = D / 16;            // 16-byte chunks per row
   constexpr float kPScale = 1024.f;
   extern __shared__ __align__(16) uint8_t smem[];
@@ -296,25 +303,18 @@ __global__ void __launch_bounds__(32 * kAttnWarps, 2) kv_attn_tc_kernel(const At
   const int b = bk / a.Hkv, kvh = bk % a.Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int G = a.G;
-  // Q fragments (rows g and g + 8 of the group, pre-scaled by 1/sqrt(D)), permuted as above
-  uint32_t qh[KS][4], ql[KS][4];
+  // B fragments of Q^T (column = head g, pre-scaled by 1/sqrt(D)), permuted as above
+  uint32_t qh[KS][2], ql[KS][2];
 #pragma unroll
   for (int ks = 0; ks < KS; ++ks) {
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (g < G) {
+      const size_t qo = ((size_t)b * a.H + kvh * G + g) * D + 16 * ks + 4 * t;
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {          // r = 0: row g, r = 1: row g + 8
-      const int row = g + 8 * r;
-      float v[4] = {0.f, 0.f, 0.f, 0.f};
-      if (row < G) {
-        const size_t qo = ((size_t)b * a.H + kvh * G + row) * D + 16 * ks + 4 * t;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) v[e] = ld_q(a.q, qo + e, a.q_dtype) * a.inv_sqrt_d;
-      }
-      uint32_t h0, l0, h1, l1;
-      split_h2(v[0], v[1], h0, l0);
-      split_h2(v[2], v[3], h1, l1);
-      qh[ks][r] = h0; ql[ks][r] = l0;          // a0 / a1: logical k 2t, 2t+1
-      qh[ks][2 + r] = h1; ql[ks][2 + r] = l1;  // a2 / a3: logical k 2t+8, 2t+9
+      for (int e = 0; e < 4; ++e) v[e] = ld_q(a.q, qo + e, a.q_dtype) * a.inv_sqrt_d;
     }
+    split_h2(v[0], v[1], qh[ks][0], ql[ks][0]);   // b0: logical k 2t, 2t+1
+    split_h2(v[2], v[3], qh[ks][1], ql[ks][1]);   // b1: logical k 2t+8, 2t+9
   }
   const int t0 = split * a.tsplit, t1 = min(a.T, t0 + a.tsplit);
   const int8_t* kb = a.kc + (size_t)bk * a.T * D;
@@ -323,6 +323,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps, 2) kv_attn_tc_kernel(const At
   const float* vsb = a.vs + (size_t)bk * a.T;
   const uint32_t wbase = smem_u32(smem + warp * Ly::WARP);
   const uint32_t vtile = wbase + 2 * Ly::STAGE;
+  const uint32_t ptile = vtile + 32 * Ly::PITCH;   // P'^T high, then low at + PT
 
   // this warp's blocks: base = t0 + 32 * (warp + kAttnWarps * i)
   auto issue = [&](int i) {
@@ -341,10 +342,11 @@ __global__ void __launch_bounds__(32 * kAttnWarps, 2) kv_attn_tc_kernel(const At
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
 
+  // softmax state of heads 2t and 2t + 1
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-  float o[DT][4];
+  float o[DM][4];   // O^T: d tile md rows 16 md + g (+8), heads 2t, 2t + 1
 #pragma unroll
-  for (int i = 0; i < DT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  for (int i = 0; i < DM; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
   issue(0);
   issue(1);
@@ -371,110 +373,118 @@ __global__ void __launch_bounds__(32 * kAttnWarps, 2) kv_attn_tc_kernel(const At
       asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sa), "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3]) : "memory");
       asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sa + 16), "r"(h[4]), "r"(h[5]), "r"(h[6]), "r"(h[7]) : "memory");
     }
-    // S = Q K^T for 4 tiles of 8 tokens
-    float s[4][4];
+    // S^T = K Q^T for two tiles of 16 tokens: s[mt] = rows (tokens) 16 mt + g
+    // and + 8, columns (heads) 2t, 2t + 1
+    float s[2][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-      const uint32_t kr = st + (8 * j + g) * Ly::RP + 4 * t;
+    for (int mt = 0; mt < 2; ++mt) {
+      s[mt][0] = s[mt][1] = s[mt][2] = s[mt][3] = 0.f;
+      const uint32_t kr = st + (16 * mt + g) * Ly::RP + 4 * t;
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
-        uint32_t w;
-        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w) : "r"(kr + 16 * ks));
-        uint32_t b0, b1;
-        i8x4_to_h2x2(w, b0, b1);
-        mma16816(s[j], qh[ks], b0, b1);
-        mma16816(s[j], ql[ks], b0, b1);
+        uint32_t w0, w1;
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w0) : "r"(kr + 16 * ks));
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w1) : "r"(kr + 8 * Ly::RP + 16 * ks));
+        uint32_t af[4];
+        i8x4_to_h2x2(w0, af[0], af[2]);   // row g: logical k 2t, 2t+1 | 2t+8, 2t+9
+        i8x4_to_h2x2(w1, af[1], af[3]);   // row g + 8
+        mma16816(s[mt], af, qh[ks][0], qh[ks][1]);
+        mma16816(s[mt], af, ql[ks][0], ql[ks][1]);
       }
     }
-    // per-token key scale, mask past t1, online softmax on rows g and g + 8
+    // per-token key scale, mask past t1, online softmax per head (column)
     float rmax[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int tok = base + 8 * j + 2 * t + e;
+      for (int r = 0; r < 2; ++r) {
+        const int tok = base + 16 * mt + g + 8 * r;
         const float sk = tok < t1 ? ksb[tok] : 0.f;
-        s[j][e] = tok < t1 ? s[j][e] * sk : -INFINITY;
-        s[j][2 + e] = tok < t1 ? s[j][2 + e] * sk : -INFINITY;
-        rmax[0] = fmaxf(rmax[0], s[j][e]);
-        rmax[1] = fmaxf(rmax[1], s[j][2 + e]);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          s[mt][2 * r + e] = tok < t1 ? s[mt][2 * r + e] * sk : -INFINITY;
+          rmax[e] = fmaxf(rmax[e], s[mt][2 * r + e]);
+        }
       }
     float corr[2];
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      rmax[r] = fmaxf(rmax[r], __shfl_xor_sync(0xffffffffu, rmax[r], 1));
-      rmax[r] = fmaxf(rmax[r], __shfl_xor_sync(0xffffffffu, rmax[r], 2));
-      const float mn = fmaxf(m[r], rmax[r]);
-      corr[r] = expf(m[r] - mn);
-      m[r] = mn;
+    for (int e = 0; e < 2; ++e) {
+      rmax[e] = fmaxf(rmax[e], __shfl_xor_sync(0xffffffffu, rmax[e], 4));
+      rmax[e] = fmaxf(rmax[e], __shfl_xor_sync(0xffffffffu, rmax[e], 8));
+      rmax[e] = fmaxf(rmax[e], __shfl_xor_sync(0xffffffffu, rmax[e], 16));
+      const float mn = fmaxf(m[e], rmax[e]);
+      corr[e] = expf(m[e] - mn);
+      m[e] = mn;
     }
     float rsum[2] = {0.f, 0.f};
-    uint32_t ph[2][4], pl[2][4];     // A fragments of P' for the two 16-token k-steps
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float pv[4];
+    for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int tok = base + 8 * j + 2 * t + e;
+      for (int r = 0; r < 2; ++r) {
+        const int tl = 16 * mt + g + 8 * r, tok = base + tl;
         const float sv = tok < t1 ? vsb[tok] * kPScale : 0.f;
-        const float p0 = expf(s[j][e] - m[0]), p1 = expf(s[j][2 + e] - m[1]);
+        const float p0 = expf(s[mt][2 * r] - m[0]), p1 = expf(s[mt][2 * r + 1] - m[1]);
         rsum[0] += p0;
         rsum[1] += p1;
-        pv[e] = p0 * sv;
-        pv[2 + e] = p1 * sv;
+        uint32_t hi, lo;
+        split_h2(p0 * sv, p1 * sv, hi, lo);
+        asm volatile("st.shared.u32 [%0], %1;" ::"r"(ptile + tl * 16 + 4 * t), "r"(hi) : "memory");
+        asm volatile("st.shared.u32 [%0], %1;" ::"r"(ptile + Ly::PT + tl * 16 + 4 * t), "r"(lo) : "memory");
       }
-      const int kk = j >> 1, hf = j & 1;     // tile j is k 0-7 (hf 0) or 8-15 (hf 1) of k-step kk
-      split_h2(pv[0], pv[1], ph[kk][2 * hf], pl[kk][2 * hf]);          // row g
-      split_h2(pv[2], pv[3], ph[kk][2 * hf + 1], pl[kk][2 * hf + 1]);  // row g + 8
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      rsum[e] += __shfl_xor_sync(0xffffffffu, rsum[e], 4);
+      rsum[e] += __shfl_xor_sync(0xffffffffu, rsum[e], 8);
+      rsum[e] += __shfl_xor_sync(0xffffffffu, rsum[e], 16);
+      l[e] = l[e] * corr[e] + rsum[e];
     }
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      rsum[r] += __shfl_xor_sync(0xffffffffu, rsum[r], 1);
-      rsum[r] += __shfl_xor_sync(0xffffffffu, rsum[r], 2);
-      l[r] = l[r] * corr[r] + rsum[r];
-    }
-#pragma unroll
-    for (int q = 0; q < DT; ++q) {
-      o[q][0] *= corr[0]; o[q][1] *= corr[0];
-      o[q][2] *= corr[1]; o[q][3] *= corr[1];
+    for (int q = 0; q < DM; ++q) {
+      o[q][0] *= corr[0]; o[q][1] *= corr[1];
+      o[q][2] *= corr[0]; o[q][3] *= corr[1];
     }
     __syncwarp();
-    // O += P' V: B fragments of two d tiles per ldmatrix.x4.trans
+    // O^T += V^T P'^T: per 16-token k-step, B = P'^T (high and low) by one
+    // ldmatrix.x4.trans, A = V^T of each 16-row d tile by another
+    const int mi = lane >> 3, rr = lane & 7;
 #pragma unroll
     for (int kk = 0; kk < 2; ++kk) {
-#pragma unroll
-      for (int dn = 0; dn < DT; dn += 2) {
-        const int mi = lane >> 3, rr = lane & 7;
-        const uint32_t addr = vtile + (16 * kk + (mi & 1) * 8 + rr) * Ly::PITCH + (8 * (dn + (mi >> 1))) * 2;
-        uint32_t v0, v1, v2, v3;
+      uint32_t ph0, ph1, pl0, pl1;
+      {
+        const uint32_t addr = ptile + (uint32_t)(mi >> 1) * Ly::PT + (16 * kk + (mi & 1) * 8 + rr) * 16;
         asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                     : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3)
+                     : "=r"(ph0), "=r"(ph1), "=r"(pl0), "=r"(pl1)
                      : "r"(addr));
-        mma16816(o[dn], ph[kk], v0, v1);
-        mma16816(o[dn], pl[kk], v0, v1);
-        mma16816(o[dn + 1], ph[kk], v2, v3);
-        mma16816(o[dn + 1], pl[kk], v2, v3);
+      }
+#pragma unroll
+      for (int md = 0; md < DM; ++md) {
+        const uint32_t addr = vtile + (16 * kk + (mi >> 1) * 8 + rr) * Ly::PITCH + (16 * md + (mi & 1) * 8) * 2;
+        uint32_t av[4];
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(av[0]), "=r"(av[1]), "=r"(av[2]), "=r"(av[3])
+                     : "r"(addr));
+        mma16816(o[md], av, ph0, ph1);
+        mma16816(o[md], av, pl0, pl1);
       }
     }
-    __syncwarp();          // stage i & 1 and the fp16 tile are free again
+    __syncwarp();          // stage i & 1, the fp16 tile and the P' tiles are free again
     issue(i + 2);
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   // merge the warps of this CTA (rows < G), write the split's partial
   __syncthreads();   // every warp is done with its shared memory
   auto wacc = reinterpret_cast<float (*)[16][D]>(smem);
-  if (t == 0) {
-    wm[warp][g] = m[0]; wl[warp][g] = l[0];
-    wm[warp][g + 8] = m[1]; wl[warp][g + 8] = l[1];
+  if (g == 0) {
+    wm[warp][2 * t] = m[0]; wl[warp][2 * t] = l[0];
+    wm[warp][2 * t + 1] = m[1]; wl[warp][2 * t + 1] = l[1];
   }
 #pragma unroll
-  for (int q = 0; q < DT; ++q) {
-    const int d = 8 * q + 2 * t;
-    wacc[warp][g][d] = o[q][0] / kPScale;
-    wacc[warp][g][d + 1] = o[q][1] / kPScale;
-    wacc[warp][g + 8][d] = o[q][2] / kPScale;
-    wacc[warp][g + 8][d + 1] = o[q][3] / kPScale;
+  for (int q = 0; q < DM; ++q) {
+    const int d = 16 * q + g;
+    wacc[warp][2 * t][d] = o[q][0] / kPScale;
+    wacc[warp][2 * t + 1][d] = o[q][1] / kPScale;
+    wacc[warp][2 * t][d + 8] = o[q][2] / kPScale;
+    wacc[warp][2 * t + 1][d + 8] = o[q][3] / kPScale;
   }
   __syncthreads();
   const size_t nbh = (size_t)a.B * a.H;
@@ -575,7 +585,7 @@ int sf_kv_attention_decode(const void* q, int q_dtype, const int8_t* k_codes, co
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid((unsigned)n_split, (unsigned)(B * Hkv));
   cudaError_t e;
-  if (D <= 128 && G <= 16) {
+  if (D <= 128 && G <= 8) {
     e = D == 64 ? launch_tc_d<64>(a, grid, st) : launch_tc_d<128>(a, grid, st);
   } else {
     e = D == 64 ? launch_split_d<64>(a, grid, st)
