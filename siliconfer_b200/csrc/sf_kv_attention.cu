@@ -244,7 +244,10 @@ __global__ void __launch_bounds__(256) kv_attn_merge_kernel(const AttnArgs a) {
 //    operand (also ldmatrix.trans).  The accumulators hold O^T[d][head] with
 //    the same heads 2t, 2t+1 per lane as the softmax state.
 // Per 32 tokens and head_dim 128 this is 32 + 32 MMAs (the untransposed form,
-// with at most 8 of 16 rows in use, needs 64 + 64).
+// with at most 8 of 16 rows in use, needs 64 + 64).  With PR (groups of at
+// most 4 heads) a head's high and low parts take two adjacent columns (2h, 2h+1)
+// of one MMA instead of two MMAs, and each lane's column pair (2t, 2t+1) is then
+// one head, t: 16 + 16 MMAs.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -290,7 +293,7 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool v
                : "memory");
 }
 
-template <int D>
+template <int D, bool PR>
 __global__ void __launch_bounds__(32 * kAttnWarps, 2) kv_attn_tc_kernel(const AttnArgs a) {
   using Ly = TcAttnLayout<D>;
   constexpr int KS = D / 16;            // k-steps of S^T (over head_dim)
@@ -304,17 +307,23 @@ __global__ void __launch_bounds__(32 * kAttnWarps, 2) kv_attn_tc_kernel(const At
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int G = a.G;
   // B fragments of Q^T (column = head g, pre-scaled by 1/sqrt(D)), permuted as above
+  // (PR: column g is the high (g even) or low part of head g / 2)
   uint32_t qh[KS][2], ql[KS][2];
+  const int qhead = PR ? (g >> 1) : g;
 #pragma unroll
   for (int ks = 0; ks < KS; ++ks) {
     float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (g < G) {
-      const size_t qo = ((size_t)b * a.H + kvh * G + g) * D + 16 * ks + 4 * t;
+    if (qhead < G) {
+      const size_t qo = ((size_t)b * a.H + kvh * G + qhead) * D + 16 * ks + 4 * t;
 #pragma unroll
       for (int e = 0; e < 4; ++e) v[e] = ld_q(a.q, qo + e, a.q_dtype) * a.inv_sqrt_d;
     }
     split_h2(v[0], v[1], qh[ks][0], ql[ks][0]);   // b0: logical k 2t, 2t+1
     split_h2(v[2], v[3], qh[ks][1], ql[ks][1]);   // b1: logical k 2t+8, 2t+9
+    if (PR && (g & 1)) {
+      qh[ks][0] = ql[ks][0];
+      qh[ks][1] = ql[ks][1];
+    }
   }
   const int t0 = split * a.tsplit, t1 = min(a.T, t0 + a.tsplit);
   const int8_t* kb = a.kc + (size_t)bk * a.T * D;
@@ -389,8 +398,15 @@ __global__ void __launch_bounds__(32 * kAttnWarps, 2) kv_attn_tc_kernel(const At
         i8x4_to_h2x2(w0, af[0], af[2]);   // row g: logical k 2t, 2t+1 | 2t+8, 2t+9
         i8x4_to_h2x2(w1, af[1], af[3]);   // row g + 8
         mma16816(s[mt], af, qh[ks][0], qh[ks][1]);
-        mma16816(s[mt], af, ql[ks][0], ql[ks][1]);
+        if (!PR) mma16816(s[mt], af, ql[ks][0], ql[ks][1]);
       }
+    }
+    if constexpr (PR) {
+      // head t's score = its high column + its low column (kept in both)
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) s[mt][2 * r] = s[mt][2 * r + 1] = s[mt][2 * r] + s[mt][2 * r + 1];
     }
     // per-token key scale, mask past t1, online softmax per head (column)
     float rmax[2] = {-INFINITY, -INFINITY};
@@ -428,8 +444,14 @@ __global__ void __launch_bounds__(32 * kAttnWarps, 2) kv_attn_tc_kernel(const At
         rsum[1] += p1;
         uint32_t hi, lo;
         split_h2(p0 * sv, p1 * sv, hi, lo);
-        asm volatile("st.shared.u32 [%0], %1;" ::"r"(ptile + tl * 16 + 4 * t), "r"(hi) : "memory");
-        asm volatile("st.shared.u32 [%0], %1;" ::"r"(ptile + Ly::PT + tl * 16 + 4 * t), "r"(lo) : "memory");
+        if constexpr (PR) {
+          // columns 2t, 2t+1 = high and low part of head t's p' (p0 == p1 here)
+          hi = (hi & 0xFFFFu) | (lo << 16);
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(ptile + tl * 16 + 4 * t), "r"(hi) : "memory");
+        } else {
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(ptile + tl * 16 + 4 * t), "r"(hi) : "memory");
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(ptile + Ly::PT + tl * 16 + 4 * t), "r"(lo) : "memory");
+        }
       }
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -464,7 +486,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps, 2) kv_attn_tc_kernel(const At
                      : "=r"(av[0]), "=r"(av[1]), "=r"(av[2]), "=r"(av[3])
                      : "r"(addr));
         mma16816(o[md], av, ph0, ph1);
-        mma16816(o[md], av, pl0, pl1);
+        if (!PR) mma16816(o[md], av, pl0, pl1);
       }
     }
     __syncwarp();          // stage i & 1, the fp16 tile and the P' tiles are free again
@@ -474,17 +496,28 @@ __global__ void __launch_bounds__(32 * kAttnWarps, 2) kv_attn_tc_kernel(const At
   // merge the warps of this CTA (rows < G), write the split's partial
   __syncthreads();   // every warp is done with its shared memory
   auto wacc = reinterpret_cast<float (*)[16][D]>(smem);
-  if (g == 0) {
-    wm[warp][2 * t] = m[0]; wl[warp][2 * t] = l[0];
-    wm[warp][2 * t + 1] = m[1]; wl[warp][2 * t + 1] = l[1];
-  }
+  if constexpr (PR) {
+    // head t: its high and low columns summed
+    if (g == 0) { wm[warp][t] = m[0]; wl[warp][t] = l[0]; }
 #pragma unroll
-  for (int q = 0; q < DM; ++q) {
-    const int d = 16 * q + g;
-    wacc[warp][2 * t][d] = o[q][0] / kPScale;
-    wacc[warp][2 * t + 1][d] = o[q][1] / kPScale;
-    wacc[warp][2 * t][d + 8] = o[q][2] / kPScale;
-    wacc[warp][2 * t + 1][d + 8] = o[q][3] / kPScale;
+    for (int q = 0; q < DM; ++q) {
+      const int d = 16 * q + g;
+      wacc[warp][t][d] = (o[q][0] + o[q][1]) / kPScale;
+      wacc[warp][t][d + 8] = (o[q][2] + o[q][3]) / kPScale;
+    }
+  } else {
+    if (g == 0) {
+      wm[warp][2 * t] = m[0]; wl[warp][2 * t] = l[0];
+      wm[warp][2 * t + 1] = m[1]; wl[warp][2 * t + 1] = l[1];
+    }
+#pragma unroll
+    for (int q = 0; q < DM; ++q) {
+      const int d = 16 * q + g;
+      wacc[warp][2 * t][d] = o[q][0] / kPScale;
+      wacc[warp][2 * t + 1][d] = o[q][1] / kPScale;
+      wacc[warp][2 * t][d + 8] = o[q][2] / kPScale;
+      wacc[warp][2 * t + 1][d + 8] = o[q][3] / kPScale;
+    }
   }
   __syncthreads();
   const size_t nbh = (size_t)a.B * a.H;
@@ -507,14 +540,19 @@ __global__ void __launch_bounds__(32 * kAttnWarps, 2) kv_attn_tc_kernel(const At
   }
 }
 
-template <int D>
-cudaError_t launch_tc_d(const AttnArgs& a, dim3 grid, cudaStream_t st) {
+template <int D, bool PR>
+cudaError_t launch_tc_dp(const AttnArgs& a, dim3 grid, cudaStream_t st) {
   using Ly = TcAttnLayout<D>;
   static_assert(Ly::SMEM >= kAttnWarps * 16 * D * 4, "merge buffer must fit");
-  cudaError_t e = cudaFuncSetAttribute(kv_attn_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM);
+  cudaError_t e =
+      cudaFuncSetAttribute(kv_attn_tc_kernel<D, PR>, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM);
   if (e != cudaSuccess) return e;
-  kv_attn_tc_kernel<D><<<grid, 32 * kAttnWarps, Ly::SMEM, st>>>(a);
+  kv_attn_tc_kernel<D, PR><<<grid, 32 * kAttnWarps, Ly::SMEM, st>>>(a);
   return cudaGetLastError();
+}
+template <int D>
+cudaError_t launch_tc_d(const AttnArgs& a, dim3 grid, cudaStream_t st) {
+  return a.G <= 4 ? launch_tc_dp<D, true>(a, grid, st) : launch_tc_dp<D, false>(a, grid, st);
 }
 
 template <int D>
